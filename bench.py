@@ -1,0 +1,353 @@
+"""Benchmark of the weight-quantised matmul hot path on B200 (the driver's bench contract).
+
+Headline workload: Q4_0 (G=32) decode GEMV over every matmul of one
+Llama-3.2-1B layer (qkv 3072x2048, o 2048x2048, gate|up 16384x2048, down 2048x8192) plus the
+128256x2048 lm_head, batch 1, fp32 activations. A step is one pass of the five GEMVs.
+N GPUs shard every matrix column-parallel along its output rows (no communication), so the
+total work is fixed as N grows ("scaling": "strong"). value = algorithmic bytes of the whole job
+(packed weights + fp16 scales + fp32 x and y) / max-over-ranks time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mq|reference]
+  torchrun --nproc-per-node N bench.py --gpus N ...
+
+--impl reference times the reference's CPU path for the same workload on this host's cores: its
+dequantiser (Weights.int4 of qwen3moe/reference.py:53-65, restated in oracle/q4.py) followed by
+a torch fp32 matmul (qwen3moe/reference.py:135), on a bounded sample of the rows per step.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "mojo-adreno_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+METRIC = "Q4_0 GEMV HBM GB/s (Llama-3.2-1B layer + lm_head decode, batch 1)"
+GROUP = 32
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured (MEASURED_PEAKS.json)"
+    return 6650.0, 1590.0, "fallback (no MEASURED_PEAKS.json)"
+
+
+def q4_bytes(n, k, batch):
+    """Algorithmic bytes of one int4 GEMV: packed weights, fp16 scales, fp32 x and y."""
+    return n * k // 2 + n * (k // GROUP) * 2 + batch * k * 4 + batch * n * 4
+
+
+class Clocks:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=10)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [v.strip() for v in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def shard(n, world, rank):
+    lo = n * rank // world
+    hi = n * (rank + 1) // world
+    return lo, hi
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
+def run_mq(args):
+    import mq
+    from mq import synth
+
+    world, rank, local = init_dist()
+    dev = torch.device("cuda", local)
+    batch = 1
+    layer = synth.llama_layer(batch=batch, seed=0)
+    mats = []
+    shard_bytes = 0
+    for name, n, k in synth.LLAMA_LAYER:
+        x, wq, ws = layer[name]
+        lo, hi = shard(n, world, rank)
+        mats.append(dict(name=name, n=hi - lo, k=k, x=torch.from_numpy(x).to(dev),
+                         wq=torch.from_numpy(wq[lo:hi].view(np.int32)).to(dev), ws=torch.from_numpy(ws[lo:hi]).to(dev),
+                         y=torch.empty(batch, hi - lo, device=dev)))
+        shard_bytes += (hi - lo) * k // 2 + (hi - lo) * (k // GROUP) * 2
+    # Rotate weight copies so each step streams from HBM: copies x shard >= 2 x L2.
+    copies = max(1, -(-2 * L2_BYTES // shard_bytes))
+    for m in mats:
+        m["wqs"] = [m["wq"]] + [m["wq"].clone() for _ in range(copies - 1)]
+        m["wss"] = [m["ws"]] + [m["ws"].clone() for _ in range(copies - 1)]
+    job_bytes = sum(q4_bytes(n, k, batch) for _, n, k in synth.LLAMA_LAYER)
+
+    stream = torch.cuda.current_stream()
+
+    def step(i, events=None):
+        for j, m in enumerate(mats):
+            if events is not None:
+                events[j][0].record(stream)
+            mq.gemv_q4(m["wqs"][i % copies], m["wss"][i % copies], m["x"], m["y"], m["k"], group=GROUP)
+            if events is not None:
+                events[j][1].record(stream)
+
+    for i in range(args.warmup):
+        step(i)
+    barrier(world)
+
+    # ---- device-resident timed region ------------------------------------------------------
+    per_launch = [[] for _ in mats]
+    with Clocks(local) as clk:
+        evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in mats]
+               for _ in range(args.steps)]
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        start.record(stream)
+        for i in range(args.steps):
+            step(i, evs[i])
+        stop.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    for i in range(args.steps):
+        for j in range(len(mats)):
+            per_launch[j].append(evs[i][j][0].elapsed_time(evs[i][j][1]))
+    ms = max_over_ranks(ms, world)
+    ms_step = ms / args.steps
+    value = job_bytes / (ms_step * 1e-3) / 1e9
+
+    # ---- end to end through the public API: x from pinned host, logits back, every step ------
+    xs_host = [m["x"].cpu().pin_memory() for m in mats]
+    y_host = torch.empty(mats[-1]["y"].shape, dtype=torch.float32).pin_memory()
+    h2d = sum(x.numel() * x.element_size() for x in xs_host)
+    d2h = y_host.numel() * 4
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        for m, xh in zip(mats, xs_host):
+            m["x"].copy_(xh, non_blocking=True)
+        step(i)
+        y_host.copy_(mats[-1]["y"], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    e2e_value = job_bytes / (e2e_ms * 1e-3) / 1e9
+
+    # ---- roofline of the dominant kernel (the lm_head GEMV: 81% of the bytes) --------------
+    hbm, _, peak_src = peaks()
+    head = mats[-1]
+    head_ms = statistics.mean(per_launch[-1])
+    head_ms = max_over_ranks(head_ms, world)
+    head_bytes = q4_bytes(head["n"], head["k"], batch)
+    achieved = head_bytes / (head_ms * 1e-3) / 1e9
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "gemv_q4_lm_head_traffic.json")
+    if os.path.exists(tpath) and world == 1:
+        with open(tpath) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(budget_s=args.cpu_seconds)
+
+    clocks = clk.summary()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int4 weights (fp16 scales) x fp32 activations, fp32 accumulate",
+            "data": "synthetic (seeded; BASELINE configs[1] distributions)",
+            "config": {"workload": "llama-3.2-1b decode layer + lm_head, Q4_0 G=32 GEMV, batch 1",
+                       "matrices": {nm: [n, k] for nm, n, k in synth.LLAMA_LAYER}, "batch": batch,
+                       "parallelism": f"column-parallel (rows) x{world}, no communication",
+                       "l2": f"inputs larger than L2: {copies} rotating weight copies per rank"},
+            "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "note": "mq.gemv_q4 python API; x from pinned host and lm_head logits to host every step"},
+            "roofline": {"bound": "hbm", "kernel": "gemv_q4_kernel<32,1,true> (lm_head)", "achieved": round(achieved, 1),
+                         "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": traffic,
+                         "algorithmic_bytes_per_launch": head_bytes, "peak_source": peak_src},
+            "per_matrix_ms": {m["name"]: round(statistics.mean(t), 5) for m, t in zip(mats, per_launch)},
+            "gpu_launches": args.steps * len(mats),
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+class CpuSample:
+    """The reference's CPU path on a row sample of the workload: dequantise the int4 words as
+    Weights.int4 does (oracle/q4.py restates qwen3moe/reference.py:53-65, numpy), then a torch
+    fp32 matmul (qwen3moe/reference.py:135). The sample's inputs are drawn once."""
+
+    def __init__(self, rows):
+        from mq import synth
+
+        rng = np.random.default_rng(0)
+        self.x = torch.from_numpy(rng.standard_normal((1, 2048)).astype(np.float32))
+        self.wq, self.ws = synth.q4_matrix(rng, rows, 2048, GROUP)
+        self.bytes = q4_bytes(rows, 2048, 1)
+        self.rows = rows
+
+    def run(self):
+        """Returns the seconds one dequantise + matmul of the sample takes."""
+        from oracle import q4
+
+        t0 = time.perf_counter()
+        w = torch.from_numpy(q4.dequant(self.wq, self.ws, GROUP))
+        y = self.x @ w.T
+        dt = time.perf_counter() - t0
+        assert torch.isfinite(y).all()
+        return dt
+
+
+def cpu_baseline(budget_s=10.0):
+    torch.set_num_threads(os.cpu_count())
+    smp = CpuSample(8192)
+    dt = smp.run()  # warm-up and sizing
+    reps = min(50, max(3, int(budget_s / max(dt, 1e-3))))
+    med = statistics.median(smp.run() for _ in range(reps))
+    return {"value": round(smp.bytes / med / 1e9, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{smp.rows}x2048 Q4_0 rows (G=32) of the workload: numpy dequantise (single-threaded, as "
+                      f"the reference's) + torch fp32 matmul ({torch.get_num_threads()} threads), median of {reps}",
+            "cpu": platform_cpu()}
+
+
+def platform_cpu():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from mq import synth
+
+    torch.set_num_threads(os.cpu_count())
+    rows = 8192
+    job_bytes = sum(q4_bytes(n, k, 1) for _, n, k in synth.LLAMA_LAYER)
+    smp = CpuSample(rows)
+    for _ in range(args.warmup):
+        smp.run()
+    med = statistics.median(smp.run() for _ in range(args.steps))
+    value = smp.bytes / med / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(job_bytes / (value * 1e9) * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int4 weights dequantised to fp32, fp32 matmul", "data": "synthetic (seeded)",
+        "config": {"workload": "llama-3.2-1b decode layer + lm_head, Q4_0 G=32 GEMV, batch 1",
+                   "sample_per_step": f"{rows}x2048 rows; ms_per_step extrapolates to the whole job"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{rows}x2048 Q4_0 rows per step (reference dequantiser restated + torch fp32 matmul)",
+                         "cpu": platform_cpu()},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["mq", "reference"], default="mq")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_mq(args)
+
+
+if __name__ == "__main__":
+    main()

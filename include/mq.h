@@ -1,0 +1,100 @@
+/*
+ * mq.h - C ABI of the B200 (sm_100a) weight-quantised matmul library (libmq.so).
+ *
+ * Every entry point is stream-ordered and asynchronous: it validates its arguments on the host,
+ * enqueues its kernels on `stream` (a cudaStream_t, NULL = the legacy default stream) and returns.
+ * The caller allocates and owns every buffer (device pointers, as from cudaMalloc or
+ * torch.Tensor.data_ptr()); no entry point allocates device memory. Where an operator needs
+ * scratch memory the caller passes it, sized by the matching *_workspace_size() call.
+ *
+ * Return value: MQ_OK (0) or a negative MQ_E* code; the message of the most recent failure on the
+ * calling thread is returned by mq_last_error(). This mirrors the reference's status-code
+ * convention: an int status, 0 = success, plus a first-error string
+ * (driver/executor.h:13-26, driver/protocol.h:36-40).
+ *
+ * Storage formats (the reference's own bytes, read unchanged):
+ *   int4 "word layout": W[n][k] row-major as uint32 wq[n][k/8]; element 8w+j of a row sits in
+ *     bits 4j..4j+3 of word w as a 4-bit two's complement nibble (value = (nib ^ 8) - 8);
+ *     one fp16 scale per `group` consecutive weights of a row, ws[n][k/group]
+ *     (llama/kernels/gemv_q4.mojo:1-4,18-27; lfm2/convert.c:4-7; qwen3moe/export.py:152-176).
+ *   ternary transposed layout: codes c in {0,1,2} (value c - 1), 16 per uint32; the code of
+ *     (k, n) is (w[(k/16)*n_total + n] >> 2*(k%16)) & 3; one fp16 scale per 128 k of an output,
+ *     s[k/128][n] (qwen3/convert.cpp:39-74, bonsai/kernels/kernels.mojo:190-223).
+ */
+#ifndef MQ_H
+#define MQ_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MQ_API __attribute__((visibility("default")))
+#else
+#define MQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define MQ_OK 0
+#define MQ_EINVAL (-1)       /* bad shape, group, batch or null pointer */
+#define MQ_EALIGN (-2)       /* a pointer is not aligned as the operator needs */
+#define MQ_ECUDA (-3)        /* a CUDA call failed (launch error, no device, ...) */
+#define MQ_EUNSUPPORTED (-4) /* the device is not sm_100 or the size is above a stated maximum */
+#define MQ_ETIMEOUT (-5)     /* a kernel's bounded wait ran out (see mq_device_status) */
+
+/* Activation dtypes. */
+#define MQ_F32 0
+#define MQ_F16 1
+
+/* The message of the last failure on this thread ("" when none). */
+MQ_API const char *mq_last_error(void);
+
+/* Library ABI version (major * 100 + minor). */
+MQ_API int mq_version(void);
+
+/* Reads the device-side status word that kernels with bounded waits set when a wait runs out
+ * (0 = none, else the code of the first wait that gave up). Synchronises `stream`. When `reset`
+ * is nonzero the word is cleared afterwards. Returns the word (>= 0) or a negative MQ_E* code. */
+MQ_API int mq_device_status(int reset, void *stream);
+
+/*
+ * q[r][c] = ((nib ^ 8) - 8) as int8 and s_out = ws unchanged, for the int4 word layout: the
+ * bit-exact unpack hook. Replaces the nibble decode inside gemv_q4 (llama/kernels/gemv_q4.mojo:23-25)
+ * and the host dequantiser's integer step (qwen3moe/reference.py:53-65).
+ * wq: [n][k/8] u32, ws: [n][k/group] f16, q: [n][k] i8, s_out: [n][k/group] f16 (may be NULL).
+ */
+MQ_API int mq_unpack_q4(const uint32_t *wq, const uint16_t *ws, int8_t *q, uint16_t *s_out, int64_t n,
+                 int64_t k, int group, void *stream);
+
+/*
+ * Decode GEMV over int4 weights: y[b][r] (+)= sum_c W[r][c] * x[b][c] for b < batch.
+ * Replaces gemv_q4 / gemv_add_q4 (llama/kernels/gemv_q4.mojo:13-30,
+ * llama/kernels/gemv_add_q4.mojo:13-30; the G=32 Q4_0 variant lfm2/kernels/lk.mojo:56-72,134-143;
+ * the G=128 expert rows qwen3moe/kernels/moek.mojo:29-45) and the batched t_gemv_q4 / p_gemv_q4
+ * (qwen3moe/kernels/moek.mojo:273-281,528-545) with the argument order wq, ws, x, y, cols.
+ * x: [batch][k] fp32 (x_dtype MQ_F32) or fp16 (MQ_F16); y: [batch][n] fp32.
+ * group in {32, 64, 128}; k % 32 == 0 and k % group == 0; 1 <= batch <= 64 (batch > 4 runs the
+ * tensor-core GEMM); add != 0 adds into y (gemv_add_q4).
+ * wq, ws, x: 16-, 4- and 16-byte aligned.
+ */
+MQ_API int mq_gemv_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y,
+               int64_t n, int64_t k, int group, int batch, int add, void *stream);
+
+/*
+ * Ternary GEMV: y[b][i] = sum_k s[k/128][i] * (code(k, i) - 1) * x[b][k], b < batch <= 4.
+ * Replaces packed_linear + packed_reduce and the GEMV part of packed_head
+ * (bonsai/kernels/kernels.mojo:283-325,437-448,451-489) as called by qwen3/model.mojo:128-135,170-181.
+ * w: [k/16][n] u32, s: [k/128][n] f16, x: [batch][k] fp16 (the reference's fp16 pairs,
+ * qwen3/kernels/qwen3k.mojo:17-20, are the same bytes), y: [batch][n] fp32.
+ * k % 128 == 0; n % 4 == 0; w, s 16- and 8-byte aligned.
+ */
+MQ_API int mq_tgemv(const uint16_t *x, const uint32_t *w, const uint16_t *s, float *y, int64_t n, int64_t k,
+             int batch, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MQ_H */

@@ -1,0 +1,72 @@
+// Library-wide entry points (error string, version, device status word) and the host helpers
+// declared in common.cuh.
+#include "common.cuh"
+
+namespace mq {
+
+namespace {
+thread_local char t_error[512] = "";
+}
+
+int fail(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_error, sizeof t_error, fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char *what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(MQ_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  return MQ_OK;
+}
+
+int device_info(DeviceInfo *out) {
+  static DeviceInfo cache[64];
+  static bool valid[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(MQ_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(MQ_EUNSUPPORTED, "device index %d out of range", dev);
+  if (!valid[dev]) {
+    DeviceInfo d;
+    int v = 0;
+    if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
+      return fail(MQ_ECUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+    d.smem_optin = static_cast<size_t>(v);
+    if (d.major != 10) return fail(MQ_EUNSUPPORTED, "libmq is built for sm_100a; device is sm_%d%d", d.major, d.minor);
+    cache[dev] = d;
+    valid[dev] = true;
+  }
+  *out = cache[dev];
+  return MQ_OK;
+}
+
+}  // namespace mq
+
+extern "C" {
+
+const char *mq_last_error(void) { return mq::t_error; }
+
+int mq_version(void) { return 100; }
+
+int mq_device_status(int reset, void *stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int value = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&value, mq::g_status, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return mq::fail(MQ_ECUDA, "mq_device_status: %s", cudaGetErrorString(e));
+  if (reset && value) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(mq::g_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return mq::fail(MQ_ECUDA, "mq_device_status reset: %s", cudaGetErrorString(e));
+  }
+  return value;
+}
+
+}  // extern "C"

@@ -1,0 +1,55 @@
+"""Loads libmq.so (built in-tree next to this file) and declares its C ABI (include/mq.h)."""
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+library_path = os.path.join(_HERE, "libmq.so")
+
+c_int, c_i64, c_vp, c_char_p = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_char_p
+
+# name -> (restype, argtypes), in include/mq.h order.
+SIGNATURES = {
+    "mq_last_error": (c_char_p, []),
+    "mq_version": (c_int, []),
+    "mq_device_status": (c_int, [c_int, c_vp]),
+    "mq_unpack_q4": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_vp]),
+    "mq_gemv_q4": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_int, c_int, c_int, c_vp]),
+    "mq_tgemv": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_vp]),
+}
+
+
+class MQError(RuntimeError):
+    """A libmq entry point returned a non-zero status (the message is mq_last_error())."""
+
+    def __init__(self, code, message):
+        super().__init__(f"{message} (status {code})")
+        self.code = code
+
+
+class _Lib:
+    def __init__(self):
+        self._dll = None
+
+    def load(self):
+        if self._dll is None:
+            if not os.path.exists(library_path):
+                raise MQError(-3, f"libmq.so is not built ({library_path}); run python mojo-adreno_b200/build.py")
+            dll = ctypes.CDLL(library_path)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(dll, name)
+                fn.restype, fn.argtypes = res, args
+            self._dll = dll
+        return self._dll
+
+    def __getattr__(self, name):
+        return getattr(self.load(), name)
+
+    def call(self, name, *args):
+        """Calls entry point `name`; raises MQError on a negative status."""
+        rc = getattr(self.load(), name)(*args)
+        if rc < 0:
+            raise MQError(rc, f"{name}: {self.load().mq_last_error().decode()}")
+        return rc
+
+
+lib = _Lib()

@@ -1,0 +1,101 @@
+"""Reference-named operators over libmq (torch tensors as device buffers).
+
+Each function keeps the argument order of the reference kernel it replaces (cited per function)
+and adds what the reference fixed at compile time (group size, batch). Shapes are taken from the
+buffers. Every operator is asynchronous on the current torch CUDA stream; failures raise MQError
+with the library's message, as the reference's helpers return a non-zero status.
+"""
+import ctypes
+
+import torch
+
+from ._lib import MQError, lib
+
+MQ_F32, MQ_F16 = 0, 1
+
+__all__ = ["MQ_F32", "MQ_F16", "MQError", "gemv_q4", "gemv_add_q4", "unpack_q4", "project", "device_status"]
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _need(t, name, dtypes, numel=None):
+    if not isinstance(t, torch.Tensor):
+        raise MQError(-1, f"{name}: expected a torch.Tensor")
+    if not t.is_cuda:
+        raise MQError(-1, f"{name}: must be a CUDA tensor (there is no CPU path)")
+    if t.dtype not in dtypes:
+        raise MQError(-1, f"{name}: dtype {t.dtype} not in {dtypes}")
+    if not t.is_contiguous():
+        raise MQError(-1, f"{name}: must be contiguous")
+    if numel is not None and t.numel() != numel:
+        raise MQError(-1, f"{name}: has {t.numel()} elements, expected {numel}")
+
+
+_WORDS = (torch.int32, torch.uint32)
+
+
+def gemv_q4(wq, ws, x, y, cols, group=64, add=False):
+    """y[b, r] (+)= sum_c W[r, c] x[b, c] for the int4 word-layout W.
+
+    Mirrors gemv_q4(wq, ws, x, y, cols) of llama/kernels/gemv_q4.mojo:13-30 (one row per
+    workgroup there; here the rows come from wq's size). wq: int32/uint32 [rows, cols/8];
+    ws: fp16 [rows, cols/group]; x: fp32 or fp16 [batch, cols]; y: fp32 [batch, rows].
+    group: 64 (llama), 32 (Q4_0 / GGUF, lfm2/kernels/lk.mojo:26), 128 (qwen3moe experts).
+    """
+    _need(wq, "wq", _WORDS)
+    rows = wq.numel() * 8 // cols
+    _need(ws, "ws", (torch.float16,), rows * cols // group)
+    _need(x, "x", (torch.float32, torch.float16))
+    batch = x.numel() // cols
+    if batch * cols != x.numel():
+        raise MQError(-1, f"x: {x.numel()} elements is not a whole number of rows of {cols}")
+    _need(y, "y", (torch.float32,), batch * rows)
+    lib.call("mq_gemv_q4", _p(wq), _p(ws), _p(x), MQ_F16 if x.dtype == torch.float16 else MQ_F32, _p(y),
+             rows, cols, group, batch, int(bool(add)), _stream())
+    return y
+
+
+def gemv_add_q4(wq, ws, x, y, cols, group=64):
+    """y += W x: gemv_add_q4 of llama/kernels/gemv_add_q4.mojo:13-30 (the residual)."""
+    return gemv_q4(wq, ws, x, y, cols, group, add=True)
+
+
+def unpack_q4(wq, ws, cols, group, q=None, s=None):
+    """The bit-exact decode hook: int8 q [rows, cols] = ((nib ^ 8) - 8) and the scales unchanged
+    (the integer step of qwen3moe/reference.py:53-65)."""
+    _need(wq, "wq", _WORDS)
+    rows = wq.numel() * 8 // cols
+    _need(ws, "ws", (torch.float16,), rows * cols // group)
+    if q is None:
+        q = torch.empty(rows, cols, dtype=torch.int8, device=wq.device)
+    _need(q, "q", (torch.int8,), rows * cols)
+    if s is not None:
+        _need(s, "s", (torch.float16,), ws.numel())
+    lib.call("mq_unpack_q4", _p(wq), _p(ws), _p(q), _p(s) if s is not None else None, rows, cols, group, _stream())
+    return q, s
+
+
+def project(x, w, s, y, n, k):
+    """y = W x for the ternary transposed layout: the reference's project() =
+    packed_linear + packed_reduce (qwen3/model.mojo:128-135; bonsai/kernels/kernels.mojo:283-325,
+    437-448), argument order (input, words, scales, output, n, k). x: fp16 [batch, k] (or the
+    fp16-pair int32 [batch, k/2] buffer the reference passes); w: int32/uint32 [k/16, n];
+    s: fp16 [k/128, n]; y: fp32 [batch, n]."""
+    _need(x, "x", (torch.float16, torch.int32, torch.uint32))
+    batch = x.numel() * x.element_size() // 2 // k
+    _need(w, "w", _WORDS, k // 16 * n)
+    _need(s, "s", (torch.float16,), k // 128 * n)
+    _need(y, "y", (torch.float32,), batch * n)
+    lib.call("mq_tgemv", _p(x), _p(w), _p(s), _p(y), n, k, batch, _stream())
+    return y
+
+
+def device_status(reset=True):
+    """The device status word set by kernels whose bounded waits ran out (0 = none)."""
+    return lib.call("mq_device_status", int(bool(reset)), _stream())

@@ -1,0 +1,61 @@
+"""Ternary (2-bit) transposed layout: codes, GEMV (exact and fp16-chain emulation), packer.
+
+TEST INFRASTRUCTURE ONLY (see oracle/__init__.py).
+"""
+import numpy as np
+
+SHIFTS2 = np.arange(16, dtype=np.uint32) * 2
+
+
+def codes(w, n, k):
+    """codes [n, k] of the transposed layout: code(k, i) = (w[k/16, i] >> 2 (k % 16)) & 3
+    (bonsai/kernels/kernels.mojo:201-208, qwen3/convert.cpp:39-74). `w` is [k/16, n] uint32."""
+    w = np.asarray(w, np.uint32).reshape(k // 16, n)
+    c = (w[:, None, :] >> SHIFTS2[None, :, None]) & 3  # [k/16, 16, n]
+    return c.reshape(k, n).T.astype(np.int8)
+
+
+def tgemv(x16, w, s, n, k):
+    """Exact y[b, i] = sum_g s[g, i] sum_{k in g} (code - 1) x[b, k] (float64), the value
+    packed_linear + packed_reduce approximate (bonsai/kernels/kernels.mojo:283-325,437-448)."""
+    c = codes(w, n, k).astype(np.float64) - 1.0
+    sc = np.asarray(s, np.float16).astype(np.float64).reshape(k // 128, n)
+    x = np.atleast_2d(np.asarray(x16, np.float16)).astype(np.float64)
+    wd = (c.reshape(n, k // 128, 128) * sc.T[:, :, None]).reshape(n, k)
+    return x @ wd.T
+
+
+def tgemv_fp16_chains(x16, w, s, n, k):
+    """The reference's own arithmetic (batch 1): per 128-group, _group_dot's four fp16 FMA chains
+    per activation half (pair % 4), each step rounded to fp16, joined in fp32 as
+    ((d0lo + d0hi) + (d1lo + d1hi)) + ((d2lo + d2hi) + (d3lo + d3hi)), times the fp32 scale,
+    groups summed in fp32 (bonsai/kernels/kernels.mojo:190-223,227-280). Small sizes only."""
+    c = codes(w, n, k).astype(np.float32) - 1.0  # [n, k]
+    x = np.asarray(x16, np.float16).reshape(k).astype(np.float32)
+    sc = np.asarray(s, np.float16).astype(np.float32).reshape(k // 128, n)
+    y = np.zeros(n, np.float32)
+    for g in range(k // 128):
+        d = np.zeros((4, 2, n), np.float16)
+        for word in range(8):
+            for pair in range(8):
+                kk = g * 128 + word * 16 + 2 * pair
+                for h in range(2):
+                    prod = c[:, kk + h] * x[kk + h]
+                    d[pair % 4, h] = (d[pair % 4, h].astype(np.float32) + prod).astype(np.float16)
+        df = d.astype(np.float32)
+        tot = ((df[0, 0] + df[0, 1]) + (df[1, 0] + df[1, 1])) + ((df[2, 0] + df[2, 1]) + (df[3, 0] + df[3, 1]))
+        y = (y + tot * sc[g]).astype(np.float32)
+    return y
+
+
+def pack_transposed(w_rows, s_rows, b_rows=None):
+    """MLX 2-bit rows -> the kernels' transposed layout, as qwen3/convert.cpp:39-74 (addPacked):
+    codes [n, k/16] -> [k/16, n] words, scales [n, k/128] -> [k/128, n]; every group must be
+    ternary (bias == -scale) or ValueError."""
+    w_rows = np.asarray(w_rows, np.uint32)
+    s_rows = np.asarray(s_rows, np.float16)
+    if b_rows is not None:
+        b = np.asarray(b_rows, np.float16).astype(np.float32)
+        if np.any(b != -s_rows.astype(np.float32)):
+            raise ValueError("not ternary (bias != -scale)")
+    return np.ascontiguousarray(w_rows.T), np.ascontiguousarray(s_rows.T)

@@ -1,0 +1,80 @@
+"""The C ABI without a GPU: libmq.so loads, exports every entry point include/mq.h declares, and
+rejects bad arguments with a status and a message before touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import REPO
+
+HEADER = os.path.join(REPO, "include", "mq.h")
+
+
+def declared():
+    text = open(HEADER).read()
+    return re.findall(r"MQ_API\s+[\w\s\*]*?\b(mq_\w+)\s*\(", text)
+
+
+def test_header_and_signatures_agree():
+    from mq._lib import SIGNATURES
+
+    names = declared()
+    assert names, "no MQ_API declarations found"
+    assert sorted(names) == sorted(SIGNATURES), "mq/_lib.py SIGNATURES must list exactly include/mq.h's entry points"
+
+
+def test_library_exports_every_declared_symbol():
+    from mq._lib import lib, library_path
+
+    assert os.path.exists(library_path), "build libmq.so first (python mojo-adreno_b200/build.py)"
+    dll = ctypes.CDLL(library_path)
+    missing = [n for n in declared() if not hasattr(dll, n)]
+    assert not missing, f"not exported: {missing}"
+    assert lib.mq_version() >= 100
+
+
+def _status(name, *args):
+    from mq._lib import lib
+
+    rc = getattr(lib, name)(*args)
+    return rc, lib.mq_last_error().decode()
+
+
+def test_gemv_rejects_bad_arguments_before_launch():
+    P = ctypes.c_void_p
+    ok = P(1 << 20)  # never dereferenced: validation fails first
+    rc, msg = _status("mq_gemv_q4", None, ok, ok, 0, ok, 16, 256, 32, 1, 0, None)
+    assert rc == -1 and "null" in msg
+    rc, msg = _status("mq_gemv_q4", ok, ok, ok, 0, ok, 16, 256, 48, 1, 0, None)
+    assert rc == -1 and "group" in msg
+    rc, msg = _status("mq_gemv_q4", ok, ok, ok, 0, ok, 16, 200, 32, 1, 0, None)
+    assert rc == -1 and "multiple" in msg
+    rc, msg = _status("mq_gemv_q4", ok, ok, ok, 0, ok, 16, 256, 32, 0, 0, None)
+    assert rc == -1 and "batch" in msg
+    rc, msg = _status("mq_gemv_q4", P((1 << 20) + 4), ok, ok, 0, ok, 16, 256, 32, 1, 0, None)
+    assert rc == -2 and "aligned" in msg
+
+
+def test_tgemv_rejects_bad_arguments_before_launch():
+    P = ctypes.c_void_p
+    ok = P(1 << 20)
+    rc, msg = _status("mq_tgemv", ok, ok, ok, ok, 64, 200, 1, None)
+    assert rc == -1 and "128" in msg
+    rc, msg = _status("mq_tgemv", ok, ok, ok, ok, 66, 256, 1, None)
+    assert rc == -1 and "multiple of 4" in msg
+    rc, msg = _status("mq_tgemv", ok, ok, ok, ok, 64, 256, 5, None)
+    assert rc == -1 and "batch" in msg
+
+
+def test_python_ops_refuse_cpu_tensors():
+    import torch
+
+    import mq
+
+    wq = torch.zeros(16, 32, dtype=torch.int32)
+    ws = torch.zeros(16, 8, dtype=torch.float16)
+    x = torch.zeros(1, 256)
+    y = torch.zeros(1, 16)
+    with pytest.raises(mq.MQError, match="CUDA"):
+        mq.gemv_q4(wq, ws, x, y, 256, group=32)
