@@ -46,6 +46,40 @@ int device_info(DeviceInfo *out) {
   return MQ_OK;
 }
 
+namespace {
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+}  // namespace
+
+int encode_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem_bytes, uint64_t cols,
+                   uint64_t rows, uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows,
+                   CUtensorMapSwizzle swizzle, const char *what) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MQ_ECUDA, "%s: cuTensorMapEncodeTiled is not available from the driver", what);
+  if (reinterpret_cast<uintptr_t>(base) % 16 || row_stride_bytes % 16 || (box_cols * elem_bytes) % 16)
+    return fail(MQ_EALIGN, "%s: tensor map needs a 16-byte aligned base, row stride and box row", what);
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MQ_ECUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+  return MQ_OK;
+}
+
 }  // namespace mq
 
 extern "C" {

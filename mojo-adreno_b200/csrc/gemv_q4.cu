@@ -2,32 +2,38 @@
 //
 // Replaces gemv_q4 / gemv_add_q4 (llama/kernels/gemv_q4.mojo:13-30, gemv_add_q4.mojo:13-30), the
 // Q4_0 G=32 variant (lfm2/kernels/lk.mojo:56-72,134-143) and the small-batch t_gemv_q4 / p_gemv_q4
-// (qwen3moe/kernels/moek.mojo:273-281,528-545). Same arithmetic: y[r] = sum over words of
-// scale * sum_j ((nib_j ^ 8) - 8) * x[8w + j], fp32 x and y.
+// (qwen3moe/kernels/moek.mojo:273-281,528-545). Same arithmetic: y[r] = sum over groups of
+// scale * sum_j ((nib_j ^ 8) - 8) * x[k_j], fp32 x and y.
 //
 // B200 design (HBM-bound: 0.5625 B per weight at G=32):
-//  * Issue budget. At ~6.5 TB/s an SM must retire ~46 weights per clock; it issues 128 lane
-//    instructions per clock, so decode + multiply must cost well under 2.8 instructions per
-//    weight. An fp32 FMA path (extract, convert, subtract, FMA) costs ~4. Here the warp-level
-//    tensor op mma.m16n8k16 (fp16 in, fp32 accumulate) does the multiply-add, and the decode is
-//    two logic ops per pair of weights.
+//  * Streaming. Each of 16 warps streams its own 32-row x 256-k weight tiles (4 KB, one TMA box of
+//    32 rows x 128 bytes with the 128-byte swizzle) and their fp16 scales from HBM into a private
+//    2-slot shared-memory ring (cp.async.bulk.tensor), refilling a slot as soon as it is consumed:
+//    no hand-off between warps. Persistent CTAs, one per SM, 160 KB of ring per SM. (Sweeping
+//    warps x slots over 8x4, 12x3, 16x1, 16x2, 20x2 and 24x1 on B200 put 16x2 first.)
+//  * Issue budget. At ~6.5 TB/s an SM must retire ~46 weights per clock out of 128 issued lane
+//    instructions. The warp-level tensor op mma.m16n8k16 (fp16 in, fp32 accumulate) does the
+//    multiply-add; a warp covers 32 rows (two m16 tiles) so every activation-fragment, x-sum and
+//    address computation serves twice the weights, and the two tiles give four independent
+//    accumulator chains.
 //  * Decode. A nibble pair masked straight into the mantissa bits of an fp16x2 register is an
 //    exact fp16 subnormal: (u & 0x000F000F) holds u_lo * 2^-24 | u_hi * 2^-24 and
 //    (u & 0x00F000F0) holds 16u * 2^-24 (still below the 2^-14 normal threshold), where
-//    u = nib ^ 8 = value + 8 in 0..15 (offset binary). So per 32-bit word: one XOR, one shift and
-//    four ANDs give all eight weights, exactly. The factors 2^-24 (and 16) are undone on the
-//    activation side (x/16 in the matching B slots) and in the fp32 epilogue (scale * 2^24), and
-//    the offset is removed with the precomputed sum of x: sum (u - 8) x = sum u x - 8 sum x.
-//  * Exact per-group scales. Lanes of a quad (lane % 4 == q) load 16 consecutive bytes of a row
-//    (32 weights = 32 k of the same scale group for G=32). The B fragment puts quad q's slots of
-//    x in column q only, so D column q holds quad q's dot product alone: the fp32 epilogue applies
-//    each group's scale to its own partial sum, in fp32, as the reference does.
-//  * fp32 x fidelity. Columns 4..7 carry the fp16 residual x - fp16(x) (batch <= 2), so the
-//    product sees ~22 bits of x; the weights are exact integers; accumulation is fp32.
-//  * Memory. Each lane streams 128-bit, L1-no-allocate loads (rows g and g+8 of a 16-row tile,
-//    64 contiguous bytes per row per quad), 4 chunks of 128 k in flight. Small matrices split K
-//    across the 8 warps of a CTA (partials reduced in shared memory); CTAs are persistent over
-//    row blocks so x is staged once per CTA.
+//    u = nib ^ 8 = value + 8 in 0..15 (offset binary). Per 32-bit word one XOR, one shift and four
+//    ANDs give all eight weights exactly. The factors 2^-24 (and 16) are undone on the activation
+//    side (x/16 in the matching B slots) and in the fp32 epilogue, and the offset is removed with
+//    the precomputed sum of x: sum (u - 8) x = sum u x - 8 sum x.
+//  * Exact per-group scales. Lanes of a quad (lane % 4 == q) read 16 consecutive bytes of a row
+//    (32 weights = one scale group for G=32). The B fragment puts quad q's slots of x in column q
+//    only, so D column q holds quad q's dot product alone and the fp32 epilogue applies each
+//    group's scale to its own partial sum, as the reference does.
+//  * fp32 x fidelity. Columns 4..7 carry the fp16 residual x - fp16(x) (batch <= 2), so products
+//    see ~22 bits of x; the weights are exact integers; accumulation is fp32.
+//  * Bank conflicts. The 128-byte TMA swizzle XORs a row's 16-byte chunk index with row % 8; mma row
+//    g reads physical row (g >> 1) | (g & 1) << 2, which puts the 8 lanes of every shared-memory
+//    phase on 8 different chunks.
+//  * Small matrices split K across the warps of a CTA (partials reduced in shared memory), so even
+//    a 2048-row matrix keeps every SM streaming.
 #include <algorithm>
 
 #include "common.cuh"
@@ -35,78 +41,169 @@
 namespace mq {
 namespace gemv {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = 8;
-constexpr int kPrefetch = 4;  // 128-k chunks whose loads a warp issues together
+constexpr int kWarps = 16;  // 4 per scheduler
+constexpr int kThreads = 32 * kWarps;
+constexpr int kMaxSlots = 2;
+constexpr int kRows = 32;     // rows of a tile: two m16 tiles
+constexpr int kSlotK = 256;   // k of a slot: 32 words = one 128-byte swizzle row
+constexpr int kWordBytes = kRows * 128;
+constexpr int kScaleHalvesTma = 8;  // a TMA-loaded scale row: 8 halves (16 bytes), G = 32 only
 
-struct GemvQ4Params {
-  const uint32_t *wq;
-  const __half *ws;
+struct Params {
+  const __half *ws;  // scales in global memory (read directly when they are not TMA-loaded)
   const void *x;
   float *y;
   int n, k, batch, x_f16, add;
-  int ks;       // warps of a CTA that split K
-  int rt;       // 16-row tiles of a CTA (rt * ks == kWarps)
-  int nblocks;  // row blocks (rt tiles each)
+  int ks;       // warps that split a tile's K range (1 = no reduction between warps)
+  int rt;       // tiles per round (rt * ks == kWarps)
+  int tiles;    // ceil(n / 32)
+  int nrounds;  // ceil(tiles / rt)
+  int slots;    // ring slots per warp (<= kMaxSlots)
+  int scales_tma;
+  int slot_bytes;
 };
 
-// The eight weights of one word as four fp16x2 subnormal pairs (see the file comment).
-__device__ __forceinline__ void decode_q4(uint32_t w, uint32_t &p0, uint32_t &p1, uint32_t &p2, uint32_t &p3) {
+__device__ __forceinline__ void decode_q4(uint32_t w, uint32_t (&p)[4]) {
   const uint32_t u = w ^ 0x88888888u;
-  p0 = u & 0x000F000Fu;  // nibbles 0 | 4, factor 1
-  p1 = u & 0x00F000F0u;  // nibbles 1 | 5, factor 16
+  p[0] = u & 0x000F000Fu;  // nibbles 0 | 4, factor 1
+  p[1] = u & 0x00F000F0u;  // nibbles 1 | 5, factor 16
   const uint32_t v = u >> 8;
-  p2 = v & 0x000F000Fu;  // nibbles 2 | 6, factor 1
-  p3 = v & 0x00F000F0u;  // nibbles 3 | 7, factor 16
+  p[2] = v & 0x000F000Fu;  // nibbles 2 | 6, factor 1
+  p[3] = v & 0x00F000F0u;  // nibbles 3 | 7, factor 16
 }
 
-__device__ __forceinline__ float load_x(const void *x, int x_f16, size_t i) {
-  return x_f16 ? __half2float(static_cast<const __half *>(x)[i]) : static_cast<const float *>(x)[i];
+__device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+
+// Physical row (within 8) that mma row g reads: keeps the 8 lanes of a phase on distinct chunks.
+__device__ __forceinline__ int phys_row(int g) { return (g >> 1) | ((g & 1) << 2); }
+
+// Shared-memory layout (byte offsets from a 1024-aligned base).
+struct Layout {
+  uint32_t slots, bfrag, xsum, red, bars, total;
+};
+
+__host__ __device__ inline Layout layout(int k, int batch, int nt, int slots, int slot_bytes) {
+  Layout L;
+  const int kc = (k + 127) / 128;
+  L.slots = 0;
+  L.bfrag = kWarps * slots * slot_bytes;
+  L.xsum = L.bfrag + nt * kc * 8 * 8 * 8;
+  L.red = L.xsum + batch * kc * 4 * 4;
+  L.bars = (L.red + kWarps * kRows * batch * 4 + 7) / 8 * 8;
+  L.total = L.bars + kWarps * kMaxSlots * 8;
+  return L;
 }
 
-// NT: mma n-tiles per k step; LO: column 4+q carries the residual of column q (batch <= 2),
-// otherwise columns 4..7 carry a second token.
+// The work of one warp, as a sequence of (tile, slot of K) items: round j of this CTA covers
+// tile (blockIdx.x + j * gridDim.x) * rt + rtl, K slots kw * spw .. + per_round - 1.
+struct Items {
+  int rtl, kw, spw, per_round, rt, tiles, grid, cta;
+  __device__ bool get(uint32_t u, int &tile, int &sk) const {
+    if (per_round <= 0) return false;
+    const int j = static_cast<int>(u) / per_round, i = static_cast<int>(u) % per_round;
+    tile = (cta + j * grid) * rt + rtl;
+    sk = kw * spw + i;
+    return tile < tiles;
+  }
+};
+
 template <int G, int NT, bool LO>
-__global__ void __launch_bounds__(kThreads) gemv_q4_kernel(const GemvQ4Params p) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int K = p.k, N = p.n, B = p.batch;
-  const int kc = (K + 127) / 128;  // chunks of 128 k
-  const int nsteps = kc * 8;       // mma k16 steps
-  const int wpr = K / 8;           // words per row
-  const int spr = K / G;           // scales per row
-  uint2 *bfrag = reinterpret_cast<uint2 *>(smem);                 // [NT][nsteps][8]
-  float *xsum = reinterpret_cast<float *>(bfrag + NT * nsteps * 8);  // [B][kc*4]
-  float *red = xsum + B * kc * 4;                                 // [kWarps][16][B]
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_q4_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const Layout L = layout(p.k, p.batch, NT, p.slots, p.slot_bytes);
+  const int K = p.k, N = p.n, B = p.batch, S = p.slots;
+  const int kc = (K + 127) / 128;
+  const int nsteps = kc * 8;
+  const int nslotk = (K + kSlotK - 1) / kSlotK;
+  const int spw = (nslotk + p.ks - 1) / p.ks;  // K slots per warp per round
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars) + warp * kMaxSlots;
+  uint8_t *ring = smem + L.slots + warp * S * p.slot_bytes;
+  const uint32_t bytes = kWordBytes + (p.scales_tma ? kRows * kScaleHalvesTma * 2 : 0);
 
-  // ---- stage x: B fragments (fp16 hi/lo, permuted to the decode's slot order) and quad sums --
+  Items items;
+  items.rtl = warp / p.ks;
+  items.kw = warp % p.ks;
+  items.spw = spw;
+  items.per_round = min(spw, nslotk - items.kw * spw);
+  items.rt = p.rt;
+  items.tiles = p.tiles;
+  items.grid = gridDim.x;
+  items.cta = blockIdx.x;
+
+  // Each warp streams its own tiles: lane 0 issues the TMA loads for the next S items.
+  auto issue = [&](uint32_t u) {
+    int tile, sk;
+    if (lane != 0 || !items.get(u, tile, sk)) return;
+    const int slot = u % S;
+    uint64_t *bar = full + slot;
+    uint8_t *dst = ring + slot * p.slot_bytes;
+    mbar_expect_tx(bar, bytes);
+    tma_load_2d(dst, &wmap, bar, sk * (kSlotK / 8), tile * kRows);
+    if (p.scales_tma) tma_load_2d(dst + kWordBytes, &smap, bar, sk * kScaleHalvesTma, tile * kRows);
+  };
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(full + s, 1);
+    fence_mbar_init();
+    prefetch_tmap(&wmap);
+    if (p.scales_tma) prefetch_tmap(&smap);
+  }
+  __syncwarp();
+  for (int s = 0; s < S; ++s) issue(s);  // loads start before x is staged
+
+  uint2 *bfrag = reinterpret_cast<uint2 *>(smem + L.bfrag);  // [NT][nsteps][8]
+  float *xsum = reinterpret_cast<float *>(smem + L.xsum);     // [B][kc*4]
+  float *red = reinterpret_cast<float *>(smem + L.red);       // [kWarps][32][B]
+
+  // Stage x once per CTA: B fragments (fp16 hi/lo, in the decode's slot order) and quad sums.
   for (int i = threadIdx.x; i < NT * nsteps * 8; i += kThreads) bfrag[i] = make_uint2(0u, 0u);
   __syncthreads();
-  for (int it = threadIdx.x; it < B * kc * 16; it += kThreads) {
-    const int t = it / (kc * 16), wi = it % (kc * 16);
+  const int nitems = B * kc * 16;
+  for (int base = 0; base < nitems; base += kThreads) {
+    const int it = base + threadIdx.x;
+    const bool live = it < nitems;
+    const int t = live ? it / (kc * 16) : 0, wi = it % (kc * 16);
     const int c = wi / 16, q = (wi / 4) % 4, j = wi % 4;
     float xv[8];
+    if (live && 8 * wi + 8 <= K) {
+      if (p.x_f16) {
+        const uint4 v =
+            *reinterpret_cast<const uint4 *>(static_cast<const __half *>(p.x) + static_cast<size_t>(t) * K + 8 * wi);
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int kk = 8 * wi + e;
-      xv[e] = kk < K ? load_x(p.x, p.x_f16, static_cast<size_t>(t) * K + kk) : 0.f;
-      if (e == 1 || e == 3 || e == 5 || e == 7) xv[e] *= 0.0625f;  // slots whose weights carry 16
+        for (int e = 0; e < 4; ++e) {
+          xv[2 * e] = __low2float(h[e]);
+          xv[2 * e + 1] = __high2float(h[e]);
+        }
+      } else {
+        const float4 *src =
+            reinterpret_cast<const float4 *>(static_cast<const float *>(p.x) + static_cast<size_t>(t) * K + 8 * wi);
+        const float4 a = src[0], b = src[1];
+        xv[0] = a.x, xv[1] = a.y, xv[2] = a.z, xv[3] = a.w, xv[4] = b.x, xv[5] = b.y, xv[6] = b.z, xv[7] = b.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xv[e] = 0.f;
     }
+    float sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sum += xv[e];
+    // Quad sums: the 4 words of a quad are 4 consecutive items in lanes 4m..4m+3.
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if (!live) continue;
+    if (j == 0) xsum[t * kc * 4 + c * 4 + q] = sum;
     float hv[8], lv[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      hv[e] = __half2float(__float2half_rn(xv[e]));
-      lv[e] = xv[e] - hv[e];
+      const float xs = (e & 1) ? xv[e] * 0.0625f : xv[e];  // odd nibbles carry a factor 16
+      hv[e] = __half2float(__float2half_rn(xs));
+      lv[e] = xs - hv[e];
     }
-    const int s0 = c * 8 + 2 * j;
-    int tile, col;
-    if (LO) {
-      tile = t;
-      col = q;
-    } else {
-      tile = t / 2;
-      col = 4 * (t % 2) + q;
-    }
-    uint2 *dst = bfrag + (static_cast<size_t>(tile) * nsteps + s0) * 8;
+    const int tile = LO ? t : t / 2, col = LO ? q : 4 * (t % 2) + q;
+    uint2 *dst = bfrag + (static_cast<size_t>(tile) * nsteps + c * 8 + 2 * j) * 8;
     dst[col] = make_uint2(pack_half2(hv[0], hv[4]), pack_half2(hv[1], hv[5]));
     dst[8 + col] = make_uint2(pack_half2(hv[2], hv[6]), pack_half2(hv[3], hv[7]));
     if (LO) {
@@ -114,163 +211,228 @@ __global__ void __launch_bounds__(kThreads) gemv_q4_kernel(const GemvQ4Params p)
       dst[8 + 4 + col] = make_uint2(pack_half2(lv[2], lv[6]), pack_half2(lv[3], lv[7]));
     }
   }
-  for (int it = threadIdx.x; it < B * kc * 4; it += kThreads) {
-    const int t = it / (kc * 4), qi = it % (kc * 4);
-    float s = 0.f;
-    for (int e = 0; e < 32; ++e) {
-      const int kk = 32 * qi + e;
-      if (kk < K) s += load_x(p.x, p.x_f16, static_cast<size_t>(t) * K + kk);
-    }
-    xsum[t * kc * 4 + qi] = s;
-  }
   __syncthreads();
 
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int g = lane >> 2, q = lane & 3;
-  const int kw = warp % p.ks, rtl = warp / p.ks;
-  const int cpw = (kc + p.ks - 1) / p.ks;
-  const int cb = kw * cpw, ce = min(kc, cb + cpw);
   const bool act = q == (g & 3);  // lanes whose B fragment is non-zero
   const int qa = 2 * (q & 1);     // first of the two quads whose columns this lane's D holds
+  const int pr = phys_row(g);     // physical rows pr, pr + 8, pr + 16, pr + 24 of the tile
+  const int spr = K / G;
+  const uint2 *bl = bfrag + g;    // this lane's column of the B fragments
+  uint32_t u = 0, u_abort = 0;
+  bool aborted = false;
 
-  for (int rb = blockIdx.x; rb < p.nblocks; rb += gridDim.x) {
-    const int row0 = (rb * p.rt + rtl) * 16;
-    const int ra = row0 + g, rbw = row0 + g + 8;
-    const bool va = ra < N, vb = rbw < N;
-    const uint32_t *pa = p.wq + static_cast<size_t>(va ? ra : 0) * wpr + 4 * q;
-    const uint32_t *pb = p.wq + static_cast<size_t>(vb ? rbw : 0) * wpr + 4 * q;
-    const __half *sa = p.ws + static_cast<size_t>(va ? ra : 0) * spr;
-    const __half *sb = p.ws + static_cast<size_t>(vb ? rbw : 0) * spr;
-    float acc[NT][2];
+  for (int r = blockIdx.x; r < p.nrounds; r += gridDim.x) {
+    const int tile = r * p.rt + items.rtl;
+    float acc[NT][2][2];  // [token tile][row tile][row g, row g + 8]
 #pragma unroll
-    for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = 0.f;
-
-    for (int c = cb; c < ce; c += kPrefetch) {
-      uint4 wa[kPrefetch], wb[kPrefetch];
-      float s_a[kPrefetch][2], s_b[kPrefetch][2];
-#pragma unroll
-      for (int i = 0; i < kPrefetch; ++i) {
-        const int cc = c + i;
-        const bool okw = cc < ce && (cc * 16 + 4 * q) < wpr;
-        wa[i] = (okw && va) ? ldg_stream_v4(pa + cc * 16) : make_uint4(0u, 0u, 0u, 0u);
-        wb[i] = (okw && vb) ? ldg_stream_v4(pb + cc * 16) : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int si = (128 * cc + 32 * (qa + h)) / G;
-          const bool oks = cc < ce && si < spr;
-          s_a[i][h] = (oks && va) ? __half2float(sa[si]) : 0.f;
-          s_b[i][h] = (oks && vb) ? __half2float(sb[si]) : 0.f;
+    for (int t = 0; t < NT; ++t) acc[t][0][0] = acc[t][0][1] = acc[t][1][0] = acc[t][1][1] = 0.f;
+    if (tile < p.tiles) {
+      for (int i = 0; i < items.per_round; ++i, ++u) {
+        const int sk = items.kw * spw + i;
+        const uint32_t slot = u % S;
+        if (!aborted && !mbar_wait(&full[slot], (u / S) & 1)) {
+          raise_status(kStatusGemvConsumerWait);
+          aborted = true;  // the load never landed: no later load is issued into this ring
+          u_abort = u;
         }
-      }
+        const uint8_t *sb = ring + slot * p.slot_bytes;
+        const int nchunk = min(2, (K - sk * kSlotK + 127) / 128);
+        if (!aborted) {
+#pragma unroll 1
+          for (int c = 0; c < nchunk; ++c) {
+            const int cg = sk * 2 + c;  // global 128-k chunk
+            const uint8_t *rowp = sb + pr * 128 + (((c << 2) | q) ^ pr) * 16;
+            const uint4 w0 = lds128(rowp), w1 = lds128(rowp + 1024), w2 = lds128(rowp + 2048), w3 = lds128(rowp + 3072);
+            // Scales of rows pr + 8m (m = 0..3) for this lane's two columns (groups of quads qa, qa + 1).
+            float s0[4], s1[4];
+            if (p.scales_tma) {
+              const uint8_t *sc = sb + kWordBytes + pr * 16 + (4 * c + qa) * 2;
 #pragma unroll
-      for (int i = 0; i < kPrefetch; ++i) {
-        const int cc = c + i;
-        if (cc >= ce) break;
-        float d[NT][4];
+              for (int m = 0; m < 4; ++m) {
+                const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(sc + m * 8 * 16));
+                s0[m] = v.x;
+                s1[m] = v.y;
+              }
+            } else {
+              const int i0 = (cg * 128 + 32 * qa) / G, i1 = (cg * 128 + 32 * (qa + 1)) / G;
 #pragma unroll
-        for (int t = 0; t < NT; ++t) d[t][0] = d[t][1] = d[t][2] = d[t][3] = 0.f;
-        const uint32_t wav[4] = {wa[i].x, wa[i].y, wa[i].z, wa[i].w};
-        const uint32_t wbv[4] = {wb[i].x, wb[i].y, wb[i].z, wb[i].w};
+              for (int m = 0; m < 4; ++m) {
+                const int row = min(tile * kRows + pr + 8 * m, N - 1);
+                s0[m] = i0 < spr ? __half2float(p.ws[static_cast<size_t>(row) * spr + i0]) : 0.f;
+                s1[m] = i1 < spr ? __half2float(p.ws[static_cast<size_t>(row) * spr + i1]) : 0.f;
+              }
+            }
+            // Four independent accumulator chains: (row tile 0, 1) x (words 0-1, 2-3).
+            float d[NT][2][4], e[NT][2][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-          decode_q4(wav[j], a0, a1, a2, a3);
-          decode_q4(wbv[j], b0, b1, b2, b3);
-          const int s = cc * 8 + 2 * j;
+            for (int t = 0; t < NT; ++t)
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            const uint2 *bf = bfrag + (static_cast<size_t>(t) * nsteps + s) * 8 + g;
-            const uint2 f0 = act ? bf[0] : make_uint2(0u, 0u);
-            const uint2 f1 = act ? bf[8] : make_uint2(0u, 0u);
-            mma_16816(d[t], a0, b0, a1, b1, f0.x, f0.y);
-            mma_16816(d[t], a2, b2, a3, b3, f1.x, f1.y);
+              for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int i2 = 0; i2 < 4; ++i2) d[t][h][i2] = e[t][h][i2] = 0.f;
+            const uint32_t v0[4] = {w0.x, w0.y, w0.z, w0.w}, v1[4] = {w1.x, w1.y, w1.z, w1.w};
+            const uint32_t v2[4] = {w2.x, w2.y, w2.z, w2.w}, v3[4] = {w3.x, w3.y, w3.z, w3.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint32_t a0[4], a1[4], a2[4], a3[4];
+              decode_q4(v0[j], a0);  // row pr
+              decode_q4(v1[j], a1);  // row pr + 8
+              decode_q4(v2[j], a2);  // row pr + 16
+              decode_q4(v3[j], a3);  // row pr + 24
+              const int s = cg * 8 + 2 * j;
+#pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                const uint2 *bf = bl + (static_cast<size_t>(t) * nsteps + s) * 8;
+                uint2 f0 = make_uint2(0u, 0u), f1 = make_uint2(0u, 0u);
+                if (act) {
+                  f0 = bf[0];
+                  f1 = bf[8];
+                }
+                float(&c0)[4] = j < 2 ? d[t][0] : e[t][0];
+                float(&c1)[4] = j < 2 ? d[t][1] : e[t][1];
+                mma_16816(c0, a0[0], a1[0], a0[1], a1[1], f0.x, f0.y);
+                mma_16816(c1, a2[0], a3[0], a2[1], a3[1], f0.x, f0.y);
+                mma_16816(c0, a0[2], a1[2], a0[3], a1[3], f1.x, f1.y);
+                mma_16816(c1, a2[2], a3[2], a2[3], a3[3], f1.x, f1.y);
+              }
+            }
+            // fp32 epilogue: per-column group scale, the 2^24 factor, the offset through the quad sums.
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              const int tok = LO ? t : 2 * t + (q >> 1);
+              if (tok < B) {
+                const bool hi = LO ? (q < 2) : true;
+                const float2 xs = *reinterpret_cast<const float2 *>(xsum + tok * kc * 4 + cg * 4 + qa);
+                const float x0 = hi ? 8.f * xs.x : 0.f, x1 = hi ? 8.f * xs.y : 0.f;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const float dd0 = d[t][h][0] + e[t][h][0], dd1 = d[t][h][1] + e[t][h][1];
+                  const float dd2 = d[t][h][2] + e[t][h][2], dd3 = d[t][h][3] + e[t][h][3];
+                  acc[t][h][0] += s0[2 * h] * fmaf(dd0, 16777216.f, -x0) + s1[2 * h] * fmaf(dd1, 16777216.f, -x1);
+                  acc[t][h][1] += s0[2 * h + 1] * fmaf(dd2, 16777216.f, -x0) + s1[2 * h + 1] * fmaf(dd3, 16777216.f, -x1);
+                }
+              }
+            }
           }
         }
-        // fp32 epilogue: per-column group scale, 2^24 factor, offset through the quad sums of x.
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const int tok = LO ? t : 2 * t + (q >> 1);
-          const bool hi = LO ? (q < 2) : true;
-          if (tok < B) {
-            const float *xs = xsum + tok * kc * 4 + cc * 4 + qa;
-            const float x0 = hi ? 8.f * xs[0] : 0.f, x1 = hi ? 8.f * xs[1] : 0.f;
-            acc[t][0] += s_a[i][0] * fmaf(d[t][0], 16777216.f, -x0) + s_a[i][1] * fmaf(d[t][1], 16777216.f, -x1);
-            acc[t][1] += s_b[i][0] * fmaf(d[t][2], 16777216.f, -x0) + s_b[i][1] * fmaf(d[t][3], 16777216.f, -x1);
-          }
-        }
+        __syncwarp();  // every lane is done with the slot before lane 0 refills it
+        if (!aborted) issue(u + S);
       }
     }
-    // Reduce the quad's lanes, then the K-splitting warps through shared memory.
+    // Reduce the quad's lanes, then (when K is split) the warps through shared memory.
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        float v = acc[t][r];
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        if (LO) v += __shfl_xor_sync(0xffffffffu, v, 2);
-        acc[t][r] = v;
-      }
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float v = acc[t][h][hh];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          if (LO) v += __shfl_xor_sync(0xffffffffu, v, 2);
+          acc[t][h][hh] = v;
+        }
       const int tok = LO ? t : 2 * t + (q >> 1);
       const bool writer = LO ? (q == 0) : ((q & 1) == 0);
       if (writer && tok < B) {
-        red[(kw * 16 * p.rt + rtl * 16 + g) * B + tok] = acc[t][0];
-        red[(kw * 16 * p.rt + rtl * 16 + g + 8) * B + tok] = acc[t][1];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {  // rows pr + 8m: (tile h = m / 2, row g or g + 8 = m % 2)
+          const float v = acc[t][m >> 1][m & 1];
+          if (p.ks == 1) {  // the warp owns whole rows: store directly, no barrier
+            const int row = tile * kRows + pr + 8 * m;
+            if (tile < p.tiles && row < N && !aborted) {
+              float *out = p.y + static_cast<size_t>(tok) * N + row;
+              *out = p.add ? *out + v : v;
+            }
+          } else {
+            red[(items.kw * kRows * p.rt + items.rtl * kRows + pr + 8 * m) * B + tok] = v;
+          }
+        }
       }
     }
+    if (p.ks == 1) continue;
     __syncthreads();
-    const int rows = 16 * p.rt;
+    const int rows = kRows * p.rt;
     for (int it = threadIdx.x; it < rows * B; it += kThreads) {
       const int rl = it / B, tok = it % B;
-      const int r = rb * rows + rl;
-      if (r < N) {
+      const int row = r * rows + rl;
+      if (row < N) {
         float v = 0.f;
         for (int w = 0; w < p.ks; ++w) v += red[(w * rows + rl) * B + tok];
-        float *out = p.y + static_cast<size_t>(tok) * N + r;
+        float *out = p.y + static_cast<size_t>(tok) * N + row;
         *out = p.add ? *out + v : v;
       }
     }
     __syncthreads();
   }
+  // Leave no copy in flight: after an abort, wait (bounded) for the loads issued before it.
+  if (lane == 0 && aborted) {
+    for (uint32_t v = u_abort; v < u_abort + S; ++v) {
+      int tile, sk;
+      if (items.get(v, tile, sk)) mbar_wait(&full[v % S], (v / S) & 1);
+    }
+  }
 }
 
 template <int G, int NT, bool LO>
-int launch(const GemvQ4Params &p0, cudaStream_t stream, const DeviceInfo &dev) {
-  GemvQ4Params p = p0;
-  const int kc = (p.k + 127) / 128;
-  const size_t smem = static_cast<size_t>(NT) * (kc * 8) * 8 * sizeof(uint2) +
-                      static_cast<size_t>(p.batch) * kc * 4 * sizeof(float) +
-                      static_cast<size_t>(kWarps) * 16 * p.batch * sizeof(float);
-  MQ_REQUIRE(smem <= dev.smem_optin, MQ_EUNSUPPORTED, "mq_gemv_q4: k=%d batch=%d needs %zu B of shared memory (max %zu)",
-             p.k, p.batch, smem, dev.smem_optin);
+int launch(const uint32_t *wq, Params p, cudaStream_t stream, const DeviceInfo &dev) {
+  p.scales_tma = G == 32 && (p.k / G) % 8 == 0 && aligned(p.ws, 16);
+  p.slot_bytes = ((kWordBytes + (p.scales_tma ? kRows * kScaleHalvesTma * 2 : 0) + 1023) / 1024) * 1024;
+  Layout L{};
+  for (p.slots = kMaxSlots; p.slots >= 1; --p.slots) {
+    L = layout(p.k, p.batch, NT, p.slots, p.slot_bytes);
+    if (L.total + 1024 <= dev.smem_optin) break;
+  }
+  const size_t smem = L.total + 1024;
+  MQ_REQUIRE(p.slots >= 1 && smem <= dev.smem_optin, MQ_EUNSUPPORTED,
+             "mq_gemv_q4: k=%d batch=%d needs %zu B of shared memory (max %zu)", p.k, p.batch, smem, dev.smem_optin);
+  CUtensorMap wmap, smap;
+  if (int rc = encode_tmap_2d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.k / 8, p.n, static_cast<uint64_t>(p.k) / 2, 32,
+                              kRows, CU_TENSOR_MAP_SWIZZLE_128B, "mq_gemv_q4 weights"))
+    return rc;
+  if (p.scales_tma) {
+    if (int rc = encode_tmap_2d(&smap, p.ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k / G, p.n,
+                                static_cast<uint64_t>(p.k / G) * 2, kScaleHalvesTma, kRows, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                "mq_gemv_q4 scales"))
+      return rc;
+  } else {
+    smap = wmap;  // not read
+  }
+  // Split K across warps (ks divides kWarps) until the rounds cover every SM or K runs out of slots.
+  const int nslotk = (p.k + kSlotK - 1) / kSlotK;
+  p.ks = 1;
+  for (int ks = 1; ks <= kWarps; ks *= 2) {
+    if (ks > nslotk) break;
+    p.ks = ks;
+    if ((p.tiles * ks + kWarps - 1) / kWarps >= dev.sms) break;
+  }
+  p.rt = kWarps / p.ks;
+  p.nrounds = (p.tiles + p.rt - 1) / p.rt;
   auto kern = gemv_q4_kernel<G, NT, LO>;
-  static size_t configured = 0;  // largest dynamic smem size set on this instantiation
-  if (smem > 48 * 1024 && smem > configured) {
+  static size_t configured = 0;
+  if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_gemv_q4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured = smem;
   }
-  int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
-  if (e != cudaSuccess || per_sm < 1) return fail(MQ_ECUDA, "mq_gemv_q4: occupancy query failed (%s)", cudaGetErrorString(e));
-  const int grid = std::min(p.nblocks, dev.sms * per_sm);
-  kern<<<grid, kThreads, smem, stream>>>(p);
+  const int grid = std::min(p.nrounds, dev.sms);
+  kern<<<grid, kThreads, smem, stream>>>(wmap, smap, p);
   return check_launch("mq_gemv_q4");
 }
 
 template <int G>
-int dispatch_nt(const GemvQ4Params &p, cudaStream_t s, const DeviceInfo &dev) {
+int dispatch_nt(const uint32_t *wq, const Params &p, cudaStream_t s, const DeviceInfo &dev) {
   const bool lo = !p.x_f16 && p.batch <= 2;
-  if (lo) return p.batch == 1 ? launch<G, 1, true>(p, s, dev) : launch<G, 2, true>(p, s, dev);
-  return p.batch <= 2 ? launch<G, 1, false>(p, s, dev) : launch<G, 2, false>(p, s, dev);
+  if (lo) return p.batch == 1 ? launch<G, 1, true>(wq, p, s, dev) : launch<G, 2, true>(wq, p, s, dev);
+  return p.batch <= 2 ? launch<G, 1, false>(wq, p, s, dev) : launch<G, 2, false>(wq, p, s, dev);
 }
 
-// Used by the batched path and by the MoE decode: one GEMV launch over [n, k] with batch <= 4.
-int gemv_q4_small(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y, int64_t n,
-                  int64_t k, int group, int batch, int add, cudaStream_t stream) {
+// One GEMV launch over [n, k] with batch <= 4 (also used by the MoE decode).
+int gemv_q4_small(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y, int64_t n, int64_t k,
+                  int group, int batch, int add, cudaStream_t stream) {
   DeviceInfo dev;
   if (int rc = device_info(&dev)) return rc;
-  GemvQ4Params p{};
-  p.wq = wq;
+  Params p{};
   p.ws = reinterpret_cast<const __half *>(ws);
   p.x = x;
   p.y = y;
@@ -279,18 +441,11 @@ int gemv_q4_small(const uint32_t *wq, const uint16_t *ws, const void *x, int x_d
   p.batch = batch;
   p.x_f16 = x_dtype == MQ_F16;
   p.add = add != 0;
-  const int kc = static_cast<int>((k + 127) / 128);
-  const int tiles = static_cast<int>((n + 15) / 16);
-  const int target = dev.sms * 16;  // warps wanted in flight
-  int ks = 1;
-  while (ks < kWarps && static_cast<long>(tiles) * ks < target && ks * 2 <= kc) ks *= 2;
-  p.ks = ks;
-  p.rt = kWarps / ks;
-  p.nblocks = (tiles + p.rt - 1) / p.rt;
+  p.tiles = (p.n + kRows - 1) / kRows;
   switch (group) {
-    case 32: return dispatch_nt<32>(p, stream, dev);
-    case 64: return dispatch_nt<64>(p, stream, dev);
-    default: return dispatch_nt<128>(p, stream, dev);
+    case 32: return dispatch_nt<32>(wq, p, stream, dev);
+    case 64: return dispatch_nt<64>(wq, p, stream, dev);
+    default: return dispatch_nt<128>(wq, p, stream, dev);
   }
 }
 
@@ -307,8 +462,8 @@ extern "C" int mq_gemv_q4(const uint32_t *wq, const uint16_t *ws, const void *x,
              static_cast<long long>(k), group);
   MQ_REQUIRE(x_dtype == MQ_F32 || x_dtype == MQ_F16, MQ_EINVAL, "mq_gemv_q4: x_dtype must be MQ_F32 or MQ_F16");
   MQ_REQUIRE(batch >= 1 && batch <= 64, MQ_EINVAL, "mq_gemv_q4: batch must be in 1..64 (got %d)", batch);
-  MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(ws, 2) && mq::aligned(x, 4) && mq::aligned(y, 4), MQ_EALIGN,
-             "mq_gemv_q4: wq must be 16-byte aligned, x and y 4-byte aligned");
+  MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(ws, 2) && mq::aligned(x, 16) && mq::aligned(y, 4), MQ_EALIGN,
+             "mq_gemv_q4: wq and x must be 16-byte aligned, y 4-byte aligned");
   if (batch > 4) return mq::fail(MQ_EUNSUPPORTED, "mq_gemv_q4: batch > 4 needs the tensor-core GEMM path");
   return mq::gemv::gemv_q4_small(wq, ws, x, x_dtype, y, n, k, group, batch, add, static_cast<cudaStream_t>(stream));
 }

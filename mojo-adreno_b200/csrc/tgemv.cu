@@ -7,8 +7,12 @@
 // multiplies exactly (codes are small integers, x is fp16) and accumulates in fp32, so its error
 // against exact arithmetic is far below the reference's own.
 //
-// B200 design (HBM-bound: 0.2656 B per weight, ~92 weights per SM clock at 6.5 TB/s, leaving
-// under 1.4 issued instructions per weight):
+// B200 design (HBM-bound: 0.2656 B per weight, ~92 weights per SM clock at 6.5 TB/s, so under
+// 1.4 issued instructions per weight):
+//  * Streaming: each of 16 warps TMA-loads its own 32-output x 1024-k tiles of the [k/16][n]
+//    word array (64 word rows of 128 bytes, 128-byte swizzle) and their [k/128][n] scales into a
+//    private shared-memory ring and refills a slot as soon as it is consumed. Persistent CTAs,
+//    one per SM.
 //  * Decode: a 2-bit code pair masked into the mantissa of an fp16x2 register is an exact
 //    subnormal: (w & (0x00030003 << 2j)) holds c * 4^j * 2^-24 for j = 0..3; one shift by 8 gives
 //    the other four pairs. Eight ANDs and one shift per 16 weights; the 4^-j factors go into the
@@ -16,9 +20,9 @@
 //    group's sum of x: sum (c - 1) x = sum c x - sum x.
 //  * Multiply: mma.m16n8k16 (fp16 in, fp32 accumulate); one group (128 k) = 8 k16 steps, after
 //    which the group's fp16 scale is applied in fp32.
-//  * Memory: the layout is [k/16][n] words, so a lane loads one 128-bit vector = 4 adjacent
-//    outputs x 16 k; 8 lanes of a quad row read 128 contiguous bytes. A warp owns 32 outputs
-//    (two m16 tiles) over a K range; small matrices split K over the CTA's 8 warps.
+//  * Bank conflicts: lane (g, q) reads word row 4b + q and the 16-byte column chunk
+//    (g >> 1) | (g & 1) << 2; with the swizzle's XOR by row % 8 the 8 lanes of a phase hit 8
+//    distinct chunks.
 #include <algorithm>
 
 #include "common.cuh"
@@ -26,20 +30,31 @@
 namespace mq {
 namespace tg {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = 8;
-constexpr int kPrefetch = 4;  // groups (2 x 128-bit loads per lane each) in flight
+constexpr int kWarps = 16;
+constexpr int kThreads = 32 * kWarps;
+constexpr int kMaxSlots = 2;
+constexpr int kCols = 32;                 // outputs of a tile (two m16 tiles)
+// A slot holds 32 outputs x SK k: SK/16 word rows of 128 bytes and SK/128 scale rows of 64 bytes.
+// SK = 1024 normally; 512 when x (2 bytes per k per token) leaves too little shared memory.
+template <int SK>
+struct Slot {
+  static constexpr int kSlotK = SK;
+  static constexpr int kWordRows = SK / 16;
+  static constexpr int kWordBytes = kWordRows * 128;
+  static constexpr int kGroups = SK / 128;
+  static constexpr int kScaleBytes = kGroups * kCols * 2;
+  static constexpr int kSlotBytes = ((kWordBytes + kScaleBytes + 1023) / 1024) * 1024;
+};
 
-struct TgemvParams {
+struct Params {
   const uint16_t *x;
-  const uint32_t *w;
   const __half *s;
   float *y;
   int n, k, batch;
-  int ks, rt, nblocks;
+  int ks, rt, tiles, nrounds, slots, scales_tma;
 };
 
-// Pairs j = 0..7 of a word: codes (j, j + 8) for j < 4 from w, (j, j + 8) for j >= 4 from w >> 8.
+// Pairs j = 0..7 of a word: codes (j, j + 8), factor 4^(j % 4), j >= 4 from w >> 8.
 __device__ __forceinline__ void decode_t2(uint32_t w, uint32_t (&q)[8]) {
   q[0] = w & 0x00030003u;
   q[1] = w & 0x000C000Cu;
@@ -52,29 +67,101 @@ __device__ __forceinline__ void decode_t2(uint32_t w, uint32_t (&q)[8]) {
   q[7] = v & 0x00C000C0u;
 }
 
-template <int NB>  // NB = batch (columns used)
-__global__ void __launch_bounds__(kThreads) tgemv_kernel(const TgemvParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int K = p.k, N = p.n;
-  const int kb = K / 64;    // blocks of 4 k16 steps
-  const int kg = K / 128;   // scale groups
-  const int nsteps = kb * 4;
-  uint2 *bfrag = reinterpret_cast<uint2 *>(smem);             // [nsteps][NB][4]
-  float *xsum = reinterpret_cast<float *>(bfrag + nsteps * NB * 4);  // [NB][kg]
-  float *red = xsum + NB * kg;                                // [kWarps][32][NB]
+struct Layout {
+  uint32_t slots, bfrag, xsum, red, bars, total;
+};
 
-  // ---- stage x: per step s = 4b + t and lane (column tok, quad q):
-  //      b0 = (x[16(4b+q) + 2t], x[.. + 2t + 8]) / 4^e(2t), b1 = (x[.. + 2t + 1], x[.. + 2t + 9]) / 4^e(2t+1)
+template <int SK>
+__host__ __device__ inline Layout layout(int k, int nb, int slots) {
+  Layout L;
+  const int kb = k / 64, kg = k / 128;
+  L.slots = 0;
+  L.bfrag = kWarps * slots * Slot<SK>::kSlotBytes;
+  L.xsum = L.bfrag + kb * 4 * nb * 4 * 8;
+  L.red = L.xsum + nb * kg * 4;
+  L.bars = (L.red + kWarps * kCols * nb * 4 + 7) / 8 * 8;
+  L.total = L.bars + kWarps * kMaxSlots * 8;
+  return L;
+}
+
+struct Items {
+  int rtl, kw, spw, per_round, rt, tiles, grid, cta;
+  __device__ bool get(uint32_t u, int &tile, int &sk) const {
+    if (per_round <= 0) return false;
+    const int j = static_cast<int>(u) / per_round, i = static_cast<int>(u) % per_round;
+    tile = (cta + j * grid) * rt + rtl;
+    sk = kw * spw + i;
+    return tile < tiles;
+  }
+};
+
+template <int NB, int SK>  // NB = batch (D columns used), SK = k of a slot
+__global__ void __launch_bounds__(kThreads, 1)
+    tgemv_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap, const Params p) {
+  constexpr int kSlotK = Slot<SK>::kSlotK, kWordRows = Slot<SK>::kWordRows, kWordBytes = Slot<SK>::kWordBytes;
+  constexpr int kGroups = Slot<SK>::kGroups, kScaleBytes = Slot<SK>::kScaleBytes, kSlotBytes = Slot<SK>::kSlotBytes;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const Layout L = layout<SK>(p.k, NB, p.slots);
+  const int K = p.k, N = p.n, S = p.slots;
+  const int kb = K / 64, kg = K / 128;
+  const int nslotk = (K + kSlotK - 1) / kSlotK;
+  const int spw = (nslotk + p.ks - 1) / p.ks;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars) + warp * kMaxSlots;
+  uint8_t *ring = smem + L.slots + warp * S * kSlotBytes;
+  const uint32_t bytes = kWordBytes + (p.scales_tma ? kScaleBytes : 0);
+
+  Items items;
+  items.rtl = warp / p.ks;
+  items.kw = warp % p.ks;
+  items.spw = spw;
+  items.per_round = min(spw, nslotk - items.kw * spw);
+  items.rt = p.rt;
+  items.tiles = p.tiles;
+  items.grid = gridDim.x;
+  items.cta = blockIdx.x;
+
+  auto issue = [&](uint32_t u) {
+    int tile, sk;
+    if (lane != 0 || !items.get(u, tile, sk)) return;
+    const int slot = u % S;
+    uint64_t *bar = full + slot;
+    uint8_t *dst = ring + slot * kSlotBytes;
+    mbar_expect_tx(bar, bytes);
+    tma_load_2d(dst, &wmap, bar, tile * kCols, sk * kWordRows);
+    if (p.scales_tma) tma_load_2d(dst + kWordBytes, &smap, bar, tile * kCols, sk * kGroups);
+  };
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(full + s, 1);
+    fence_mbar_init();
+    prefetch_tmap(&wmap);
+    if (p.scales_tma) prefetch_tmap(&smap);
+  }
+  __syncwarp();
+  for (int s = 0; s < S; ++s) issue(s);
+
+  uint2 *bfrag = reinterpret_cast<uint2 *>(smem + L.bfrag);  // [kb*4 steps][NB][4]
+  float *xsum = reinterpret_cast<float *>(smem + L.xsum);     // [NB][kg]
+  float *red = reinterpret_cast<float *>(smem + L.red);       // [kWarps][32][NB]
+
+  // Stage x: per step s = 4b + t and lane (column tok, quad q):
+  //   b0 = (x[16(4b+q) + 2t], x[.. + 2t + 8]) / 4^(2t % 4), b1 = (x[.. + 2t + 1], x[.. + 2t + 9]) / 4^((2t+1) % 4)
   for (int it = threadIdx.x; it < NB * kb * 4; it += kThreads) {
-    const int tok = it / (kb * 4), wr = it % (kb * 4);  // wr = word row k/16
+    const int tok = it / (kb * 4), wr = it % (kb * 4);  // wr = word row k / 16
     const int b = wr / 4, q = wr % 4;
-    const __half *xr = reinterpret_cast<const __half *>(p.x) + static_cast<size_t>(tok) * K + 16 * wr;
+    const uint4 *xr = reinterpret_cast<const uint4 *>(p.x + static_cast<size_t>(tok) * K + 16 * wr);
+    const uint4 v0 = xr[0], v1 = xr[1];
+    const __half *h0 = reinterpret_cast<const __half *>(&v0), *h1 = reinterpret_cast<const __half *>(&v1);
     float xv[16];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) xv[e] = __half2float(xr[e]);
+    for (int e = 0; e < 8; ++e) {
+      xv[e] = __half2float(h0[e]);
+      xv[8 + e] = __half2float(h1[e]);
+    }
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-      const int j0 = 2 * t, j1 = 2 * t + 1;  // pair indices
+      const int j0 = 2 * t, j1 = 2 * t + 1;
       const float f0 = 1.f / static_cast<float>(1 << (2 * (j0 & 3))), f1 = 1.f / static_cast<float>(1 << (2 * (j1 & 3)));
       bfrag[((4 * b + t) * NB + tok) * 4 + q] =
           make_uint2(pack_half2(xv[j0] * f0, xv[j0 + 8] * f0), pack_half2(xv[j1] * f1, xv[j1 + 8] * f1));
@@ -82,103 +169,121 @@ __global__ void __launch_bounds__(kThreads) tgemv_kernel(const TgemvParams p) {
   }
   for (int it = threadIdx.x; it < NB * kg; it += kThreads) {
     const int tok = it / kg, gi = it % kg;
-    const __half *xr = reinterpret_cast<const __half *>(p.x) + static_cast<size_t>(tok) * K + 128 * gi;
+    const __half2 *xr = reinterpret_cast<const __half2 *>(p.x + static_cast<size_t>(tok) * K + 128 * gi);
     float s = 0.f;
-    for (int e = 0; e < 128; ++e) s += __half2float(xr[e]);
+    for (int e = 0; e < 64; ++e) {
+      const float2 v = __half22float2(xr[e]);
+      s += v.x + v.y;
+    }
     xsum[tok * kg + gi] = s;
   }
   __syncthreads();
 
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int g = lane >> 2, q = lane & 3;
-  const int kw = warp % p.ks, rtl = warp / p.ks;
-  const int gpw = (kg + p.ks - 1) / p.ks;
-  const int gb = kw * gpw, ge = min(kg, gb + gpw);
   const bool act = g < NB;
-  const int t0 = 2 * q, t1 = 2 * q + 1;  // D columns (tokens) of this lane
+  const int t0 = 2 * q, t1 = 2 * q + 1;       // D columns (tokens) of this lane
+  const int cgc = (g >> 1) | ((g & 1) << 2);  // this lane's 16-byte column chunk: outputs 4 cgc .. + 3
+  uint32_t u = 0, u_abort = 0;
+  bool aborted = false;
 
-  for (int rb = blockIdx.x; rb < p.nblocks; rb += gridDim.x) {
-    const int n0 = (rb * p.rt + rtl) * 32;
-    const int col = n0 + 4 * g;
-    const bool valid = col < N;
-    const uint32_t *wp = p.w + (valid ? col : 0) + static_cast<size_t>(q) * N;
-    const __half *sp = p.s + (valid ? col : 0);
+  for (int r = blockIdx.x; r < p.nrounds; r += gridDim.x) {
+    const int tile = r * p.rt + items.rtl;
+    const int col = tile * kCols + 4 * cgc;
     float acc[2][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[0][i] = acc[1][i] = 0.f;
-
-    for (int gr = gb; gr < ge; gr += kPrefetch) {
-      uint4 wv[kPrefetch][2];
-      float sc[kPrefetch][4];
-#pragma unroll
-      for (int i = 0; i < kPrefetch; ++i) {
-        const int gg = gr + i;
-        const bool ok = valid && gg < ge;
-#pragma unroll
-        for (int h = 0; h < 2; ++h)  // blocks 2gg and 2gg+1: word rows 4(2gg+h) + q
-          wv[i][h] = ok ? ldg_stream_v4(wp + static_cast<size_t>(4 * (2 * gg + h)) * N) : make_uint4(0u, 0u, 0u, 0u);
-        if (ok) {
-          const uint2 sv = *reinterpret_cast<const uint2 *>(sp + static_cast<size_t>(gg) * N);
-          const __half2 lo = *reinterpret_cast<const __half2 *>(&sv.x), hi = *reinterpret_cast<const __half2 *>(&sv.y);
-          sc[i][0] = __low2float(lo);
-          sc[i][1] = __high2float(lo);
-          sc[i][2] = __low2float(hi);
-          sc[i][3] = __high2float(hi);
-        } else {
-          sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+    if (tile < p.tiles) {
+      for (int i = 0; i < items.per_round; ++i, ++u) {
+        const int sk = items.kw * spw + i;
+        const uint32_t slot = u % S;
+        if (!aborted && !mbar_wait(&full[slot], (u / S) & 1)) {
+          raise_status(kStatusGemvConsumerWait);
+          aborted = true;
+          u_abort = u;
         }
-      }
+        const uint8_t *sb = ring + slot * kSlotBytes;
+        const int ngr = min(kGroups, kg - sk * kGroups);
+        if (!aborted) {
+          for (int gi = 0; gi < ngr; ++gi) {
+            const int gg = sk * kGroups + gi;  // global group
+            float sc[4];
+            if (p.scales_tma) {
+              const uint2 sv = *reinterpret_cast<const uint2 *>(sb + kWordBytes + gi * kCols * 2 + cgc * 8);
+              const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&sv.x));
+              const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&sv.y));
+              sc[0] = a.x, sc[1] = a.y, sc[2] = b.x, sc[3] = b.y;
+            } else {
 #pragma unroll
-      for (int i = 0; i < kPrefetch; ++i) {
-        const int gg = gr + i;
-        if (gg >= ge) break;
-        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+              for (int o = 0; o < 4; ++o)
+                sc[o] = col + o < N ? __half2float(p.s[static_cast<size_t>(gg) * N + col + o]) : 0.f;
+            }
+            // Four independent accumulator chains: (tile 0, tile 1) x (block h = 0, 1).
+            float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+            float e0[4] = {0.f, 0.f, 0.f, 0.f}, e1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t qx[8], qy[8], qz[8], qw[8];
-          decode_t2(wv[i][h].x, qx);  // output col + 0: tile 0 row g
-          decode_t2(wv[i][h].y, qy);  // col + 1: tile 0 row g + 8
-          decode_t2(wv[i][h].z, qz);  // col + 2: tile 1 row g
-          decode_t2(wv[i][h].w, qw);  // col + 3: tile 1 row g + 8
-          const int b = 2 * gg + h;
+            for (int h = 0; h < 2; ++h) {
+              const int b = 2 * gi + h, wr = 4 * b + q;
+              const uint4 wv = *reinterpret_cast<const uint4 *>(sb + wr * 128 + ((cgc ^ (wr & 7)) << 4));
+              uint32_t qx[8], qy[8], qz[8], qw[8];
+              decode_t2(wv.x, qx);  // output col + 0: tile 0 row g
+              decode_t2(wv.y, qy);  // col + 1: tile 0 row g + 8
+              decode_t2(wv.z, qz);  // col + 2: tile 1 row g
+              decode_t2(wv.w, qw);  // col + 3: tile 1 row g + 8
+              const int bg = sk * (kSlotK / 64) + b;  // global block
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const uint2 f = act ? bfrag[((4 * b + t) * NB + g) * 4 + q] : make_uint2(0u, 0u);
-            mma_16816(d0, qx[2 * t], qy[2 * t], qx[2 * t + 1], qy[2 * t + 1], f.x, f.y);
-            mma_16816(d1, qz[2 * t], qw[2 * t], qz[2 * t + 1], qw[2 * t + 1], f.x, f.y);
+              for (int t = 0; t < 4; ++t) {
+                uint2 f = make_uint2(0u, 0u);
+                if (act) f = bfrag[((4 * bg + t) * NB + g) * 4 + q];
+                mma_16816(h ? e0 : d0, qx[2 * t], qy[2 * t], qx[2 * t + 1], qy[2 * t + 1], f.x, f.y);
+                mma_16816(h ? e1 : d1, qz[2 * t], qw[2 * t], qz[2 * t + 1], qw[2 * t + 1], f.x, f.y);
+              }
+            }
+#pragma unroll
+            for (int i2 = 0; i2 < 4; ++i2) {
+              d0[i2] += e0[i2];
+              d1[i2] += e1[i2];
+            }
+            // D: [0] = (row g, col t0), [1] = (row g, col t1), [2] = (row g+8, col t0), [3] = (row g+8, col t1)
+            if (t0 < NB) {
+              const float xs = xsum[t0 * kg + gg];
+              acc[0][0] += sc[0] * fmaf(d0[0], 16777216.f, -xs);
+              acc[0][1] += sc[1] * fmaf(d0[2], 16777216.f, -xs);
+              acc[0][2] += sc[2] * fmaf(d1[0], 16777216.f, -xs);
+              acc[0][3] += sc[3] * fmaf(d1[2], 16777216.f, -xs);
+            }
+            if (t1 < NB) {
+              const float xs = xsum[t1 * kg + gg];
+              acc[1][0] += sc[0] * fmaf(d0[1], 16777216.f, -xs);
+              acc[1][1] += sc[1] * fmaf(d0[3], 16777216.f, -xs);
+              acc[1][2] += sc[2] * fmaf(d1[1], 16777216.f, -xs);
+              acc[1][3] += sc[3] * fmaf(d1[3], 16777216.f, -xs);
+            }
           }
         }
-        // D: d[0] = (row g, col t0), d[1] = (row g, col t1), d[2] = (row g+8, col t0), d[3] = (row g+8, col t1)
-        if (t0 < NB) {
-          const float xs = xsum[t0 * kg + gg];
-          acc[0][0] += sc[i][0] * fmaf(d0[0], 16777216.f, -xs);
-          acc[0][1] += sc[i][1] * fmaf(d0[2], 16777216.f, -xs);
-          acc[0][2] += sc[i][2] * fmaf(d1[0], 16777216.f, -xs);
-          acc[0][3] += sc[i][3] * fmaf(d1[2], 16777216.f, -xs);
-        }
-        if (t1 < NB) {
-          const float xs = xsum[t1 * kg + gg];
-          acc[1][0] += sc[i][0] * fmaf(d0[1], 16777216.f, -xs);
-          acc[1][1] += sc[i][1] * fmaf(d0[3], 16777216.f, -xs);
-          acc[1][2] += sc[i][2] * fmaf(d1[1], 16777216.f, -xs);
-          acc[1][3] += sc[i][3] * fmaf(d1[3], 16777216.f, -xs);
-        }
+        __syncwarp();
+        if (!aborted) issue(u + S);
       }
     }
-    // Partials of this warp's K range into shared memory: red[kw][32 outputs][NB].
-    const int rows = 32 * p.rt;
+    const int rows = kCols * p.rt;
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int tok = 2 * q + u;
+    for (int uu = 0; uu < 2; ++uu) {
+      const int tok = 2 * q + uu;
       if (tok < NB) {
+        if (p.ks == 1) {  // the warp owns whole outputs: store directly, no barrier
+          if (tile < p.tiles && col < N && !aborted)
+            *reinterpret_cast<float4 *>(p.y + static_cast<size_t>(tok) * N + col) =
+                make_float4(acc[uu][0], acc[uu][1], acc[uu][2], acc[uu][3]);
+        } else {
 #pragma unroll
-        for (int o = 0; o < 4; ++o) red[(kw * rows + rtl * 32 + 4 * g + o) * NB + tok] = acc[u][o];
+          for (int o = 0; o < 4; ++o) red[(items.kw * rows + items.rtl * kCols + 4 * cgc + o) * NB + tok] = acc[uu][o];
+        }
       }
     }
+    if (p.ks == 1) continue;
     __syncthreads();
     for (int it = threadIdx.x; it < rows * NB; it += kThreads) {
       const int rl = it / NB, tok = it % NB;
-      const int i = rb * rows + rl;
+      const int i = r * rows + rl;
       if (i < N) {
         float v = 0.f;
         for (int w = 0; w < p.ks; ++w) v += red[(w * rows + rl) * NB + tok];
@@ -187,28 +292,61 @@ __global__ void __launch_bounds__(kThreads) tgemv_kernel(const TgemvParams p) {
     }
     __syncthreads();
   }
+  if (lane == 0 && aborted) {
+    for (uint32_t v = u_abort; v < u_abort + S; ++v) {
+      int tile, sk;
+      if (items.get(v, tile, sk)) mbar_wait(&full[v % S], (v / S) & 1);
+    }
+  }
 }
 
-template <int NB>
-int launch(const TgemvParams &p, cudaStream_t stream, const DeviceInfo &dev) {
-  const int kb = p.k / 64, kg = p.k / 128;
-  const size_t smem = static_cast<size_t>(kb) * 4 * NB * 4 * sizeof(uint2) + static_cast<size_t>(NB) * kg * sizeof(float) +
-                      static_cast<size_t>(kWarps) * 32 * NB * sizeof(float);
+template <int NB, int SK>
+int launch_sk(const uint32_t *w, Params p, cudaStream_t stream, const DeviceInfo &dev) {
+  using Sl = Slot<SK>;
+  Layout L{};
+  for (p.slots = kMaxSlots; p.slots >= 1; --p.slots) {
+    L = layout<SK>(p.k, NB, p.slots);
+    if (L.total + 1024 <= dev.smem_optin) break;
+  }
+  const size_t smem = L.total + 1024;
   MQ_REQUIRE(smem <= dev.smem_optin, MQ_EUNSUPPORTED, "mq_tgemv: k=%d batch=%d needs %zu B of shared memory (max %zu)", p.k,
              NB, smem, dev.smem_optin);
-  auto kern = tgemv_kernel<NB>;
+  CUtensorMap wmap, smap;
+  if (int rc = encode_tmap_2d(&wmap, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.n, p.k / 16, static_cast<uint64_t>(p.n) * 4,
+                              kCols, Sl::kWordRows, CU_TENSOR_MAP_SWIZZLE_128B, "mq_tgemv words"))
+    return rc;
+  p.scales_tma = p.n % 8 == 0 && aligned(p.s, 16);
+  if (p.scales_tma) {
+    if (int rc = encode_tmap_2d(&smap, p.s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.n, p.k / 128,
+                                static_cast<uint64_t>(p.n) * 2, kCols, Sl::kGroups, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                "mq_tgemv scales"))
+      return rc;
+  } else {
+    smap = wmap;  // not read
+  }
+  const int nslotk = (p.k + SK - 1) / SK;
+  int ks = 1;
+  while (ks < kWarps && ks < nslotk && (p.tiles * ks + kWarps - 1) / kWarps < dev.sms) ks *= 2;
+  p.ks = ks;
+  p.rt = kWarps / ks;
+  p.nrounds = (p.tiles + p.rt - 1) / p.rt;
+  auto kern = tgemv_kernel<NB, SK>;
   static size_t configured = 0;
-  if (smem > 48 * 1024 && smem > configured) {
+  if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_tgemv: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured = smem;
   }
-  int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
-  if (e != cudaSuccess || per_sm < 1) return fail(MQ_ECUDA, "mq_tgemv: occupancy query failed (%s)", cudaGetErrorString(e));
-  const int grid = std::min(p.nblocks, dev.sms * per_sm);
-  kern<<<grid, kThreads, smem, stream>>>(p);
+  const int grid = std::min(p.nrounds, dev.sms);
+  kern<<<grid, kThreads, smem, stream>>>(wmap, smap, p);
   return check_launch("mq_tgemv");
+}
+
+template <int NB>
+int launch(const uint32_t *w, Params p, cudaStream_t stream, const DeviceInfo &dev) {
+  const Layout big = layout<1024>(p.k, NB, 1);
+  if (big.total + 1024 <= dev.smem_optin) return launch_sk<NB, 1024>(w, p, stream, dev);
+  return launch_sk<NB, 512>(w, p, stream, dev);
 }
 
 }  // namespace tg
@@ -222,31 +360,23 @@ extern "C" int mq_tgemv(const uint16_t *x, const uint32_t *w, const uint16_t *s,
   MQ_REQUIRE(k % 128 == 0, MQ_EINVAL, "mq_tgemv: k=%lld must be a multiple of 128", static_cast<long long>(k));
   MQ_REQUIRE(n % 4 == 0, MQ_EINVAL, "mq_tgemv: n=%lld must be a multiple of 4", static_cast<long long>(n));
   MQ_REQUIRE(batch >= 1 && batch <= 4, MQ_EINVAL, "mq_tgemv: batch must be in 1..4 (got %d)", batch);
-  MQ_REQUIRE(mq::aligned(w, 16) && mq::aligned(s, 8) && mq::aligned(x, 2) && mq::aligned(y, 4), MQ_EALIGN,
-             "mq_tgemv: w must be 16-byte aligned, s 8-byte aligned");
+  MQ_REQUIRE(mq::aligned(w, 16) && mq::aligned(s, 8) && mq::aligned(x, 16) && mq::aligned(y, 4), MQ_EALIGN,
+             "mq_tgemv: w and x must be 16-byte aligned, s 8-byte aligned");
   mq::DeviceInfo dev;
   if (int rc = mq::device_info(&dev)) return rc;
-  mq::tg::TgemvParams p{};
+  mq::tg::Params p{};
   p.x = x;
-  p.w = w;
   p.s = reinterpret_cast<const __half *>(s);
   p.y = y;
   p.n = static_cast<int>(n);
   p.k = static_cast<int>(k);
   p.batch = batch;
-  const int kg = static_cast<int>(k / 128);
-  const int tiles = static_cast<int>((n + 31) / 32);
-  const int target = dev.sms * 16;
-  int ks = 1;
-  while (ks < mq::tg::kWarps && static_cast<long>(tiles) * ks < target && ks * 2 <= kg) ks *= 2;
-  p.ks = ks;
-  p.rt = mq::tg::kWarps / ks;
-  p.nblocks = (tiles + p.rt - 1) / p.rt;
+  p.tiles = static_cast<int>((n + mq::tg::kCols - 1) / mq::tg::kCols);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (batch) {
-    case 1: return mq::tg::launch<1>(p, st, dev);
-    case 2: return mq::tg::launch<2>(p, st, dev);
-    case 3: return mq::tg::launch<3>(p, st, dev);
-    default: return mq::tg::launch<4>(p, st, dev);
+    case 1: return mq::tg::launch<1>(w, p, st, dev);
+    case 2: return mq::tg::launch<2>(w, p, st, dev);
+    case 3: return mq::tg::launch<3>(w, p, st, dev);
+    default: return mq::tg::launch<4>(w, p, st, dev);
   }
 }

@@ -85,7 +85,7 @@ def test_gemv_extreme_values(cuda):
     ws = np.full((n, k // 32), 0.0625, np.float16)
     ws[5] = 0
     ws[6] = np.float16(6e-8)
-    x = np.linspace(-100, 100, k, dtype=np.float32)[None]
+    x = np.linspace(-100, 60, k, dtype=np.float32)[None]  # sum(x) != 0: the reference is well away from zero
     y = run_gemv(cuda, wq, ws, x, 32)
     ref = q4.gemv(wq, ws, x, 32)
     assert normwise(y, ref) <= TIGHT_F32

@@ -69,4 +69,5 @@ def test_tgemv_all_codes(cuda):
     y = run(cuda, x, w, s, n, k)
     ref = ternary.tgemv(x, w, s, n, k)
     assert normwise(y, ref) <= TIGHT
-    assert np.all(y[0, 8:16] == 0.0)
+    # code 1 is weight 0: zero up to the fp32 rounding of the -sum(x) correction
+    assert np.abs(y[0, 8:16]).max() <= 1e-6 * 0.5 * np.abs(x.astype(np.float64)).sum()
