@@ -24,6 +24,7 @@
 #ifndef MQ_H
 #define MQ_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -75,12 +76,26 @@ MQ_API int mq_unpack_q4(const uint32_t *wq, const uint16_t *ws, int8_t *q, uint1
  * the G=128 expert rows qwen3moe/kernels/moek.mojo:29-45) and the batched t_gemv_q4 / p_gemv_q4
  * (qwen3moe/kernels/moek.mojo:273-281,528-545) with the argument order wq, ws, x, y, cols.
  * x: [batch][k] fp32 (x_dtype MQ_F32) or fp16 (MQ_F16); y: [batch][n] fp32.
- * group in {32, 64, 128}; k % 32 == 0 and k % group == 0; 1 <= batch <= 64 (batch > 4 runs the
- * tensor-core GEMM); add != 0 adds into y (gemv_add_q4).
- * wq, ws, x: 16-, 4- and 16-byte aligned.
+ * group in {32, 64, 128}; k % 32 == 0 and k % group == 0; add != 0 adds into y (gemv_add_q4).
+ * 1 <= batch <= 64: batch <= 4 runs the streaming GEMV; batch > 4 runs the tensor-core GEMM
+ * (mq_gemm_q4), which needs fp16 x here (fp32 x needs mq_gemm_q4's workspace) and k % 256 == 0.
+ * wq and x 16-byte aligned (ws too for batch > 4), y 4-byte aligned.
  */
 MQ_API int mq_gemv_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y,
                int64_t n, int64_t k, int group, int batch, int add, void *stream);
+
+/*
+ * Prefill GEMM over int4 weights on the tcgen05 tensor cores: y[t][r] (+)= sum_c W[r][c] * x[t][c]
+ * for t < m tokens. Replaces p_gemm_q4 (llama/kernels/prefill/p_gemm_q4.mojo:26-62, argument order
+ * wq, ws, x, y, n, k) and gemm_q4 (lfm2/kernels/lk.mojo:458-495), without their rows % 128 and
+ * n % 128 restrictions. x: [m][k] fp16 (MQ_F16) or fp32 (MQ_F32, converted to fp16 in `workspace`,
+ * mq_gemm_q4_workspace_size() bytes); y: [m][n] fp32. group in {32, 64, 128}; k % 256 == 0.
+ * The product uses fp16 x and fp16 q*scale with fp32 accumulation. wq, ws, x and workspace 16-byte
+ * aligned, y 4-byte aligned. When K is split across CTAs (small n * m) y is zeroed first unless add.
+ */
+MQ_API size_t mq_gemm_q4_workspace_size(int64_t m, int64_t k, int x_dtype);
+MQ_API int mq_gemm_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y, int64_t n,
+                      int64_t k, int64_t m, int group, int add, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
  * Ternary GEMV: y[b][i] = sum_k s[k/128][i] * (code(k, i) - 1) * x[b][k], b < batch <= 4.

@@ -1,0 +1,376 @@
+// Prefill GEMM over int4 word-layout weights on the 5th-generation tensor cores (mq_gemm_q4).
+//
+// Replaces p_gemm_q4 (llama/kernels/prefill/p_gemm_q4.mojo:26-62) and gemm_q4 (lfm2/kernels/lk.mojo:
+// 458-495): Y[m][r] (+)= sum_k X[m][k] * W[r][k], W int4 with an fp16 scale per `group` weights of a
+// row, X fp16 [M][K], Y fp32 [M][N]. The reference stages X and the dequantised W slice in shared
+// memory and multiplies on fp32 cooperative matrices; here:
+//  * The MMA sees W as the A operand (M = 128 weight rows per CTA) and the tokens as B (N = BN, a
+//    multiple of 16 up to 256), so the accumulator tile in TMEM is [128 weight rows][BN tokens]
+//    and the epilogue writes Y rows with consecutive threads on consecutive addresses.
+//  * Warp 0 streams each 64-k stage with TMA: the packed weights (128 rows x 32 bytes) and the X
+//    tile (BN rows x 128 bytes, 128-byte swizzle, zero-filled past M).
+//  * Warps 2-5 (one thread per weight row) dequantise the stage in registers -- byte permute,
+//    mask into an fp16 mantissa (1024 + u), one fp16x2 FMA to q = u - 8 (exact), one fp16x2
+//    multiply by the group scale (a single rounding) -- and store the fp16 tile in the canonical
+//    K-major 128-byte-swizzle layout the MMA reads.
+//  * Warp 1 owns the TMEM accumulator and one of its threads issues tcgen05.mma kind::f16
+//    (fp16 x fp16 -> fp32, M = 128, N = BN, K = 16, four per stage), committing each stage back to
+//    the producer and the final one to the epilogue.
+//  * Warps 2-5 then move the accumulator out of TMEM (tcgen05.ld 32x32b, one weight row per
+//    thread) and store fp32 Y (+= with `add`, red.add when K is split across CTAs).
+//  * Numerics: the product uses fp16 X and fp16 q*s (one rounding each); accumulation is fp32.
+// Every wait on an mbarrier is bounded; on a time-out the kernel records a status code
+// (mq_device_status), stops issuing work, drains what is in flight and frees its TMEM.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace mq {
+namespace gemm {
+
+constexpr int kBM = 128;  // weight rows per CTA tile (the UMMA M)
+constexpr int kBK = 64;   // k per pipeline stage: one 128-byte fp16 row
+constexpr int kMaxStages = 6;
+constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 dequant + epilogue
+constexpr int kATileBytes = kBM * 128;
+constexpr int kWTileBytes = kBM * 32;
+
+struct Params {
+  const __half *ws;
+  float *y;
+  int n, k, m;
+  int bn;        // tokens per tile (multiple of 16, <= 256)
+  int stages;    // pipeline depth (<= kMaxStages)
+  int add;       // y += instead of y =
+  int splitk;    // CTAs along K (red.add into y)
+  int kb_split;  // 64-k blocks per split (a multiple of 4)
+  int tiles_n, tiles_m;
+  uint32_t tmem_cols;
+};
+
+struct Layout {
+  uint32_t a, x, w, bars, tmem_slot, total;
+};
+
+__host__ __device__ inline Layout layout(int bn, int stages) {
+  Layout L;
+  L.a = 0;
+  L.x = L.a + stages * kATileBytes;
+  L.w = L.x + stages * bn * 128;
+  L.bars = L.w + stages * kWTileBytes;
+  L.tmem_slot = L.bars + (3 * kMaxStages + 1) * 8;
+  L.total = L.tmem_slot + 16;
+  return L;
+}
+
+// fp16 (q - 8) * s for the 8 nibbles of a word, in k order, as 4 half2 (16 bytes).
+__device__ __forceinline__ uint4 dequant_word(uint32_t w, __half2 s2) {
+  const __half2 mul = __halves2half2(__float2half_rn(1.f), __float2half_rn(0.0625f));
+  const __half2 off = __halves2half2(__float2half_rn(-1032.f), __float2half_rn(-72.f));
+  uint32_t out[4];
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    // byte b = nibbles 2b (low) and 2b + 1 (high), copied to both halves of the word
+    const uint32_t t = __byte_perm(w, 0u, 0x4040u | b | (b << 8));
+    // low half: 0x6400 | (nib ^ 8) = 1024 + u; high half: 0x6400 | (nib ^ 8) << 4 = 1024 + 16u
+    const uint32_t h = (t & 0x00F0000Fu) ^ 0x64806408u;
+    __half2 f = __hfma2(*reinterpret_cast<const __half2 *>(&h), mul, off);  // (u - 8, u' - 8), exact
+    f = __hmul2(f, s2);
+    out[b] = *reinterpret_cast<uint32_t *>(&f);
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+template <int G>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_q4_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const Layout L = layout(p.bn, p.stages);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);
+  uint64_t *deq = full + kMaxStages;
+  uint64_t *empty = deq + kMaxStages;
+  uint64_t *accum = empty + kMaxStages;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem_slot);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.tmem_slot + 8);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int S = p.stages;
+
+  // Tile: token tiles fastest, so consecutive CTAs share (and L2-reuse) a weight tile.
+  const int t = blockIdx.x;
+  const int tm = t % p.tiles_m, tn = (t / p.tiles_m) % p.tiles_n, split = t / (p.tiles_m * p.tiles_n);
+  const int n0 = tn * kBM, m0 = tm * p.bn;
+  const int nkb_total = p.k / kBK;
+  const int kb0 = split * p.kb_split, nk = min(p.kb_split, nkb_total - kb0);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(deq + i, 128);
+      mbar_init(empty + i, 1);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, p.tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_d = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------------------------------------------------
+    if (lane == 0) {
+      prefetch_tmap(&wmap);
+      prefetch_tmap(&xmap);
+      const uint32_t bytes = kWTileBytes + p.bn * 128;
+      int issued = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % S;
+        if (i >= S && !*abort_flag && !mbar_wait(&empty[s], ((i / S) - 1) & 1)) {
+          raise_status(kStatusGemmTmaWait);
+          *abort_flag = 1;
+        }
+        if (*abort_flag) break;
+        mbar_expect_tx(&full[s], bytes);
+        tma_load_2d(smem + L.w + s * kWTileBytes, &wmap, &full[s], (kb0 + i) * (kBK / 8), n0);
+        tma_load_2d(smem + L.x + s * p.bn * 128, &xmap, &full[s], (kb0 + i) * kBK, m0);
+        issued = i + 1;
+      }
+      // Leave no copy in flight: wait (bounded) for the last load issued into each stage.
+      for (int i = max(0, issued - S); i < issued; ++i) mbar_wait(&full[i % S], (i / S) & 1);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer -------------------------------------------------------------
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(kBM, p.bn);
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % S;
+        if (!*abort_flag && (!mbar_wait(&full[s], (i / S) & 1) || !mbar_wait(&deq[s], (i / S) & 1))) {
+          raise_status(kStatusGemmMmaWait);
+          *abort_flag = 1;
+        }
+        if (*abort_flag) break;
+        tc_fence_after();
+        const uint64_t da = umma_desc_sw128(smem_u32(smem + L.a + s * kATileBytes));
+        const uint64_t db = umma_desc_sw128(smem_u32(smem + L.x + s * p.bn * 128));
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)  // +32 bytes along K = +2 in the descriptor's address field
+          umma_f16(tmem_d, da + 2 * kk, db + 2 * kk, idesc, (i | kk) != 0);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accum);  // also after an abort: it lands once the issued MMAs are done
+    }
+  } else {
+    // ---------------- dequant (one weight row per thread), then the epilogue ----------------
+    const int quarter = warp & 3;  // the TMEM lanes this warp may read: 32 * quarter ..
+    const int row = quarter * 32 + lane;
+    const int grow = min(n0 + row, p.n - 1);  // rows past N are zero-filled by TMA; their scale is unused
+    const int spr = p.k / G;
+    // Scales: 4 stages (256 k) per vector load, prefetched one quad of stages ahead.
+    constexpr int kHalvesPerQuad = 4 * kBK / G;  // 8, 4 or 2
+    auto load_scales = [&](int quad, uint32_t (&dst)[4]) {
+      const int kb = kb0 + 4 * quad;
+      const __half *src = p.ws + static_cast<size_t>(grow) * spr + kb * kBK / G;
+      dst[0] = dst[1] = dst[2] = dst[3] = 0u;
+      if (4 * quad >= nk) return;
+      if (kHalvesPerQuad == 8) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src));
+        dst[0] = v.x, dst[1] = v.y, dst[2] = v.z, dst[3] = v.w;
+      } else if (kHalvesPerQuad == 4) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2 *>(src));
+        dst[0] = v.x, dst[1] = v.y;
+      } else {
+        dst[0] = __ldg(reinterpret_cast<const unsigned int *>(src));
+      }
+    };
+    uint32_t cur[4], nxt[4];
+    load_scales(0, cur);
+    const uint32_t xr = row & 7;
+    uint8_t *a_row = smem + L.a + row * 128;
+    for (int q4 = 0; q4 * 4 < nk; ++q4) {
+      load_scales(q4 + 1, nxt);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = 4 * q4 + u;
+        if (i >= nk) break;
+        const int s = i % S;
+        if (!*abort_flag && !mbar_wait(&full[s], (i / S) & 1)) {
+          raise_status(kStatusGemmDeqWait);
+          *abort_flag = 1;
+        }
+        if (!*abort_flag) {
+          // the stage's scale(s) for this row, as a half2 of (s, s) per 32-k half of the stage
+          __half2 s_lo, s_hi;
+          if (G == 32) {
+            const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[u]);
+            s_lo = __low2half2(pair);
+            s_hi = __high2half2(pair);
+          } else if (G == 64) {
+            const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[u >> 1]);
+            s_lo = s_hi = (u & 1) ? __high2half2(pair) : __low2half2(pair);
+          } else {
+            const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[0]);
+            s_lo = s_hi = (u >> 1) ? __high2half2(pair) : __low2half2(pair);
+          }
+          const uint4 *wp = reinterpret_cast<const uint4 *>(smem + L.w + s * kWTileBytes + row * 32);
+          const uint4 w0 = wp[0], w1 = wp[1];
+          const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          uint8_t *a = a_row + s * kATileBytes;
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4 *>(a + ((c ^ xr) << 4)) = dequant_word(wv[c], c < 4 ? s_lo : s_hi);
+          fence_proxy_async_smem();
+        }
+        mbar_arrive(&deq[s]);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
+    }
+
+    // Epilogue: TMEM -> registers -> Y.
+    bool ok = !*abort_flag;
+    if (!mbar_wait(accum, 0)) {
+      raise_status(kStatusGemmEpiWait);
+      ok = false;
+    }
+    tc_fence_after();
+    if (ok && !*abort_flag && nk > 0) {
+      const uint32_t taddr = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16);
+      const int r = n0 + row;
+      for (int c0 = 0; c0 < p.bn; c0 += 32) {
+        float v[32];
+        tmem_ld32(taddr + c0, v);
+        if (r < p.n) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int tok = m0 + c0 + j;
+            if (c0 + j < p.bn && tok < p.m) {
+              float *out = p.y + static_cast<size_t>(tok) * p.n + r;
+              if (p.splitk > 1)
+                atomicAdd(out, v[j]);
+              else
+                *out = p.add ? *out + v[j] : v[j];
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_d, p.tmem_cols);
+  }
+}
+
+__global__ void f32_to_f16_kernel(const float4 *__restrict__ x, uint2 *__restrict__ out, int64_t n4) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float4 v = x[i];
+    out[i] = make_uint2(pack_half2(v.x, v.y), pack_half2(v.z, v.w));
+  }
+}
+
+template <int G>
+int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream, const DeviceInfo &dev) {
+  // Tiles: tokens split as evenly as possible into <= 256-wide tiles of a multiple of 16.
+  p.tiles_m = (p.m + 255) / 256;
+  p.bn = ((p.m + p.tiles_m - 1) / p.tiles_m + 15) / 16 * 16;
+  p.tiles_n = (p.n + kBM - 1) / kBM;
+  p.tmem_cols = 32;
+  while (p.tmem_cols < static_cast<uint32_t>(p.bn)) p.tmem_cols *= 2;
+  // Split K (in quads of 64-k blocks) while the grid leaves SMs idle.
+  const int nkb = p.k / kBK, quads = nkb / 4;
+  const int tiles = p.tiles_m * p.tiles_n;
+  int splitk = 1;
+  while (splitk * 2 <= quads && tiles * splitk * 2 <= dev.sms) splitk *= 2;
+  if (splitk == 1 && tiles < dev.sms / 2 && quads >= 3 && tiles * 3 <= dev.sms) splitk = 3;
+  p.kb_split = ((quads + splitk - 1) / splitk) * 4;
+  p.splitk = (nkb + p.kb_split - 1) / p.kb_split;
+  // Pipeline depth: as many stages as shared memory holds.
+  Layout L{};
+  for (p.stages = kMaxStages; p.stages >= 2; --p.stages) {
+    L = layout(p.bn, p.stages);
+    if (L.total + 1024 <= dev.smem_optin) break;
+  }
+  const size_t smem = L.total + 1024;
+  MQ_REQUIRE(smem <= dev.smem_optin, MQ_EUNSUPPORTED, "mq_gemm_q4: tile of %d tokens needs %zu B of shared memory", p.bn,
+             smem);
+  CUtensorMap wmap, xmap;
+  if (int rc = encode_tmap_2d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.k / 8, p.n, static_cast<uint64_t>(p.k) / 2,
+                              kBK / 8, kBM, CU_TENSOR_MAP_SWIZZLE_NONE, "mq_gemm_q4 weights"))
+    return rc;
+  if (int rc = encode_tmap_2d(&xmap, x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k, p.m, static_cast<uint64_t>(p.k) * 2, kBK,
+                              p.bn, CU_TENSOR_MAP_SWIZZLE_128B, "mq_gemm_q4 activations"))
+    return rc;
+  if (p.splitk > 1 && !p.add) {
+    cudaError_t e = cudaMemsetAsync(p.y, 0, static_cast<size_t>(p.m) * p.n * sizeof(float), stream);
+    if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_gemm_q4: zeroing y: %s", cudaGetErrorString(e));
+  }
+  auto kern = gemm_q4_kernel<G>;
+  static size_t configured = 0;
+  if (smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_gemm_q4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured = smem;
+  }
+  kern<<<tiles * p.splitk, kThreads, smem, stream>>>(wmap, xmap, p);
+  return check_launch("mq_gemm_q4");
+}
+
+}  // namespace gemm
+
+// Shared by mq_gemm_q4 and the batched decode path of mq_gemv_q4.
+int gemm_q4_run(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y, int64_t n, int64_t k,
+                int64_t m, int group, int add, void *workspace, size_t workspace_bytes, cudaStream_t stream) {
+  DeviceInfo dev;
+  if (int rc = device_info(&dev)) return rc;
+  const __half *x16 = static_cast<const __half *>(x);
+  if (x_dtype == MQ_F32) {
+    const size_t need = static_cast<size_t>(m) * k * 2;
+    MQ_REQUIRE(workspace && workspace_bytes >= need, MQ_EINVAL,
+               "mq_gemm_q4: fp32 activations need a workspace of %zu bytes (got %zu)", need, workspace_bytes);
+    MQ_REQUIRE(aligned(workspace, 16), MQ_EALIGN, "mq_gemm_q4: workspace must be 16-byte aligned");
+    const int64_t n4 = m * k / 4;
+    const int grid = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(dev.sms) * 8));
+    gemm::f32_to_f16_kernel<<<grid, 256, 0, stream>>>(static_cast<const float4 *>(x), static_cast<uint2 *>(workspace), n4);
+    if (int rc = check_launch("mq_gemm_q4 (fp32 -> fp16)")) return rc;
+    x16 = static_cast<const __half *>(workspace);
+  }
+  gemm::Params p{};
+  p.ws = reinterpret_cast<const __half *>(ws);
+  p.y = y;
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.m = static_cast<int>(m);
+  p.add = add != 0;
+  switch (group) {
+    case 32: return gemm::launch<32>(wq, x16, p, stream, dev);
+    case 64: return gemm::launch<64>(wq, x16, p, stream, dev);
+    default: return gemm::launch<128>(wq, x16, p, stream, dev);
+  }
+}
+
+}  // namespace mq
+
+extern "C" size_t mq_gemm_q4_workspace_size(int64_t m, int64_t k, int x_dtype) {
+  return x_dtype == MQ_F32 && m > 0 && k > 0 ? static_cast<size_t>(m) * k * 2 : 0;
+}
+
+extern "C" int mq_gemm_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y, int64_t n,
+                          int64_t k, int64_t m, int group, int add, void *workspace, size_t workspace_bytes, void *stream) {
+  MQ_REQUIRE(wq && ws && x && y, MQ_EINVAL, "mq_gemm_q4: null pointer");
+  MQ_REQUIRE(n > 0 && k > 0 && m > 0 && n < (1LL << 31) && k <= (1 << 20) && m < (1LL << 24), MQ_EINVAL,
+             "mq_gemm_q4: bad shape n=%lld k=%lld m=%lld", static_cast<long long>(n), static_cast<long long>(k),
+             static_cast<long long>(m));
+  MQ_REQUIRE(group == 32 || group == 64 || group == 128, MQ_EINVAL, "mq_gemm_q4: group must be 32, 64 or 128 (got %d)", group);
+  MQ_REQUIRE(k % 256 == 0, MQ_EINVAL, "mq_gemm_q4: k=%lld must be a multiple of 256", static_cast<long long>(k));
+  MQ_REQUIRE(x_dtype == MQ_F32 || x_dtype == MQ_F16, MQ_EINVAL, "mq_gemm_q4: x_dtype must be MQ_F32 or MQ_F16");
+  MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(ws, 16) && mq::aligned(x, 16) && mq::aligned(y, 4), MQ_EALIGN,
+             "mq_gemm_q4: wq, ws and x must be 16-byte aligned, y 4-byte aligned");
+  return mq::gemm_q4_run(wq, ws, x, x_dtype, y, n, k, m, group, add, workspace, workspace_bytes,
+                         static_cast<cudaStream_t>(stream));
+}

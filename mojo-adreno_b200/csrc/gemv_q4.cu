@@ -464,6 +464,12 @@ extern "C" int mq_gemv_q4(const uint32_t *wq, const uint16_t *ws, const void *x,
   MQ_REQUIRE(batch >= 1 && batch <= 64, MQ_EINVAL, "mq_gemv_q4: batch must be in 1..64 (got %d)", batch);
   MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(ws, 2) && mq::aligned(x, 16) && mq::aligned(y, 4), MQ_EALIGN,
              "mq_gemv_q4: wq and x must be 16-byte aligned, y 4-byte aligned");
-  if (batch > 4) return mq::fail(MQ_EUNSUPPORTED, "mq_gemv_q4: batch > 4 needs the tensor-core GEMM path");
+  if (batch > 4) {  // the tensor-core GEMM with the batch as its token dimension
+    MQ_REQUIRE(x_dtype == MQ_F16, MQ_EUNSUPPORTED,
+               "mq_gemv_q4: batch > 4 runs the tensor-core GEMM, which takes fp32 x only through mq_gemm_q4's workspace");
+    MQ_REQUIRE(k % 256 == 0 && mq::aligned(ws, 16), MQ_EINVAL,
+               "mq_gemv_q4: batch > 4 needs k %% 256 == 0 and 16-byte aligned scales");
+    return mq::gemm_q4_run(wq, ws, x, x_dtype, y, n, k, batch, group, add, nullptr, 0, static_cast<cudaStream_t>(stream));
+  }
   return mq::gemv::gemv_q4_small(wq, ws, x, x_dtype, y, n, k, group, batch, add, static_cast<cudaStream_t>(stream));
 }

@@ -6,3 +6,4 @@
 #include "unpack.cu"
 #include "gemv_q4.cu"
 #include "tgemv.cu"
+#include "gemm_q4.cu"

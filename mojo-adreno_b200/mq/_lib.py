@@ -5,7 +5,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 library_path = os.path.join(_HERE, "libmq.so")
 
-c_int, c_i64, c_vp, c_char_p = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_char_p
+c_int, c_i64, c_vp, c_char_p, c_size = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t
 
 # name -> (restype, argtypes), in include/mq.h order.
 SIGNATURES = {
@@ -14,6 +14,8 @@ SIGNATURES = {
     "mq_device_status": (c_int, [c_int, c_vp]),
     "mq_unpack_q4": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_vp]),
     "mq_gemv_q4": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_int, c_int, c_int, c_vp]),
+    "mq_gemm_q4_workspace_size": (c_size, [c_i64, c_i64, c_int]),
+    "mq_gemm_q4": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_int, c_int, c_vp, c_size, c_vp]),
     "mq_tgemv": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_vp]),
 }
 

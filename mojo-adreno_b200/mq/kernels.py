@@ -13,7 +13,7 @@ from ._lib import MQError, lib
 
 MQ_F32, MQ_F16 = 0, 1
 
-__all__ = ["MQ_F32", "MQ_F16", "MQError", "gemv_q4", "gemv_add_q4", "unpack_q4", "project", "device_status"]
+__all__ = ["MQ_F32", "MQ_F16", "MQError", "gemv_q4", "gemv_add_q4", "p_gemm_q4", "unpack_q4", "project", "device_status"]
 
 
 def _stream():
@@ -56,8 +56,33 @@ def gemv_q4(wq, ws, x, y, cols, group=64, add=False):
     if batch * cols != x.numel():
         raise MQError(-1, f"x: {x.numel()} elements is not a whole number of rows of {cols}")
     _need(y, "y", (torch.float32,), batch * rows)
+    if batch > 4 and x.dtype == torch.float32:  # the tensor-core path takes fp32 x through a workspace
+        return p_gemm_q4(wq, ws, x, y, rows, cols, batch, group=group, add=add)
     lib.call("mq_gemv_q4", _p(wq), _p(ws), _p(x), MQ_F16 if x.dtype == torch.float16 else MQ_F32, _p(y),
              rows, cols, group, batch, int(bool(add)), _stream())
+    return y
+
+
+def p_gemm_q4(wq, ws, x, y, n, k, rows=None, group=64, add=False):
+    """Y[t, r] (+)= sum_c W[r, c] X[t, c] on the tcgen05 tensor cores: p_gemm_q4(wq, ws, x, y, n, k) of
+    llama/kernels/prefill/p_gemm_q4.mojo:26-62 (there X's rows are padded to 128; here `rows` is the
+    true token count, default x's). wq: int32/uint32 [n, k/8]; ws: fp16 [n, k/group]; x: fp16 or fp32
+    [rows, k]; y: fp32 [rows, n]."""
+    _need(wq, "wq", _WORDS, n * k // 8)
+    _need(ws, "ws", (torch.float16,), n * k // group)
+    _need(x, "x", (torch.float32, torch.float16))
+    if rows is None:
+        rows = x.numel() // k
+    if x.numel() < rows * k:
+        raise MQError(-1, f"x: {x.numel()} elements < rows * k = {rows * k}")
+    _need(y, "y", (torch.float32,))
+    if y.numel() < rows * n:
+        raise MQError(-1, f"y: {y.numel()} elements < rows * n = {rows * n}")
+    dt = MQ_F16 if x.dtype == torch.float16 else MQ_F32
+    nbytes = lib.mq_gemm_q4_workspace_size(rows, k, dt)
+    work = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=x.device) if nbytes else None
+    lib.call("mq_gemm_q4", _p(wq), _p(ws), _p(x), dt, _p(y), n, k, rows, group, int(bool(add)),
+             _p(work) if work is not None else None, nbytes, _stream())
     return y
 
 
