@@ -253,7 +253,42 @@ def run_mq(args):
         tern[name] = {"shape": [n, k], "ms": round(tms, 5), "GB/s": round(tbytes / (tms * 1e-3) / 1e9, 1)}
         del tws, tss
 
-    hbm, _, peak_src = peaks()
+    # ---- secondary: int4 prefill GEMM, Llama-3.2-1B shapes, 431 tokens -----
+    hbm, tflops_peak, peak_src = peaks()
+    prefill = {}
+    psyn = synth.prefill(seed=0)
+    for name, n, k in synth.LLAMA_PREFILL:
+        x, wq, ws = psyn[name]
+        lo, hi = shard(n, world, rank)
+        px = torch.from_numpy(x).to(dev)
+        pw = torch.from_numpy(np.ascontiguousarray(wq[lo:hi]).view(np.int32)).to(dev)
+        ps = torch.from_numpy(np.ascontiguousarray(ws[lo:hi])).to(dev)
+        py = torch.empty(x.shape[0], hi - lo, device=dev)
+        gp = graph_of(lambda: [mq.p_gemm_q4(pw, ps, px, py, hi - lo, k, x.shape[0], group=GROUP) for _ in range(10)])
+        pms = max_over_ranks(time_graphs([gp], 10, stream) / 10, world)
+        flops = 2.0 * x.shape[0] * n * k
+        prefill[name] = {"shape": [n, k], "tokens": x.shape[0], "ms": round(pms, 5),
+                         "TFLOP/s": round(flops / (pms * 1e-3) / 1e12, 1),
+                         "frac_of_measured_bf16_peak": round(flops / (pms * 1e-3) / 1e12 / tflops_peak, 4)}
+        del gp
+
+    # ---- secondary: the decode layer at batch 64 through the tensor-core path
+    b64 = synth.llama_layer(batch=64, seed=0)
+    b64_graphs = []
+    b64_bufs = []
+    for m_ in mats:
+        x64 = torch.from_numpy(b64[m_["name"]][0]).to(dev).half()
+        y64 = torch.empty(64, m_["n"], device=dev)
+        b64_bufs.append((x64, y64))
+    for c in range(copies):
+        b64_graphs.append(graph_of(lambda c=c: [mq.gemv_q4(m_["wqs"][c], m_["wss"][c], xb, yb, m_["k"], group=GROUP)
+                                                for m_, (xb, yb) in zip(mats, b64_bufs)]))
+    b64_ms = max_over_ranks(time_graphs(b64_graphs, 50, stream), world)
+    b64_bytes = sum(q4_bytes(n, k, 64) for _, n, k in synth.LLAMA_LAYER)
+    decode64 = {"ms_per_step": round(b64_ms, 5), "GB/s": round(b64_bytes / (b64_ms * 1e-3) / 1e9, 1),
+                "x": "fp16 [64, k] per matrix", "path": "tcgen05 GEMM (batch > 4)"}
+    del b64_graphs
+
     head_bytes = q4_bytes(head["n"], head["k"], batch) * (world if world > 1 else 1)
     achieved = q4_bytes(head["n"], head["k"], batch) / (head_ms * 1e-3) / 1e9
     traffic = None
@@ -281,12 +316,14 @@ def run_mq(args):
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "note": "mq.gemv_q4 python API call per matrix (no graph); x from pinned host and lm_head logits "
                             "to host every step"},
-            "roofline": {"bound": "hbm", "kernel": "gemv_q4_kernel<32,1,true,1024> (lm_head shard)",
+            "roofline": {"bound": "hbm", "kernel": "gemv_q4_kernel<32,1,true> (lm_head shard)",
                          "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "traffic": traffic, "algorithmic_bytes_per_launch": q4_bytes(head["n"], head["k"], batch),
                          "peak_source": peak_src, "launch_ms": round(head_ms, 5)},
             "per_matrix_ms": per_matrix,
             "ternary_gemv": tern,
+            "prefill_gemm": prefill,
+            "decode_batch64": decode64,
             "gpu_launches": args.steps * len(mats),
             "clocks": clocks,
         }
@@ -378,6 +415,46 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def profile_case(name, launches):
+    """A few launches of one kernel on one workload, for ncu captures (no timing, no JSON line).
+    Cases: gemv_lm_head (configs[1] head, batch 1), tgemv_head (configs[4] head), gemm_gate_up
+    (configs[2] 8192x2048, 431 tokens), gemm_decode64_head (configs[1] head, batch 64)."""
+    import mq
+    from mq import synth
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    if name in ("gemv_lm_head", "gemm_decode64_head"):
+        batch = 1 if name == "gemv_lm_head" else 64
+        x, wq, ws = synth.llama_layer(batch=batch, seed=0)["lm_head"]
+        tw = torch.from_numpy(wq.view(np.int32)).to(dev)
+        ts = torch.from_numpy(ws).to(dev)
+        tx = torch.from_numpy(x).to(dev)
+        if batch > 4:
+            tx = tx.half()
+        ty = torch.empty(batch, wq.shape[0], device=dev)
+        for _ in range(launches):
+            mq.gemv_q4(tw, ts, tx, ty, 2048, group=GROUP)
+    elif name == "tgemv_head":
+        x, w, s = synth.ternary(seed=0, which=("head",))["head"]
+        n, k = w.shape[1], w.shape[0] * 16
+        tx, tw, ts = (torch.from_numpy(a).to(dev) for a in (x, w.view(np.int32), s))
+        ty = torch.empty(1, n, device=dev)
+        for _ in range(launches):
+            mq.project(tx, tw, ts, ty, n, k)
+    elif name == "gemm_gate_up":
+        x, wq, ws = synth.prefill(seed=0)["gate_up"]
+        tw = torch.from_numpy(wq.view(np.int32)).to(dev)
+        ts, tx = torch.from_numpy(ws).to(dev), torch.from_numpy(x).to(dev)
+        ty = torch.empty(x.shape[0], wq.shape[0], device=dev)
+        for _ in range(launches):
+            mq.p_gemm_q4(tw, ts, tx, ty, wq.shape[0], 2048, x.shape[0], group=GROUP)
+    else:
+        raise SystemExit(f"unknown profile case {name}")
+    torch.cuda.synchronize()
+    assert mq.device_status() == 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -386,7 +463,12 @@ def main():
     ap.add_argument("--impl", choices=["mq", "reference"], default="mq")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--profile-case", default=None, help="run a few launches of one kernel for ncu and exit")
+    ap.add_argument("--launches", type=int, default=3)
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case, args.launches)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -9,15 +9,18 @@
 //    and the epilogue writes Y rows with consecutive threads on consecutive addresses.
 //  * Warp 0 streams each 64-k stage with TMA: the packed weights (128 rows x 32 bytes) and the X
 //    tile (BN rows x 128 bytes, 128-byte swizzle, zero-filled past M).
-//  * Warps 2-5 (one thread per weight row) dequantise the stage in registers -- byte permute,
+//  * Warps 2-9 (two threads per weight row, 32 k each) dequantise the stage in registers -- byte permute,
 //    mask into an fp16 mantissa (1024 + u), one fp16x2 FMA to q = u - 8 (exact), one fp16x2
 //    multiply by the group scale (a single rounding) -- and store the fp16 tile in the canonical
 //    K-major 128-byte-swizzle layout the MMA reads.
 //  * Warp 1 owns the TMEM accumulator and one of its threads issues tcgen05.mma kind::f16
 //    (fp16 x fp16 -> fp32, M = 128, N = BN, K = 16, four per stage), committing each stage back to
 //    the producer and the final one to the epilogue.
-//  * Warps 2-5 then move the accumulator out of TMEM (tcgen05.ld 32x32b, one weight row per
-//    thread) and store fp32 Y (+= with `add`, red.add when K is split across CTAs).
+//  * Warps 2-9 then move the accumulator out of TMEM (tcgen05.ld 32x32b, one weight row per
+//    thread, the two warps of a TMEM lane quarter taking alternate 32-column chunks) and store fp32 Y
+//    (+= with `add`, red.add when K is split across CTAs).
+//  * Each CTA starts its K loop at its own 256-k offset (rotating through K): CTAs that share a
+//    token tile then read different X tiles at any moment instead of all hitting the same L2 lines.
 //  * Numerics: the product uses fp16 X and fp16 q*s (one rounding each); accumulation is fp32.
 // Every wait on an mbarrier is bounded; on a time-out the kernel records a status code
 // (mq_device_status), stops issuing work, drains what is in flight and frees its TMEM.
@@ -31,7 +34,8 @@ namespace gemm {
 constexpr int kBM = 128;  // weight rows per CTA tile (the UMMA M)
 constexpr int kBK = 64;   // k per pipeline stage: one 128-byte fp16 row
 constexpr int kMaxStages = 6;
-constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 dequant + epilogue
+constexpr int kDeqWarps = 8;   // two per scheduler: one dequant warp alone cannot hide its latencies
+constexpr int kThreads = 32 * (2 + kDeqWarps);  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 dequant + epilogue
 constexpr int kATileBytes = kBM * 128;
 constexpr int kWTileBytes = kBM * 32;
 
@@ -65,8 +69,10 @@ __host__ __device__ inline Layout layout(int bn, int stages) {
 
 // fp16 (q - 8) * s for the 8 nibbles of a word, in k order, as 4 half2 (16 bytes).
 __device__ __forceinline__ uint4 dequant_word(uint32_t w, __half2 s2) {
-  const __half2 mul = __halves2half2(__float2half_rn(1.f), __float2half_rn(0.0625f));
-  const __half2 off = __halves2half2(__float2half_rn(-1032.f), __float2half_rn(-72.f));
+  constexpr uint32_t kMul = 0x2C003C00u;  // fp16x2 (1, 1/16)
+  constexpr uint32_t kOff = 0xD480E408u;  // fp16x2 (-1032, -72)
+  const __half2 mul = *reinterpret_cast<const __half2 *>(&kMul);
+  const __half2 off = *reinterpret_cast<const __half2 *>(&kOff);
   uint32_t out[4];
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
@@ -102,11 +108,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n0 = tn * kBM, m0 = tm * p.bn;
   const int nkb_total = p.k / kBK;
   const int kb0 = split * p.kb_split, nk = min(p.kb_split, nkb_total - kb0);
+  // Stage i works on k-block kb0 + (i + rot) % nk; rot is a whole number of 4-block quads.
+  const int rot = 4 * (tn % max(1, nk / 4));
+  auto kblock = [&](int i) { return kb0 + (i + rot) % nk; };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(full + i, 1);
-      mbar_init(deq + i, 128);
+      mbar_init(deq + i, 32 * kDeqWarps);
       mbar_init(empty + i, 1);
     }
     mbar_init(accum, 1);
@@ -134,8 +143,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (*abort_flag) break;
         mbar_expect_tx(&full[s], bytes);
-        tma_load_2d(smem + L.w + s * kWTileBytes, &wmap, &full[s], (kb0 + i) * (kBK / 8), n0);
-        tma_load_2d(smem + L.x + s * p.bn * 128, &xmap, &full[s], (kb0 + i) * kBK, m0);
+        tma_load_2d(smem + L.w + s * kWTileBytes, &wmap, &full[s], kblock(i) * (kBK / 8), n0);
+        tma_load_2d(smem + L.x + s * p.bn * 128, &xmap, &full[s], kblock(i) * kBK, m0);
         issued = i + 1;
       }
       // Leave no copy in flight: wait (bounded) for the last load issued into each stage.
@@ -163,18 +172,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(accum);  // also after an abort: it lands once the issued MMAs are done
     }
   } else {
-    // ---------------- dequant (one weight row per thread), then the epilogue ----------------
-    const int quarter = warp & 3;  // the TMEM lanes this warp may read: 32 * quarter ..
+    // ---------------- dequant (two threads per weight row), then the epilogue ----------------
+    const int quarter = warp & 3;          // the TMEM lanes this warp may read: 32 * quarter ..
+    const int half = (warp - 2) >> 2;      // which 32 k of each stage (and which column chunks) it owns
     const int row = quarter * 32 + lane;
     const int grow = min(n0 + row, p.n - 1);  // rows past N are zero-filled by TMA; their scale is unused
     const int spr = p.k / G;
     // Scales: 4 stages (256 k) per vector load, prefetched one quad of stages ahead.
     constexpr int kHalvesPerQuad = 4 * kBK / G;  // 8, 4 or 2
     auto load_scales = [&](int quad, uint32_t (&dst)[4]) {
-      const int kb = kb0 + 4 * quad;
-      const __half *src = p.ws + static_cast<size_t>(grow) * spr + kb * kBK / G;
       dst[0] = dst[1] = dst[2] = dst[3] = 0u;
       if (4 * quad >= nk) return;
+      const int kb = kblock(4 * quad);
+      const __half *src = p.ws + static_cast<size_t>(grow) * spr + kb * kBK / G;
       if (kHalvesPerQuad == 8) {
         const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src));
         dst[0] = v.x, dst[1] = v.y, dst[2] = v.z, dst[3] = v.w;
@@ -201,26 +211,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           *abort_flag = 1;
         }
         if (!*abort_flag) {
-          // the stage's scale(s) for this row, as a half2 of (s, s) per 32-k half of the stage
-          __half2 s_lo, s_hi;
+          // this thread's 32 k of the stage share one group for G >= 32: (s, s) as half2
+          __half2 s2;
           if (G == 32) {
             const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[u]);
-            s_lo = __low2half2(pair);
-            s_hi = __high2half2(pair);
+            s2 = half ? __high2half2(pair) : __low2half2(pair);
           } else if (G == 64) {
             const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[u >> 1]);
-            s_lo = s_hi = (u & 1) ? __high2half2(pair) : __low2half2(pair);
+            s2 = (u & 1) ? __high2half2(pair) : __low2half2(pair);
           } else {
             const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[0]);
-            s_lo = s_hi = (u >> 1) ? __high2half2(pair) : __low2half2(pair);
+            s2 = (u >> 1) ? __high2half2(pair) : __low2half2(pair);
           }
-          const uint4 *wp = reinterpret_cast<const uint4 *>(smem + L.w + s * kWTileBytes + row * 32);
-          const uint4 w0 = wp[0], w1 = wp[1];
-          const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          const uint4 w = *reinterpret_cast<const uint4 *>(smem + L.w + s * kWTileBytes + row * 32 + half * 16);
+          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
           uint8_t *a = a_row + s * kATileBytes;
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<uint4 *>(a + ((c ^ xr) << 4)) = dequant_word(wv[c], c < 4 ? s_lo : s_hi);
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4 *>(a + (((4 * half + c) ^ xr) << 4)) = dequant_word(wv[c], s2);
           fence_proxy_async_smem();
         }
         mbar_arrive(&deq[s]);
@@ -239,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && !*abort_flag && nk > 0) {
       const uint32_t taddr = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16);
       const int r = n0 + row;
-      for (int c0 = 0; c0 < p.bn; c0 += 32) {
+      for (int c0 = 32 * half; c0 < p.bn; c0 += 64) {
         float v[32];
         tmem_ld32(taddr + c0, v);
         if (r < p.n) {
