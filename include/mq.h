@@ -108,6 +108,57 @@ MQ_API int mq_gemm_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int
 MQ_API int mq_tgemv(const uint16_t *x, const uint32_t *w, const uint16_t *s, float *y, int64_t n, int64_t k,
              int batch, void *stream);
 
+/* ---- top-k MoE on int4 experts (Qwen3-MoE layout) ------------------------------------------------
+ * Expert weights are one word-layout matrix each: gate|up [experts * 2fe][d/8] (expert e's gate rows
+ * e*2fe .. e*2fe+fe-1, its up rows the next fe; qwen3moe/export.py:166-169) and down [experts * d][fe/8],
+ * with fp16 scales per `group` weights of a row. */
+
+/* ids[t][k], weights[t][k]: the top-k experts of each token (the lowest index among equal logits)
+ * and softmax over the k chosen logits. Replaces route / p_route (qwen3moe/kernels/moek.mojo:156-197,
+ * 385-425). logits: [tokens][experts] fp32, experts <= 256, topk <= 32. */
+MQ_API int mq_moe_route(const float *logits, int32_t *ids, float *weights, int64_t tokens, int experts, int topk,
+                        void *stream);
+
+/* Stable grouping of the tokens * topk (token, slot) pairs by expert. Replaces p_expert_lists and
+ * p_expert_items (moek.mojo:432-442, 548-557): counts[e]; offsets[e] (exclusive prefix, offsets[experts]
+ * = pairs); order[offsets[e] + r] = the r-th pair t * topk + k routed to e, in increasing pair index;
+ * slot_of[pair] = its position in order; tiles[3 * i ..] = (expert, first sorted row, rows <= tile)
+ * work items in expert order and *ntiles their count (at most experts + ceil(pairs / tile)). */
+MQ_API int mq_moe_group(const int32_t *ids, int64_t tokens, int topk, int experts, int tile, int32_t *counts,
+                        int32_t *offsets, int32_t *order, int32_t *slot_of, int32_t *tiles, int32_t *ntiles,
+                        void *stream);
+
+/* xg[s] = fp16(x[order[s] / topk]) for s < pairs: the expert-sorted activation rows (p_gather,
+ * lfm2moe/kernels/mk.mojo:164-176). x: [tokens][d] fp32 or fp16; d % 8 == 0. */
+MQ_API int mq_moe_gather(const void *x, int x_dtype, const int32_t *order, int64_t pairs, int topk, int64_t d,
+                         uint16_t *xg, void *stream);
+
+/* Grouped expert product on the tcgen05 tensor cores over the work tiles of mq_moe_group (tile_m rows
+ * per tile, grid sized for max_tiles). mode 1: gate|up with the SwiGLU fused, out = fp16 a[pairs][fe]
+ * with a = silu(gate . x) * (up . x), rows_per_expert = 2fe (t_moe_gate_up, moek.mojo:560-583);
+ * mode 2: out = fp32 z[pairs][rows_per_expert] (t_moe_down, moek.mojo:586-608). xs: expert-sorted fp16
+ * rows [pairs][k]. k % 256 == 0, rows_per_expert % 128 == 0, tile_m % 16 == 0 (<= 128 for mode 1). */
+MQ_API int mq_moe_gemm_q4(int mode, const uint32_t *wq, const uint16_t *ws, const uint16_t *xs, int64_t pairs,
+                          int64_t k, int experts, int64_t rows_per_expert, int group, const int32_t *tiles,
+                          const int32_t *ntiles, int max_tiles, int tile_m, void *out, void *stream);
+
+/* a[r][j] = silu(h[r][j]) * h[r][fe + j] in fp32 (moe_gate_up's SwiGLU, moek.mojo:200-210). */
+MQ_API int mq_moe_silu_mul(const float *h, float *a, int64_t rows, int64_t fe, void *stream);
+
+/* y[t][c] (+)= sum_k weights[t][k] * z[slot_of[t * topk + k]][c], k in order (p_moe_sum,
+ * moek.mojo:479-488); slot_of NULL means row t * topk + k. z, y 16-byte aligned, d % 4 == 0. */
+MQ_API int mq_moe_combine(const float *z, const int32_t *slot_of, const float *weights, int64_t tokens, int topk,
+                          int64_t d, int add, float *y, void *stream);
+
+/* The whole MoE layer for precomputed routing: y (+)= sum_k w[t][k] * down_e(silu(gate_e x_t) * up_e x_t).
+ * Runs group, gather, the two grouped products and the combine on `stream`, in a caller workspace of
+ * mq_moe_workspace_size() bytes (256-byte aligned). d % 256 == 0, fe % 256 == 0. */
+MQ_API size_t mq_moe_workspace_size(int64_t tokens, int experts, int topk, int64_t d, int64_t fe);
+MQ_API int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, const float *weights, const uint32_t *gu_wq,
+                          const uint16_t *gu_ws, const uint32_t *dn_wq, const uint16_t *dn_ws, float *y, int64_t tokens,
+                          int experts, int topk, int64_t d, int64_t fe, int group, int add, void *workspace,
+                          size_t workspace_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

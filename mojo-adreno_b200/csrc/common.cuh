@@ -29,6 +29,11 @@ struct DeviceInfo {
 };
 int device_info(DeviceInfo *out);
 
+// The grouped expert GEMM (gemm_q4.cu): mode 1 gate|up + SiLU (fp16 out), mode 2 plain (fp32 out).
+int moe_gemm_run(int mode, const uint32_t *wq, const uint16_t *ws, const uint16_t *xs, int64_t pairs, int64_t k,
+                 int experts, int64_t rows_per_expert, int group, const int32_t *tiles, const int32_t *ntiles,
+                 int max_tiles, int tile_m, void *out, cudaStream_t stream);
+
 // The tcgen05 GEMM (gemm_q4.cu), shared by mq_gemm_q4 and the batched path of mq_gemv_q4.
 int gemm_q4_run(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y, int64_t n, int64_t k,
                 int64_t m, int group, int add, void *workspace, size_t workspace_bytes, cudaStream_t stream);

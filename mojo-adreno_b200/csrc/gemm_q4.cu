@@ -39,9 +39,21 @@ constexpr int kThreads = 32 * (2 + kDeqWarps);  // warp 0 TMA, warp 1 MMA + TMEM
 constexpr int kATileBytes = kBM * 128;
 constexpr int kWTileBytes = kBM * 32;
 
+// MODE 0: dense Y = X W^T. MODE 1 (MoE gate|up): per expert e, rows e * 2fe + [0, fe) are gate and
+// + [fe, 2fe) up; a CTA takes 64 gate rows and the 64 matching up rows and writes
+// a = silu(gate) * up as fp16. MODE 2 (MoE down): per expert, a plain fp32 product. In MODE 1 and 2
+// the tokens are rows of an expert-sorted X and the CTA's (expert, first row, rows) comes from a
+// device tile table (mq_moe_group).
+enum { kDense = 0, kGateUp = 1, kGrouped = 2 };
+
 struct Params {
   const __half *ws;
   float *y;
+  __half *y16;            // MODE 1 output
+  const int32_t *tiles;   // MODE 1, 2: (expert, first row, rows) per work tile
+  const int32_t *ntiles;  // MODE 1, 2: number of work tiles (device)
+  int rows_per_expert;    // MODE 1, 2: weight rows per expert (2fe or d)
+  int n_out;              // MODE 1, 2: output columns per token (fe or d)
   int n, k, m;
   int bn;        // tokens per tile (multiple of 16, <= 256)
   int stages;    // pipeline depth (<= kMaxStages)
@@ -87,7 +99,7 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, __half2 s2) {
   return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
-template <int G>
+template <int G, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_q4_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -104,8 +116,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Tile: token tiles fastest, so consecutive CTAs share (and L2-reuse) a weight tile.
   const int t = blockIdx.x;
-  const int tm = t % p.tiles_m, tn = (t / p.tiles_m) % p.tiles_n, split = t / (p.tiles_m * p.tiles_n);
-  const int n0 = tn * kBM, m0 = tm * p.bn;
+  int tm = t % p.tiles_m, tn = (t / p.tiles_m) % p.tiles_n, split = t / (p.tiles_m * p.tiles_n);
+  int n0 = tn * kBM, m0 = tm * p.bn, mcount = p.m - m0, expert = 0;
+  if (MODE != kDense) {  // grouped: work tile from the device table
+    const int entry = t / p.tiles_n;
+    tn = t % p.tiles_n;
+    split = 0;
+    if (entry >= *p.ntiles) return;  // the grid is sized for the most tiles the routing can produce
+    expert = p.tiles[3 * entry];
+    m0 = p.tiles[3 * entry + 1];
+    mcount = p.tiles[3 * entry + 2];
+    n0 = expert * p.rows_per_expert + tn * (MODE == kGateUp ? kBM / 2 : kBM);
+  }
   const int nkb_total = p.k / kBK;
   const int kb0 = split * p.kb_split, nk = min(p.kb_split, nkb_total - kb0);
   // Stage i works on k-block kb0 + (i + rot) % nk; rot is a whole number of 4-block quads.
@@ -143,7 +165,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (*abort_flag) break;
         mbar_expect_tx(&full[s], bytes);
-        tma_load_2d(smem + L.w + s * kWTileBytes, &wmap, &full[s], kblock(i) * (kBK / 8), n0);
+        if (MODE == kGateUp) {  // 64 gate rows, then the 64 matching up rows
+          tma_load_2d(smem + L.w + s * kWTileBytes, &wmap, &full[s], kblock(i) * (kBK / 8), n0);
+          tma_load_2d(smem + L.w + s * kWTileBytes + kWTileBytes / 2, &wmap, &full[s], kblock(i) * (kBK / 8),
+                      n0 + p.rows_per_expert / 2);
+        } else {
+          tma_load_2d(smem + L.w + s * kWTileBytes, &wmap, &full[s], kblock(i) * (kBK / 8), n0);
+        }
         tma_load_2d(smem + L.x + s * p.bn * 128, &xmap, &full[s], kblock(i) * kBK, m0);
         issued = i + 1;
       }
@@ -176,7 +204,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;          // the TMEM lanes this warp may read: 32 * quarter ..
     const int half = (warp - 2) >> 2;      // which 32 k of each stage (and which column chunks) it owns
     const int row = quarter * 32 + lane;
-    const int grow = min(n0 + row, p.n - 1);  // rows past N are zero-filled by TMA; their scale is unused
+    // the weight row this thread dequantises (rows past N are zero-filled by TMA; their scale is unused)
+    const int grow = MODE == kGateUp ? n0 + (row < 64 ? row : p.rows_per_expert / 2 + row - 64)
+                                     : min(n0 + row, p.n - 1);
     const int spr = p.k / G;
     // Scales: 4 stages (256 k) per vector load, prefetched one quad of stages ahead.
     constexpr int kHalvesPerQuad = 4 * kBK / G;  // 8, 4 or 2
@@ -244,8 +274,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = false;
     }
     tc_fence_after();
-    if (ok && !*abort_flag && nk > 0) {
-      const uint32_t taddr = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16);
+    const bool live = __all_sync(0xffffffffu, ok && !*abort_flag && nk > 0);  // tcgen05.ld is warp-collective
+    const uint32_t taddr = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16);
+    if (MODE == kDense && live) {
       const int r = n0 + row;
       for (int c0 = 32 * half; c0 < p.bn; c0 += 64) {
         float v[32];
@@ -260,6 +291,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                 atomicAdd(out, v[j]);
               else
                 *out = p.add ? *out + v[j] : v[j];
+            }
+          }
+        }
+      }
+    } else if (MODE == kGrouped && live) {
+      const int r = tn * kBM + row;  // output column within the expert
+      for (int c0 = 32 * half; c0 < p.bn; c0 += 64) {
+        float v[32];
+        tmem_ld32(taddr + c0, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < mcount) p.y[static_cast<size_t>(m0 + c0 + j) * p.n_out + r] = v[j];
+      }
+    } else if (MODE == kGateUp) {
+      // Up rows (TMEM lanes 64-127) go through shared memory (the A ring is free now) to the
+      // threads holding the matching gate rows (lanes 0-63): a = silu(gate) * up, fp16.
+      float *up = reinterpret_cast<float *>(smem + L.a);  // [64 rows][bn]
+      if (live && row >= 64) {
+        for (int c0 = 32 * half; c0 < p.bn; c0 += 64) {
+          float v[32];
+          tmem_ld32(taddr + c0, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (c0 + j < p.bn) up[(row - 64) * p.bn + c0 + j] = v[j];
+        }
+      }
+      named_bar_sync(1, 32 * kDeqWarps);
+      if (live && row < 64) {
+        const int col = tn * (kBM / 2) + row;  // output column within the expert
+        for (int c0 = 32 * half; c0 < p.bn; c0 += 64) {
+          float v[32];
+          tmem_ld32(taddr + c0, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (c0 + j < mcount) {
+              const float g = v[j], u = up[row * p.bn + c0 + j];
+              p.y16[static_cast<size_t>(m0 + c0 + j) * p.n_out + col] = __float2half_rn(g / (1.f + expf(-g)) * u);
             }
           }
         }
@@ -318,7 +386,7 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
     cudaError_t e = cudaMemsetAsync(p.y, 0, static_cast<size_t>(p.m) * p.n * sizeof(float), stream);
     if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_gemm_q4: zeroing y: %s", cudaGetErrorString(e));
   }
-  auto kern = gemm_q4_kernel<G>;
+  auto kern = gemm_q4_kernel<G, kDense>;
   static size_t configured = 0;
   if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -329,7 +397,75 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
   return check_launch("mq_gemm_q4");
 }
 
+template <int G, int MODE>
+int launch_grouped(const uint32_t *wq, const __half *ws, const __half *xs, int64_t pairs, int64_t k, int experts,
+                   int rows_per_expert, const int32_t *tiles, const int32_t *ntiles, int max_tiles, int bn, void *out,
+                   cudaStream_t stream, const DeviceInfo &dev) {
+  Params p{};
+  p.ws = ws;
+  p.y = MODE == kGrouped ? static_cast<float *>(out) : nullptr;
+  p.y16 = MODE == kGateUp ? static_cast<__half *>(out) : nullptr;
+  p.tiles = tiles;
+  p.ntiles = ntiles;
+  p.rows_per_expert = rows_per_expert;
+  p.n_out = MODE == kGateUp ? rows_per_expert / 2 : rows_per_expert;
+  p.n = experts * rows_per_expert;
+  p.k = static_cast<int>(k);
+  p.m = static_cast<int>(pairs);
+  p.bn = bn;
+  p.tiles_m = 1;
+  p.tiles_n = MODE == kGateUp ? (rows_per_expert / 2) / (kBM / 2) : rows_per_expert / kBM;
+  p.splitk = 1;
+  p.kb_split = p.k / kBK;
+  p.tmem_cols = 32;
+  while (p.tmem_cols < static_cast<uint32_t>(bn)) p.tmem_cols *= 2;
+  Layout L{};
+  for (p.stages = kMaxStages; p.stages >= 2; --p.stages) {
+    L = layout(p.bn, p.stages);
+    if (L.total + 1024 <= dev.smem_optin) break;
+  }
+  const size_t smem = L.total + 1024;
+  CUtensorMap wmap, xmap;
+  if (int rc = encode_tmap_2d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.k / 8, p.n, static_cast<uint64_t>(p.k) / 2,
+                              kBK / 8, MODE == kGateUp ? kBM / 2 : kBM, CU_TENSOR_MAP_SWIZZLE_NONE, "mq_moe_gemm_q4 weights"))
+    return rc;
+  if (int rc = encode_tmap_2d(&xmap, xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k, p.m, static_cast<uint64_t>(p.k) * 2, kBK,
+                              p.bn, CU_TENSOR_MAP_SWIZZLE_128B, "mq_moe_gemm_q4 activations"))
+    return rc;
+  auto kern = gemm_q4_kernel<G, MODE>;
+  static size_t configured = 0;
+  if (smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_moe_gemm_q4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured = smem;
+  }
+  kern<<<max_tiles * p.tiles_n, kThreads, smem, stream>>>(wmap, xmap, p);
+  return check_launch("mq_moe_gemm_q4");
+}
+
 }  // namespace gemm
+
+// Grouped expert product (MoE): mode 1 = gate|up with SiLU (fp16 out), mode 2 = plain (fp32 out).
+int moe_gemm_run(int mode, const uint32_t *wq, const uint16_t *ws, const uint16_t *xs, int64_t pairs, int64_t k,
+                 int experts, int64_t rows_per_expert, int group, const int32_t *tiles, const int32_t *ntiles,
+                 int max_tiles, int tile_m, void *out, cudaStream_t stream) {
+  DeviceInfo dev;
+  if (int rc = device_info(&dev)) return rc;
+  const __half *w16 = reinterpret_cast<const __half *>(ws);
+  const __half *x16 = reinterpret_cast<const __half *>(xs);
+  const int rpe = static_cast<int>(rows_per_expert);
+#define MQ_GROUPED(G)                                                                                                  \
+  return mode == 1 ? gemm::launch_grouped<G, gemm::kGateUp>(wq, w16, x16, pairs, k, experts, rpe, tiles, ntiles,       \
+                                                           max_tiles, tile_m, out, stream, dev)                       \
+                   : gemm::launch_grouped<G, gemm::kGrouped>(wq, w16, x16, pairs, k, experts, rpe, tiles, ntiles,      \
+                                                            max_tiles, tile_m, out, stream, dev)
+  switch (group) {
+    case 32: MQ_GROUPED(32);
+    case 64: MQ_GROUPED(64);
+    default: MQ_GROUPED(128);
+  }
+#undef MQ_GROUPED
+}
 
 // Shared by mq_gemm_q4 and the batched decode path of mq_gemv_q4.
 int gemm_q4_run(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y, int64_t n, int64_t k,
@@ -381,4 +517,25 @@ extern "C" int mq_gemm_q4(const uint32_t *wq, const uint16_t *ws, const void *x,
              "mq_gemm_q4: wq, ws and x must be 16-byte aligned, y 4-byte aligned");
   return mq::gemm_q4_run(wq, ws, x, x_dtype, y, n, k, m, group, add, workspace, workspace_bytes,
                          static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mq_moe_gemm_q4(int mode, const uint32_t *wq, const uint16_t *ws, const uint16_t *xs, int64_t pairs,
+                              int64_t k, int experts, int64_t rows_per_expert, int group, const int32_t *tiles,
+                              const int32_t *ntiles, int max_tiles, int tile_m, void *out, void *stream) {
+  MQ_REQUIRE(wq && ws && xs && tiles && ntiles && out, MQ_EINVAL, "mq_moe_gemm_q4: null pointer");
+  MQ_REQUIRE(mode == 1 || mode == 2, MQ_EINVAL, "mq_moe_gemm_q4: mode must be 1 (gate|up, SiLU) or 2 (plain)");
+  MQ_REQUIRE(pairs > 0 && k > 0 && k % 256 == 0, MQ_EINVAL, "mq_moe_gemm_q4: k=%lld must be a multiple of 256",
+             static_cast<long long>(k));
+  MQ_REQUIRE(experts >= 1 && rows_per_expert > 0 && static_cast<int64_t>(experts) * rows_per_expert < (1LL << 31), MQ_EINVAL,
+             "mq_moe_gemm_q4: bad expert shape");
+  MQ_REQUIRE(mode == 1 ? rows_per_expert % 128 == 0 : rows_per_expert % 128 == 0, MQ_EINVAL,
+             "mq_moe_gemm_q4: rows per expert must be a multiple of 128 (gate|up: 2fe with fe %% 64 == 0)");
+  MQ_REQUIRE(group == 32 || group == 64 || group == 128, MQ_EINVAL, "mq_moe_gemm_q4: group must be 32, 64 or 128");
+  MQ_REQUIRE(tile_m >= 16 && tile_m <= (mode == 1 ? 128 : 256) && tile_m % 16 == 0, MQ_EINVAL,
+             "mq_moe_gemm_q4: tile_m must be a multiple of 16 in 16..%d", mode == 1 ? 128 : 256);
+  MQ_REQUIRE(max_tiles >= 1, MQ_EINVAL, "mq_moe_gemm_q4: max_tiles must be >= 1");
+  MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(ws, 16) && mq::aligned(xs, 16), MQ_EALIGN,
+             "mq_moe_gemm_q4: wq, ws and xs must be 16-byte aligned");
+  return mq::moe_gemm_run(mode, wq, ws, xs, pairs, k, experts, rows_per_expert, group, tiles, ntiles, max_tiles, tile_m,
+                          out, static_cast<cudaStream_t>(stream));
 }

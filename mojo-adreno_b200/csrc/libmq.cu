@@ -7,3 +7,4 @@
 #include "gemv_q4.cu"
 #include "tgemv.cu"
 #include "gemm_q4.cu"
+#include "moe.cu"

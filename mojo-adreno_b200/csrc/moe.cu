@@ -1,0 +1,348 @@
+// Top-k MoE on int4 experts: routing, grouping by expert, gathering, the SwiGLU product and the
+// weighted combine (the expert products themselves run on the grouped tcgen05 GEMM, gemm_q4.cu,
+// and for one token on the grouped GEMV, gemv_q4.cu).
+//
+// Reference functions (qwen3moe/kernels/moek.mojo): route / p_route (:156-197, :385-425),
+// p_expert_lists / p_expert_items (:432-442, :548-557), t_moe_gate_up / t_moe_down (:560-608),
+// moe_gate_up / moe_down (:200-223), p_moe_sum (:479-488); the grouped design follows
+// lfm2moe/kernels/mk.mojo:123-199 (p_group, p_gather, p_silu_mul, p_combine).
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace mq {
+namespace moe {
+
+// ---- routing: one warp per token -----------------------------------------------------------
+// Top-k experts by logit (the lowest index among equals), then softmax over the k chosen logits
+// (max-subtracted, fp32), as route / p_route compute it. E <= 256 (each lane holds E / 32 logits).
+template <int PER>  // logits per lane
+__global__ void route_kernel(const float *__restrict__ logits, int32_t *__restrict__ ids, float *__restrict__ weights,
+                             int tokens, int experts, int topk) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  if (warp >= tokens) return;
+  const float *lg = logits + static_cast<size_t>(warp) * experts;
+  float v[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = i * 32 + lane;
+    v[i] = e < experts ? lg[e] : -INFINITY;
+  }
+  float top[32];
+  int32_t idx[32];
+  for (int k = 0; k < topk; ++k) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = i * 32 + lane;
+      if (e < experts && (v[i] > best || (v[i] == best && e < bi))) {
+        best = v[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+    top[k] = best;
+    idx[k] = bi;
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (i * 32 + lane == bi) v[i] = -INFINITY;
+  }
+  if (lane == 0) {
+    float total = 0.f;
+    for (int k = 0; k < topk; ++k) total += expf(top[k] - top[0]);
+    for (int k = 0; k < topk; ++k) {
+      ids[static_cast<size_t>(warp) * topk + k] = idx[k];
+      weights[static_cast<size_t>(warp) * topk + k] = expf(top[k] - top[0]) / total;
+    }
+  }
+}
+
+// ---- grouping: a stable counting sort of the (token, slot) pairs by expert, one CTA ---------
+// offsets[e] = number of pairs routed to experts < e; order[offsets[e] + r] = the r-th pair (in
+// increasing pair index t * topk + k) whose expert is e -- p_expert_lists' lists, concatenated;
+// slot_of[pair] = its position in that order; tiles = (expert, first row, rows) work items of at
+// most `tile` rows per expert -- p_expert_items' items, over the concatenated lists.
+constexpr int kGroupThreads = 1024;
+
+__global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__restrict__ ids, int pairs, int experts,
+                                                              int tile, int32_t *__restrict__ counts,
+                                                              int32_t *__restrict__ offsets, int32_t *__restrict__ order,
+                                                              int32_t *__restrict__ slot_of, int32_t *__restrict__ tiles,
+                                                              int32_t *__restrict__ ntiles) {
+  extern __shared__ int32_t sh[];
+  int32_t *warp_cnt = sh;                        // [32 warps][experts]
+  int32_t *base = warp_cnt + 32 * experts;       // [experts] running start within the expert
+  int32_t *start = base + experts;               // [experts + 1] offsets
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const unsigned lt_mask = (1u << lane) - 1u;
+
+  // Pass 1: histogram.
+  for (int e = threadIdx.x; e < experts; e += kGroupThreads) base[e] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < pairs; i += kGroupThreads) atomicAdd(&base[ids[i]], 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0, nt = 0;
+    for (int e = 0; e < experts; ++e) {
+      start[e] = run;
+      const int c = base[e];
+      counts[e] = c;
+      offsets[e] = run;
+      for (int r = 0; r < c; r += tile) {
+        tiles[3 * nt] = e;
+        tiles[3 * nt + 1] = run + r;
+        tiles[3 * nt + 2] = min(tile, c - r);
+        ++nt;
+      }
+      run += c;
+    }
+    start[experts] = run;
+    offsets[experts] = run;
+    *ntiles = nt;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < experts; e += kGroupThreads) base[e] = start[e];
+  __syncthreads();
+
+  // Pass 2: positions, chunk by chunk of kGroupThreads pairs (stable: ranks follow pair index).
+  for (int c0 = 0; c0 < pairs; c0 += kGroupThreads) {
+    const int i = c0 + threadIdx.x;
+    const bool live = i < pairs;
+    const int e = live ? ids[i] : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int rank_in_warp = __popc(same & lt_mask);
+    for (int j = threadIdx.x; j < 32 * experts; j += kGroupThreads) warp_cnt[j] = 0;
+    __syncthreads();
+    if (live && rank_in_warp == 0) warp_cnt[warp * experts + e] = __popc(same);
+    __syncthreads();
+    // exclusive scan over warps per expert, added to the running base
+    for (int ex = threadIdx.x; ex < experts; ex += kGroupThreads) {
+      int run = base[ex];
+      for (int w = 0; w < 32; ++w) {
+        const int c = warp_cnt[w * experts + ex];
+        warp_cnt[w * experts + ex] = run;
+        run += c;
+      }
+      base[ex] = run;
+    }
+    __syncthreads();
+    if (live) {
+      const int pos = warp_cnt[warp * experts + e] + rank_in_warp;
+      order[pos] = i;
+      slot_of[i] = pos;
+    }
+    __syncthreads();
+  }
+}
+
+// ---- gather: expert-sorted fp16 copies of the tokens' rows ---------------------------------------
+// xg[s] = fp16(x[order[s] / topk]) (p_gather of lfm2moe/kernels/mk.mojo:164-176).
+__global__ void gather_kernel(const void *__restrict__ x, int x_f16, const int32_t *__restrict__ order, int pairs,
+                              int topk, int d, __half *__restrict__ xg) {
+  const int vec = d / 8;  // 8 values per thread step
+  for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < static_cast<int64_t>(pairs) * vec;
+       it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int s = static_cast<int>(it / vec), c = static_cast<int>(it % vec) * 8;
+    const int t = order[s] / topk;
+    uint4 out;
+    if (x_f16) {
+      out = *reinterpret_cast<const uint4 *>(static_cast<const __half *>(x) + static_cast<size_t>(t) * d + c);
+    } else {
+      const float4 *src = reinterpret_cast<const float4 *>(static_cast<const float *>(x) + static_cast<size_t>(t) * d + c);
+      const float4 a = src[0], b = src[1];
+      out = make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y), pack_half2(b.z, b.w));
+    }
+    *reinterpret_cast<uint4 *>(xg + static_cast<size_t>(s) * d + c) = out;
+  }
+}
+
+// ---- SwiGLU for the one-token path: a[k][j] = silu(h[k][j]) * h[k][fe + j] (moe_gate_up) -------
+__global__ void silu_mul_kernel(const float *__restrict__ h, float *__restrict__ a, int rows, int fe) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows * fe; i += gridDim.x * blockDim.x) {
+    const int r = i / fe, j = i % fe;
+    const float g = h[static_cast<size_t>(r) * 2 * fe + j], u = h[static_cast<size_t>(r) * 2 * fe + fe + j];
+    a[i] = g / (1.f + expf(-g)) * u;
+  }
+}
+
+// ---- combine: y[t][c] (+)= sum_k w[t][k] * z[slot_of[t * topk + k]][c] (p_moe_sum, p_combine) -----
+// The k terms are added in order k = 0 .. topk - 1, then added to y: deterministic.
+__global__ void combine_kernel(const float *__restrict__ z, const int32_t *__restrict__ slot_of,
+                               const float *__restrict__ w, int tokens, int topk, int d, int add, float *__restrict__ y) {
+  const int vec = d / 4;
+  for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < static_cast<int64_t>(tokens) * vec;
+       it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(it / vec), c = static_cast<int>(it % vec) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < topk; ++k) {
+      const float wk = w[static_cast<size_t>(t) * topk + k];
+      const int row = slot_of ? slot_of[static_cast<size_t>(t) * topk + k] : t * topk + k;
+      const float4 v = *reinterpret_cast<const float4 *>(z + static_cast<size_t>(row) * d + c);
+      acc.x += wk * v.x;
+      acc.y += wk * v.y;
+      acc.z += wk * v.z;
+      acc.w += wk * v.w;
+    }
+    float4 *out = reinterpret_cast<float4 *>(y + static_cast<size_t>(t) * d + c);
+    if (add) {
+      const float4 o = *out;
+      acc.x += o.x, acc.y += o.y, acc.z += o.z, acc.w += o.w;
+    }
+    *out = acc;
+  }
+}
+
+inline int grid_for(int64_t work, int threads, const DeviceInfo &dev) {
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + threads - 1) / threads, static_cast<int64_t>(dev.sms) * 8)));
+}
+
+}  // namespace moe
+}  // namespace mq
+
+extern "C" int mq_moe_route(const float *logits, int32_t *ids, float *weights, int64_t tokens, int experts, int topk,
+                            void *stream) {
+  MQ_REQUIRE(logits && ids && weights, MQ_EINVAL, "mq_moe_route: null pointer");
+  MQ_REQUIRE(tokens > 0 && tokens < (1 << 24), MQ_EINVAL, "mq_moe_route: bad token count %lld", static_cast<long long>(tokens));
+  MQ_REQUIRE(experts >= 1 && experts <= 256, MQ_EINVAL, "mq_moe_route: experts must be in 1..256 (got %d)", experts);
+  MQ_REQUIRE(topk >= 1 && topk <= 32 && topk <= experts, MQ_EINVAL, "mq_moe_route: topk must be in 1..min(32, experts)");
+  const int threads = 256, per_block = threads / 32;
+  const int grid = static_cast<int>((tokens + per_block - 1) / per_block);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int per = (experts + 31) / 32;
+  if (per <= 4)
+    mq::moe::route_kernel<4><<<grid, threads, 0, s>>>(logits, ids, weights, static_cast<int>(tokens), experts, topk);
+  else
+    mq::moe::route_kernel<8><<<grid, threads, 0, s>>>(logits, ids, weights, static_cast<int>(tokens), experts, topk);
+  return mq::check_launch("mq_moe_route");
+}
+
+extern "C" int mq_moe_group(const int32_t *ids, int64_t tokens, int topk, int experts, int tile, int32_t *counts,
+                            int32_t *offsets, int32_t *order, int32_t *slot_of, int32_t *tiles, int32_t *ntiles,
+                            void *stream) {
+  MQ_REQUIRE(ids && counts && offsets && order && slot_of && tiles && ntiles, MQ_EINVAL, "mq_moe_group: null pointer");
+  MQ_REQUIRE(tokens > 0 && topk >= 1 && tokens * topk < (1 << 30), MQ_EINVAL, "mq_moe_group: bad tokens / topk");
+  MQ_REQUIRE(experts >= 1 && experts <= 256, MQ_EINVAL, "mq_moe_group: experts must be in 1..256");
+  MQ_REQUIRE(tile >= 1, MQ_EINVAL, "mq_moe_group: tile must be >= 1");
+  const size_t smem = (32 * experts + 2 * experts + 1) * sizeof(int32_t);
+  mq::moe::group_kernel<<<1, mq::moe::kGroupThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      ids, static_cast<int>(tokens * topk), experts, tile, counts, offsets, order, slot_of, tiles, ntiles);
+  return mq::check_launch("mq_moe_group");
+}
+
+extern "C" int mq_moe_gather(const void *x, int x_dtype, const int32_t *order, int64_t pairs, int topk, int64_t d,
+                             uint16_t *xg, void *stream) {
+  MQ_REQUIRE(x && order && xg, MQ_EINVAL, "mq_moe_gather: null pointer");
+  MQ_REQUIRE(pairs > 0 && d > 0 && d % 8 == 0 && topk >= 1, MQ_EINVAL, "mq_moe_gather: d must be a multiple of 8");
+  MQ_REQUIRE(mq::aligned(x, 16) && mq::aligned(xg, 16), MQ_EALIGN, "mq_moe_gather: x and xg must be 16-byte aligned");
+  mq::DeviceInfo dev;
+  if (int rc = mq::device_info(&dev)) return rc;
+  mq::moe::gather_kernel<<<mq::moe::grid_for(pairs * (d / 8), 256, dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, x_dtype == MQ_F16, order, static_cast<int>(pairs), topk, static_cast<int>(d), reinterpret_cast<__half *>(xg));
+  return mq::check_launch("mq_moe_gather");
+}
+
+extern "C" int mq_moe_silu_mul(const float *h, float *a, int64_t rows, int64_t fe, void *stream) {
+  MQ_REQUIRE(h && a && rows > 0 && fe > 0, MQ_EINVAL, "mq_moe_silu_mul: bad arguments");
+  mq::DeviceInfo dev;
+  if (int rc = mq::device_info(&dev)) return rc;
+  mq::moe::silu_mul_kernel<<<mq::moe::grid_for(rows * fe, 256, dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      h, a, static_cast<int>(rows), static_cast<int>(fe));
+  return mq::check_launch("mq_moe_silu_mul");
+}
+
+extern "C" int mq_moe_combine(const float *z, const int32_t *slot_of, const float *weights, int64_t tokens, int topk,
+                              int64_t d, int add, float *y, void *stream) {
+  MQ_REQUIRE(z && weights && y, MQ_EINVAL, "mq_moe_combine: null pointer");
+  MQ_REQUIRE(tokens > 0 && topk >= 1 && d > 0 && d % 4 == 0, MQ_EINVAL, "mq_moe_combine: d must be a multiple of 4");
+  MQ_REQUIRE(mq::aligned(z, 16) && mq::aligned(y, 16), MQ_EALIGN, "mq_moe_combine: z and y must be 16-byte aligned");
+  mq::DeviceInfo dev;
+  if (int rc = mq::device_info(&dev)) return rc;
+  mq::moe::combine_kernel<<<mq::moe::grid_for(tokens * (d / 4), 256, dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      z, slot_of, weights, static_cast<int>(tokens), topk, static_cast<int>(d), add != 0, y);
+  return mq::check_launch("mq_moe_combine");
+}
+
+namespace mq {
+namespace moe {
+
+constexpr int kTileM = 64;  // tokens per expert work tile in the grouped GEMMs
+
+struct Work {
+  int32_t *counts, *offsets, *order, *slot_of, *tiles, *ntiles;
+  __half *xg, *a;
+  float *z;
+  size_t bytes;
+  int max_tiles;
+};
+
+inline size_t align_up(size_t v) { return (v + 255) / 256 * 256; }
+
+// Carves the caller's workspace (pointer may be null to only size it).
+inline Work carve(uint8_t *base, int64_t tokens, int experts, int topk, int64_t d, int64_t fe) {
+  Work w{};
+  const int64_t P = tokens * topk;
+  w.max_tiles = static_cast<int>(experts + (P + kTileM - 1) / kTileM);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t *p = base ? base + off : nullptr;
+    off += align_up(bytes);
+    return p;
+  };
+  w.counts = reinterpret_cast<int32_t *>(take(experts * 4));
+  w.offsets = reinterpret_cast<int32_t *>(take((experts + 1) * 4));
+  w.order = reinterpret_cast<int32_t *>(take(P * 4));
+  w.slot_of = reinterpret_cast<int32_t *>(take(P * 4));
+  w.tiles = reinterpret_cast<int32_t *>(take(static_cast<size_t>(w.max_tiles) * 3 * 4));
+  w.ntiles = reinterpret_cast<int32_t *>(take(4));
+  w.xg = reinterpret_cast<__half *>(take(P * d * 2));
+  w.a = reinterpret_cast<__half *>(take(P * fe * 2));
+  w.z = reinterpret_cast<float *>(take(P * d * 4));
+  w.bytes = off;
+  return w;
+}
+
+}  // namespace moe
+}  // namespace mq
+
+extern "C" size_t mq_moe_workspace_size(int64_t tokens, int experts, int topk, int64_t d, int64_t fe) {
+  if (tokens <= 0 || experts <= 0 || topk <= 0 || d <= 0 || fe <= 0) return 0;
+  return mq::moe::carve(nullptr, tokens, experts, topk, d, fe).bytes;
+}
+
+extern "C" int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, const float *weights, const uint32_t *gu_wq,
+                              const uint16_t *gu_ws, const uint32_t *dn_wq, const uint16_t *dn_ws, float *y, int64_t tokens,
+                              int experts, int topk, int64_t d, int64_t fe, int group, int add, void *workspace,
+                              size_t workspace_bytes, void *stream) {
+  MQ_REQUIRE(x && ids && weights && gu_wq && gu_ws && dn_wq && dn_ws && y, MQ_EINVAL, "mq_moe_forward: null pointer");
+  MQ_REQUIRE(tokens > 0 && experts >= 1 && experts <= 256 && topk >= 1 && topk <= experts, MQ_EINVAL,
+             "mq_moe_forward: bad tokens / experts / topk");
+  MQ_REQUIRE(d % 256 == 0 && fe % 256 == 0, MQ_EINVAL, "mq_moe_forward: d and fe must be multiples of 256");
+  MQ_REQUIRE(x_dtype == MQ_F32 || x_dtype == MQ_F16, MQ_EINVAL, "mq_moe_forward: x_dtype must be MQ_F32 or MQ_F16");
+  const mq::moe::Work need = mq::moe::carve(nullptr, tokens, experts, topk, d, fe);
+  MQ_REQUIRE(workspace && workspace_bytes >= need.bytes, MQ_EINVAL, "mq_moe_forward: needs a workspace of %zu bytes (got %zu)",
+             need.bytes, workspace_bytes);
+  MQ_REQUIRE(mq::aligned(workspace, 256), MQ_EALIGN, "mq_moe_forward: workspace must be 256-byte aligned");
+  const mq::moe::Work w = mq::moe::carve(static_cast<uint8_t *>(workspace), tokens, experts, topk, d, fe);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t P = tokens * topk;
+  if (int rc = mq_moe_group(ids, tokens, topk, experts, mq::moe::kTileM, w.counts, w.offsets, w.order, w.slot_of, w.tiles,
+                            w.ntiles, s))
+    return rc;
+  if (int rc = mq_moe_gather(x, x_dtype, w.order, P, topk, d, reinterpret_cast<uint16_t *>(w.xg), s)) return rc;
+  if (int rc = mq::moe_gemm_run(1, gu_wq, gu_ws, reinterpret_cast<const uint16_t *>(w.xg), P, d, experts, 2 * fe, group,
+                                w.tiles, w.ntiles, w.max_tiles, mq::moe::kTileM, w.a, s))
+    return rc;
+  if (int rc = mq::moe_gemm_run(2, dn_wq, dn_ws, reinterpret_cast<const uint16_t *>(w.a), P, fe, experts, d, group, w.tiles,
+                                w.ntiles, w.max_tiles, mq::moe::kTileM, w.z, s))
+    return rc;
+  return mq_moe_combine(w.z, w.slot_of, weights, tokens, topk, d, add, y, s);
+}

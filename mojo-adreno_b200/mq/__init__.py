@@ -8,3 +8,4 @@ no sm_100 device is present.
 """
 from ._lib import MQError, lib, library_path  # noqa: F401
 from .kernels import *  # noqa: F401,F403
+from .moe import *  # noqa: F401,F403

@@ -10,6 +10,8 @@ Sources (nothing here is restated; every output comes from the reference's own c
   * qwen3moe/convert.c (oracle/_ref/...)      -> qwen3moe_q4_g*.npz   (searched-scale packer)
   * lfm2/convert.c (oracle/_ref/lfm2_convert) -> lfm2_q4.npz          (GGUF Q4_0 -> words)
   * qwen3/convert.cpp addPacked (oracle/_ref/qwen3_pack) -> qwen3_pack.npz (ternary transpose)
+  * transformers' Qwen3MoeSparseMoeBlock (the module qwen3moe/reference.py runs as its reference,
+    :94-147), on int4 experts dequantised as Weights.int4 does -> moe_block.npz
 Inputs are small seeded arrays with edge cases (all-zero groups, tiny and large magnitudes,
 exact ties). The binaries are built by `make -C oracle`.
 """
@@ -171,6 +173,37 @@ def main():
         np.savez(os.path.join(HERE, "qwen3_pack.npz"), codes=codes, scales=scales, biases=biases,
                  w=raw[:wb].view(np.uint32).reshape(k // 16, n), s=raw[wb:].view(np.float16).reshape(k // 128, n),
                  bad_biases=bad, bad_rc=rc_bad, bad_msg=msg_bad.strip())
+    # --- the MoE block of transformers on dequantised int4 experts -------------------------------
+    from transformers import Qwen3MoeConfig
+    from transformers.models.qwen3_moe import modeling_qwen3_moe as qm
+    d, fe, experts, topk, tokens, g = 256, 256, 8, 2, 24, 32
+    cfg = Qwen3MoeConfig(hidden_size=d, num_experts=experts, num_experts_per_tok=topk, moe_intermediate_size=fe,
+                         norm_topk_prob=True, intermediate_size=4 * d, num_attention_heads=4, num_key_value_heads=2,
+                         head_dim=64)
+    block = qm.Qwen3MoeSparseMoeBlock(cfg).eval()
+    gu_wq = rng.integers(0, 1 << 32, size=(experts * 2 * fe, d // 8), dtype=np.uint32)
+    gu_ws = np.abs(rng.normal(0, 0.02, size=(experts * 2 * fe, d // g))).astype(np.float16)
+    dn_wq = rng.integers(0, 1 << 32, size=(experts * d, fe // 8), dtype=np.uint32)
+    dn_ws = np.abs(rng.normal(0, 0.02, size=(experts * d, fe // g))).astype(np.float16)
+    router = rng.normal(0, 0.1, size=(experts, d)).astype(np.float32)
+    x = rng.standard_normal((tokens, d)).astype(np.float32)
+
+    def deq(wq, ws, rows, cols):  # Weights.int4 of qwen3moe/reference.py:53-65 on the same words
+        obj = qref.Weights.__new__(qref.Weights)
+        obj.bin = np.frombuffer(wq.tobytes() + ws.tobytes(), np.uint8)
+        obj.man = {"m.q": (0, wq.nbytes, "u32", [rows, cols // 8]), "m.s": (wq.nbytes, ws.nbytes, "f16", [rows, cols // g])}
+        return obj.int4("m")
+
+    with torch.no_grad():
+        block.experts.gate_up_proj.copy_(deq(gu_wq, gu_ws, experts * 2 * fe, d).reshape(experts, 2 * fe, d))
+        block.experts.down_proj.copy_(deq(dn_wq, dn_ws, experts * d, fe).reshape(experts, d, fe))
+        block.gate.weight.copy_(torch.from_numpy(router))
+        xt = torch.from_numpy(x)
+        _, w_sel, ids_sel = block.gate(xt)
+        y = block(xt[None])[0]
+    np.savez(os.path.join(HERE, "moe_block.npz"), x=x, router=router, logits=x @ router.T, gu_wq=gu_wq, gu_ws=gu_ws,
+             dn_wq=dn_wq, dn_ws=dn_ws, ids=ids_sel.numpy().astype(np.int32), weights=w_sel.numpy().astype(np.float32),
+             y=y.numpy(), d=d, fe=fe, experts=experts, topk=topk, group=g)
     print("fixtures written to", HERE)
 
 

@@ -1,0 +1,85 @@
+"""MoE parity on the GPU through the C ABI: routing and grouping bit-exact against the oracle,
+the layer within the 1e-3 normwise bar (fp16 x and fp16 q*scale, fp32 accumulation)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, normwise
+from oracle import moe as omoe
+
+import mq
+from mq import synth
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def t(a, dev):
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint32:
+        a = a.view(np.int32)
+    return torch.from_numpy(a).to(dev)
+
+
+@pytest.mark.parametrize("tokens,experts,topk", [(404, 128, 8), (1, 128, 8), (33, 60, 6), (7, 256, 32)])
+def test_route_matches_oracle(cuda, tokens, experts, topk):
+    rng = np.random.default_rng(tokens + experts)
+    logits = rng.standard_normal((tokens, experts)).astype(np.float32)
+    logits[0, :8] = logits[0, 8]  # ties: the lowest index wins
+    ids = torch.empty(tokens, topk, dtype=torch.int32, device=cuda)
+    w = torch.empty(tokens, topk, device=cuda)
+    mq.p_route(t(logits, cuda), ids, w, topk=topk)
+    torch.cuda.synchronize()
+    rid, rw = omoe.route(logits, topk)
+    np.testing.assert_array_equal(ids.cpu().numpy(), rid)
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("tokens,experts,topk", [(404, 128, 8), (1, 128, 8), (300, 7, 3)])
+def test_group_matches_oracle(cuda, tokens, experts, topk):
+    rng = np.random.default_rng(7 + tokens)
+    ids = np.stack([rng.choice(experts, topk, replace=False) for _ in range(tokens)]).astype(np.int32)
+    counts, offsets, order, slot_of, tiles, ntiles = mq.p_expert_lists(t(ids, cuda), experts, tile=64)
+    torch.cuda.synchronize()
+    ro, rorder = omoe.expert_lists(ids, experts)
+    np.testing.assert_array_equal(offsets.cpu().numpy(), ro)
+    np.testing.assert_array_equal(order.cpu().numpy(), rorder)
+    so = slot_of.cpu().numpy()
+    np.testing.assert_array_equal(so[rorder], np.arange(tokens * topk))
+    nt = int(ntiles.item())
+    tl = tiles.cpu().numpy()[:3 * nt].reshape(nt, 3)
+    cnt = np.diff(ro)
+    assert nt == int(np.sum((cnt + 63) // 64))
+    for e, r0, rows in tl:
+        assert ro[e] <= r0 and r0 + rows <= ro[e + 1] and 1 <= rows <= 64
+
+
+def run_forward(cuda, x, ids, w, gu_wq, gu_ws, dn_wq, dn_ws, d, fe, group, add_to=None):
+    tokens = x.shape[0]
+    y = torch.full((tokens, d), float("nan"), device=cuda) if add_to is None else t(add_to, cuda)
+    mq.moe_forward(t(x, cuda), t(ids, cuda), t(w, cuda), t(gu_wq, cuda), t(gu_ws, cuda), t(dn_wq, cuda), t(dn_ws, cuda), y,
+                   d, fe, group=group, add=add_to is not None)
+    torch.cuda.synchronize()
+    assert mq.device_status() == 0
+    return y.cpu().numpy()
+
+
+def test_moe_forward_matches_transformers_block(cuda):
+    z = np.load(os.path.join(GOLDEN, "moe_block.npz"))
+    y = run_forward(cuda, z["x"], z["ids"], z["weights"], z["gu_wq"], z["gu_ws"], z["dn_wq"], z["dn_ws"], int(z["d"]),
+                    int(z["fe"]), int(z["group"]))
+    assert normwise(y, z["y"]) <= TOL
+
+
+@pytest.mark.parametrize("tokens", [404, 1, 3])
+def test_moe_forward_baseline_config(cuda, tokens):
+    """Qwen3-30B-A3B MoE layer shapes (hidden 2048, 128 experts, top-8, FE 768,
+    int4 G=32); 404 prompt tokens, and 1-token decode."""
+    m = synth.moe_layer(seed=0, tokens=tokens)
+    ids, w = omoe.route(m["logits"], 8)
+    r = np.random.default_rng(1).standard_normal((tokens, 2048)).astype(np.float32)
+    y = run_forward(cuda, m["x"], ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 2048, 768, 32, add_to=r.copy())
+    ref = r + omoe.moe_layer(m["x"], ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 32, 768)
+    assert normwise(y, ref) <= TOL

@@ -103,3 +103,39 @@ def test_gemv_reference_order_close_to_exact():
     a = q4.gemv_reference_order(z["wq"], z["ws"], x, 64)
     b = q4.gemv(z["wq"], z["ws"], x, 64)[0]
     assert np.abs(a - b).max() <= 1e-5 * np.abs(b).max()
+
+
+def test_moe_oracle_matches_transformers_block():
+    """oracle.moe (routing and the SwiGLU expert layer) against transformers' Qwen3MoeSparseMoeBlock
+    run on the same int4 experts (the reference's own check, qwen3moe/reference.py:94-147)."""
+    from oracle import moe
+
+    z = load("moe_block.npz")
+    ids, w = moe.route(z["logits"], int(z["topk"]))
+    np.testing.assert_array_equal(ids, z["ids"])
+    np.testing.assert_allclose(w, z["weights"], rtol=2e-6, atol=1e-7)
+    y = moe.moe_layer(z["x"], ids, w, z["gu_wq"], z["gu_ws"], z["dn_wq"], z["dn_ws"], int(z["group"]), int(z["fe"]))
+    assert np.abs(y - z["y"]).max() <= 1e-5 * np.abs(z["y"]).max()
+
+
+def test_route_ties_prefer_lowest_index():
+    from oracle import moe
+
+    logits = np.zeros((3, 16), np.float32)
+    logits[0, [3, 7, 9]] = 1.0          # three-way tie for the top: 3, 7, 9
+    logits[1, :] = np.arange(16)[::-1]  # strictly decreasing
+    logits[2, [5, 2]] = [2.0, 2.0]
+    ids, w = moe.route(logits, 4)
+    assert ids[0].tolist()[:3] == [3, 7, 9] and ids[0][3] == 0
+    assert ids[1].tolist() == [0, 1, 2, 3]
+    assert ids[2].tolist()[:2] == [2, 5]
+    np.testing.assert_allclose(w.sum(1), 1.0, rtol=1e-6)
+
+
+def test_expert_lists_stable():
+    from oracle import moe
+
+    ids = np.array([[3, 1], [1, 0], [3, 2], [1, 3]], np.int32)
+    offsets, order = moe.expert_lists(ids, 4)
+    assert offsets.tolist() == [0, 1, 4, 5, 8]
+    assert order.tolist() == [3, 1, 2, 6, 5, 0, 4, 7]
