@@ -289,6 +289,9 @@ def run_mq(args):
                 "x": "fp16 [64, k] per matrix", "path": "tcgen05 GEMM (batch > 4)"}
     del b64_graphs
 
+    # ---- secondary: Qwen3-30B-A3B MoE layer: 404-token prefill, 1-token decode
+    moe_res = moe_bench(mq, synth, dev, stream, world, rank)
+
     head_bytes = q4_bytes(head["n"], head["k"], batch) * (world if world > 1 else 1)
     achieved = q4_bytes(head["n"], head["k"], batch) / (head_ms * 1e-3) / 1e9
     traffic = None
@@ -324,6 +327,7 @@ def run_mq(args):
             "ternary_gemv": tern,
             "prefill_gemm": prefill,
             "decode_batch64": decode64,
+            "moe": moe_res,
             "gpu_launches": args.steps * len(mats),
             "clocks": clocks,
         }
@@ -334,6 +338,36 @@ def run_mq(args):
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+def moe_bench(mq, synth, dev, stream, world, rank):
+    """Tokens/s of the MoE layer (routing given) on this rank's experts. With N ranks the experts are
+    split expert-parallel (mq/ep.py); at N = 1 every expert is local."""
+    from oracle import moe as omoe  # routing of the synthetic logits only (ids/weights are inputs here)
+
+    out = {}
+    for tokens in (404, 1):
+        m = synth.moe_layer(seed=0, tokens=tokens)
+        ids, w = omoe.route(m["logits"], 8)
+        tx = torch.from_numpy(m["x"]).to(dev)
+        tids, tw = torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev)
+        gw = [torch.from_numpy(m[k].view(np.int32) if m[k].dtype == np.uint32 else m[k]).to(dev)
+              for k in ("gu_wq", "gu_ws", "dn_wq", "dn_ws")]
+        wbytes = sum(a.numel() * a.element_size() for a in gw)
+        copies = rotating_copies(wbytes)
+        gws = [gw] + [[a.clone() for a in gw] for _ in range(copies - 1)]
+        y = torch.zeros(tokens, 2048, device=dev)
+        ws = torch.empty(mq.lib.mq_moe_workspace_size(tokens, 128, 8, 2048, 768), dtype=torch.uint8, device=dev)
+        graphs = [graph_of(lambda c=c: mq.moe_forward(tx, tids, tw, *gws[c], y, 2048, 768, group=32, workspace=ws))
+                  for c in range(copies)]
+        ms = max_over_ranks(time_graphs(graphs, 50, stream), world)
+        used = np.unique(ids)
+        active_bytes = len(used) * (1536 * 2048 + 2048 * 768) * 9 // 16  # int4 + fp16 scales per G=32
+        out[f"tokens_{tokens}"] = {"ms": round(ms, 5), "tokens/s": round(tokens / (ms * 1e-3), 1),
+                                   "experts_touched": int(len(used)),
+                                   "expert_weight_GB/s": round(active_bytes / (ms * 1e-3) / 1e9, 1)}
+        del graphs, gws
+    return out
 
 
 class CpuSample:

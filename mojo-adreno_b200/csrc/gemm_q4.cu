@@ -4,6 +4,9 @@
 // 458-495): Y[m][r] (+)= sum_k X[m][k] * W[r][k], W int4 with an fp16 scale per `group` weights of a
 // row, X fp16 [M][K], Y fp32 [M][N]. The reference stages X and the dequantised W slice in shared
 // memory and multiplies on fp32 cooperative matrices; here:
+//  * Up to 128 tokens (decode batches, MoE expert tiles): two CTAs per SM, each with at most half the
+//    shared memory, so their pipelines hide each other's TMA, dequant and hand-off latencies. Larger
+//    prefills: one CTA per SM with token tiles up to 256, dequantising each weight tile fewer times.
 //  * The MMA sees W as the A operand (M = 128 weight rows per CTA) and the tokens as B (N = BN, a
 //    multiple of 16 up to 256), so the accumulator tile in TMEM is [128 weight rows][BN tokens]
 //    and the epilogue writes Y rows with consecutive threads on consecutive addresses.
@@ -100,7 +103,7 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, __half2 s2) {
 }
 
 template <int G, int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     gemm_q4_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -352,8 +355,11 @@ __global__ void f32_to_f16_kernel(const float4 *__restrict__ x, uint2 *__restric
 
 template <int G>
 int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream, const DeviceInfo &dev) {
-  // Tiles: tokens split as evenly as possible into <= 256-wide tiles of a multiple of 16.
-  p.tiles_m = (p.m + 255) / 256;
+  // Tiles: tokens split as evenly as possible into tiles of a multiple of 16. Up to 128 tokens: one
+  // tile, two CTAs per SM (two independent pipelines hide each other's latencies). More: tiles of up
+  // to 256 tokens and one CTA per SM, so each weight tile is dequantised as few times as possible.
+  const bool two_per_sm = p.m <= 128;
+  p.tiles_m = two_per_sm ? 1 : (p.m + 255) / 256;
   p.bn = ((p.m + p.tiles_m - 1) / p.tiles_m + 15) / 16 * 16;
   p.tiles_n = (p.n + kBM - 1) / kBM;
   p.tmem_cols = 32;
@@ -366,11 +372,12 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
   if (splitk == 1 && tiles < dev.sms / 2 && quads >= 3 && tiles * 3 <= dev.sms) splitk = 3;
   p.kb_split = ((quads + splitk - 1) / splitk) * 4;
   p.splitk = (nkb + p.kb_split - 1) / p.kb_split;
-  // Pipeline depth: as many stages as shared memory holds.
+  // Pipeline depth: as many stages as the SM's shared memory (or half of it) holds.
+  const size_t budget = two_per_sm ? dev.smem_optin / 2 - 1024 : dev.smem_optin;
   Layout L{};
   for (p.stages = kMaxStages; p.stages >= 2; --p.stages) {
     L = layout(p.bn, p.stages);
-    if (L.total + 1024 <= dev.smem_optin) break;
+    if (L.total + 1024 <= budget) break;
   }
   const size_t smem = L.total + 1024;
   MQ_REQUIRE(smem <= dev.smem_optin, MQ_EUNSUPPORTED, "mq_gemm_q4: tile of %d tokens needs %zu B of shared memory", p.bn,
@@ -422,7 +429,7 @@ int launch_grouped(const uint32_t *wq, const __half *ws, const __half *xs, int64
   Layout L{};
   for (p.stages = kMaxStages; p.stages >= 2; --p.stages) {
     L = layout(p.bn, p.stages);
-    if (L.total + 1024 <= dev.smem_optin) break;
+    if (L.total + 1024 <= dev.smem_optin / 2 - 1024) break;
   }
   const size_t smem = L.total + 1024;
   CUtensorMap wmap, xmap;
