@@ -142,6 +142,13 @@ MQ_API int mq_moe_gemm_q4(int mode, const uint32_t *wq, const uint16_t *ws, cons
                           int64_t k, int experts, int64_t rows_per_expert, int group, const int32_t *tiles,
                           const int32_t *ntiles, int max_tiles, int tile_m, void *out, void *stream);
 
+/* The expert-indirect decode GEMV (moe_gate_up / moe_down's products, moek.mojo:200-223):
+ * y[i * rows_per_group + r] = W[ids[i] * group_rows + r] . x_i for i < ngroups, r < rows_per_group,
+ * with x_i = x (x_per_group == 0) or x + i * k. W: [wrows][k/8] words; x fp32; rows_per_group % 32 == 0. */
+MQ_API int mq_moe_gemv_q4(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const float *x, float *y,
+                          const int32_t *ids, int ngroups, int group_rows, int rows_per_group, int64_t k, int group,
+                          int x_per_group, void *stream);
+
 /* a[r][j] = silu(h[r][j]) * h[r][fe + j] in fp32 (moe_gate_up's SwiGLU, moek.mojo:200-210). */
 MQ_API int mq_moe_silu_mul(const float *h, float *a, int64_t rows, int64_t fe, void *stream);
 
@@ -151,7 +158,8 @@ MQ_API int mq_moe_combine(const float *z, const int32_t *slot_of, const float *w
                           int64_t d, int add, float *y, void *stream);
 
 /* The whole MoE layer for precomputed routing: y (+)= sum_k w[t][k] * down_e(silu(gate_e x_t) * up_e x_t).
- * Runs group, gather, the two grouped products and the combine on `stream`, in a caller workspace of
+ * One fp32 token runs the decode GEMVs (mq_moe_gemv_q4); otherwise group, gather, the two grouped
+ * products and the combine run on `stream`. Both use a caller workspace of
  * mq_moe_workspace_size() bytes (256-byte aligned). d % 256 == 0, fe % 256 == 0. */
 MQ_API size_t mq_moe_workspace_size(int64_t tokens, int experts, int topk, int64_t d, int64_t fe);
 MQ_API int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, const float *weights, const uint32_t *gu_wq,

@@ -29,6 +29,13 @@ struct DeviceInfo {
 };
 int device_info(DeviceInfo *out);
 
+namespace gemv {
+// The expert-indirect GEMV of the MoE decode (gemv_q4.cu).
+int gemv_q4_grouped(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const float *x, float *y,
+                    const int32_t *ids, int ngroups, int group_rows, int rows_per_group, int64_t k, int group, int xpg,
+                    cudaStream_t stream);
+}  // namespace gemv
+
 // The grouped expert GEMM (gemm_q4.cu): mode 1 gate|up + SiLU (fp16 out), mode 2 plain (fp32 out).
 int moe_gemm_run(int mode, const uint32_t *wq, const uint16_t *ws, const uint16_t *xs, int64_t pairs, int64_t k,
                  int experts, int64_t rows_per_expert, int group, const int32_t *tiles, const int32_t *ntiles,

@@ -61,7 +61,17 @@ struct Params {
   int slots;    // ring slots per warp (<= kMaxSlots)
   int scales_tma;
   int slot_bytes;
+  // Expert indirection (MoE decode): output tile t reads weight rows ids[t / tpg] * group_rows +
+  // (t % tpg) * 32 ..; with xpg each expert slot t / tpg has its own x vector (staged as token t / tpg).
+  const int32_t *ids;
+  int group_rows, tpg, xpg;
+  int wrows;  // rows of the weight matrix (== n without expert indirection)
 };
+
+// First weight row of output tile `tile` (the rows themselves, or an expert's rows through ids).
+__device__ __forceinline__ int weight_row0(const Params &p, int tile) {
+  return p.ids ? __ldg(p.ids + tile / p.tpg) * p.group_rows + (tile % p.tpg) * 32 : tile * 32;
+}
 
 __device__ __forceinline__ void decode_q4(uint32_t w, uint32_t (&p)[4]) {
   const uint32_t u = w ^ 0x88888888u;
@@ -112,7 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemv_q4_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  const Layout L = layout(p.k, p.batch, NT, p.slots, p.slot_bytes);
+  const Layout L = layout(p.k, p.batch, p.xpg ? p.batch : NT, p.slots, p.slot_bytes);
   const int K = p.k, N = p.n, B = p.batch, S = p.slots;
   const int kc = (K + 127) / 128;
   const int nsteps = kc * 8;
@@ -140,9 +150,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int slot = u % S;
     uint64_t *bar = full + slot;
     uint8_t *dst = ring + slot * p.slot_bytes;
+    const int wrow = weight_row0(p, tile);
     mbar_expect_tx(bar, bytes);
-    tma_load_2d(dst, &wmap, bar, sk * (kSlotK / 8), tile * kRows);
-    if (p.scales_tma) tma_load_2d(dst + kWordBytes, &smap, bar, sk * kScaleHalvesTma, tile * kRows);
+    tma_load_2d(dst, &wmap, bar, sk * (kSlotK / 8), wrow);
+    if (p.scales_tma) tma_load_2d(dst + kWordBytes, &smap, bar, sk * kScaleHalvesTma, wrow);
   };
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(full + s, 1);
@@ -158,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float *red = reinterpret_cast<float *>(smem + L.red);       // [kWarps][32][B]
 
   // Stage x once per CTA: B fragments (fp16 hi/lo, in the decode's slot order) and quad sums.
-  for (int i = threadIdx.x; i < NT * nsteps * 8; i += kThreads) bfrag[i] = make_uint2(0u, 0u);
+  for (int i = threadIdx.x; i < (p.xpg ? B : NT) * nsteps * 8; i += kThreads) bfrag[i] = make_uint2(0u, 0u);
   __syncthreads();
   const int nitems = B * kc * 16;
   for (int base = 0; base < nitems; base += kThreads) {
@@ -218,12 +229,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int qa = 2 * (q & 1);     // first of the two quads whose columns this lane's D holds
   const int pr = phys_row(g);     // physical rows pr, pr + 8, pr + 16, pr + 24 of the tile
   const int spr = K / G;
+  const int BO = p.xpg ? 1 : B;   // output vectors (one per token; one in total for per-expert x)
   const uint2 *bl = bfrag + g;    // this lane's column of the B fragments
   uint32_t u = 0, u_abort = 0;
   bool aborted = false;
 
   for (int r = blockIdx.x; r < p.nrounds; r += gridDim.x) {
     const int tile = r * p.rt + items.rtl;
+    const int tb = p.xpg ? min(tile, p.tiles - 1) / p.tpg : 0;  // x vector of this tile's expert slot
+    const int wrow0 = weight_row0(p, min(tile, p.tiles - 1));
     float acc[NT][2][2];  // [token tile][row tile][row g, row g + 8]
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t][0][0] = acc[t][0][1] = acc[t][1][0] = acc[t][1][1] = 0.f;
@@ -258,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int i0 = (cg * 128 + 32 * qa) / G, i1 = (cg * 128 + 32 * (qa + 1)) / G;
 #pragma unroll
               for (int m = 0; m < 4; ++m) {
-                const int row = min(tile * kRows + pr + 8 * m, N - 1);
+                const int row = p.ids ? wrow0 + pr + 8 * m : min(tile * kRows + pr + 8 * m, N - 1);
                 s0[m] = i0 < spr ? __half2float(p.ws[static_cast<size_t>(row) * spr + i0]) : 0.f;
                 s1[m] = i1 < spr ? __half2float(p.ws[static_cast<size_t>(row) * spr + i1]) : 0.f;
               }
@@ -283,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int s = cg * 8 + 2 * j;
 #pragma unroll
               for (int t = 0; t < NT; ++t) {
-                const uint2 *bf = bl + (static_cast<size_t>(t) * nsteps + s) * 8;
+                const uint2 *bf = bl + (static_cast<size_t>(tb + t) * nsteps + s) * 8;
                 uint2 f0 = make_uint2(0u, 0u), f1 = make_uint2(0u, 0u);
                 if (act) {
                   f0 = bf[0];
@@ -301,9 +315,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
               const int tok = LO ? t : 2 * t + (q >> 1);
-              if (tok < B) {
+              if (tok < (p.xpg ? 1 : B)) {
                 const bool hi = LO ? (q < 2) : true;
-                const float2 xs = *reinterpret_cast<const float2 *>(xsum + tok * kc * 4 + cg * 4 + qa);
+                const float2 xs = *reinterpret_cast<const float2 *>(xsum + (tb + tok) * kc * 4 + cg * 4 + qa);
                 const float x0 = hi ? 8.f * xs.x : 0.f, x1 = hi ? 8.f * xs.y : 0.f;
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
@@ -334,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       const int tok = LO ? t : 2 * t + (q >> 1);
       const bool writer = LO ? (q == 0) : ((q & 1) == 0);
-      if (writer && tok < B) {
+      if (writer && tok < BO) {
 #pragma unroll
         for (int m = 0; m < 4; ++m) {  // rows pr + 8m: (tile h = m / 2, row g or g + 8 = m % 2)
           const float v = acc[t][m >> 1][m & 1];
@@ -345,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               *out = p.add ? *out + v : v;
             }
           } else {
-            red[(items.kw * kRows * p.rt + items.rtl * kRows + pr + 8 * m) * B + tok] = v;
+            red[(items.kw * kRows * p.rt + items.rtl * kRows + pr + 8 * m) * BO + tok] = v;
           }
         }
       }
@@ -353,12 +367,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.ks == 1) continue;
     __syncthreads();
     const int rows = kRows * p.rt;
-    for (int it = threadIdx.x; it < rows * B; it += kThreads) {
-      const int rl = it / B, tok = it % B;
+    for (int it = threadIdx.x; it < rows * BO; it += kThreads) {
+      const int rl = it / BO, tok = it % BO;
       const int row = r * rows + rl;
       if (row < N) {
         float v = 0.f;
-        for (int w = 0; w < p.ks; ++w) v += red[(w * rows + rl) * B + tok];
+        for (int w = 0; w < p.ks; ++w) v += red[(w * rows + rl) * BO + tok];
         float *out = p.y + static_cast<size_t>(tok) * N + row;
         *out = p.add ? *out + v : v;
       }
@@ -380,18 +394,18 @@ int launch(const uint32_t *wq, Params p, cudaStream_t stream, const DeviceInfo &
   p.slot_bytes = ((kWordBytes + (p.scales_tma ? kRows * kScaleHalvesTma * 2 : 0) + 1023) / 1024) * 1024;
   Layout L{};
   for (p.slots = kMaxSlots; p.slots >= 1; --p.slots) {
-    L = layout(p.k, p.batch, NT, p.slots, p.slot_bytes);
+    L = layout(p.k, p.batch, p.xpg ? p.batch : NT, p.slots, p.slot_bytes);
     if (L.total + 1024 <= dev.smem_optin) break;
   }
   const size_t smem = L.total + 1024;
   MQ_REQUIRE(p.slots >= 1 && smem <= dev.smem_optin, MQ_EUNSUPPORTED,
              "mq_gemv_q4: k=%d batch=%d needs %zu B of shared memory (max %zu)", p.k, p.batch, smem, dev.smem_optin);
   CUtensorMap wmap, smap;
-  if (int rc = encode_tmap_2d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.k / 8, p.n, static_cast<uint64_t>(p.k) / 2, 32,
-                              kRows, CU_TENSOR_MAP_SWIZZLE_128B, "mq_gemv_q4 weights"))
+  if (int rc = encode_tmap_2d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.k / 8, p.wrows, static_cast<uint64_t>(p.k) / 2,
+                              32, kRows, CU_TENSOR_MAP_SWIZZLE_128B, "mq_gemv_q4 weights"))
     return rc;
   if (p.scales_tma) {
-    if (int rc = encode_tmap_2d(&smap, p.ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k / G, p.n,
+    if (int rc = encode_tmap_2d(&smap, p.ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k / G, p.wrows,
                                 static_cast<uint64_t>(p.k / G) * 2, kScaleHalvesTma, kRows, CU_TENSOR_MAP_SWIZZLE_NONE,
                                 "mq_gemv_q4 scales"))
       return rc;
@@ -442,6 +456,7 @@ int gemv_q4_small(const uint32_t *wq, const uint16_t *ws, const void *x, int x_d
   p.x_f16 = x_dtype == MQ_F16;
   p.add = add != 0;
   p.tiles = (p.n + kRows - 1) / kRows;
+  p.wrows = p.n;
   switch (group) {
     case 32: return dispatch_nt<32>(wq, p, stream, dev);
     case 64: return dispatch_nt<64>(wq, p, stream, dev);
@@ -449,8 +464,53 @@ int gemv_q4_small(const uint32_t *wq, const uint16_t *ws, const void *x, int x_d
   }
 }
 
+// The expert-indirect GEMV of the MoE decode: y[i * rows_per_group + r] = W[ids[i] * group_rows + r] . x_i
+// for i < ngroups, r < rows_per_group, x_i = x (shared) or x + i * k (xpg). fp32 x.
+int gemv_q4_grouped(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const float *x, float *y,
+                    const int32_t *ids, int ngroups, int group_rows, int rows_per_group, int64_t k, int group, int xpg,
+                    cudaStream_t stream) {
+  DeviceInfo dev;
+  if (int rc = device_info(&dev)) return rc;
+  Params p{};
+  p.ws = reinterpret_cast<const __half *>(ws);
+  p.x = x;
+  p.y = y;
+  p.n = ngroups * rows_per_group;
+  p.k = static_cast<int>(k);
+  p.batch = xpg ? ngroups : 1;
+  p.x_f16 = 0;
+  p.add = 0;
+  p.tiles = p.n / kRows;
+  p.wrows = static_cast<int>(wrows);
+  p.ids = ids;
+  p.group_rows = group_rows;
+  p.tpg = rows_per_group / kRows;
+  p.xpg = xpg;
+  switch (group) {
+    case 32: return launch<32, 1, true>(wq, p, stream, dev);
+    case 64: return launch<64, 1, true>(wq, p, stream, dev);
+    default: return launch<128, 1, true>(wq, p, stream, dev);
+  }
+}
+
 }  // namespace gemv
 }  // namespace mq
+
+extern "C" int mq_moe_gemv_q4(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const float *x, float *y,
+                              const int32_t *ids, int ngroups, int group_rows, int rows_per_group, int64_t k, int group,
+                              int x_per_group, void *stream) {
+  MQ_REQUIRE(wq && ws && x && y && ids, MQ_EINVAL, "mq_moe_gemv_q4: null pointer");
+  MQ_REQUIRE(ngroups >= 1 && ngroups <= 64 && group_rows > 0 && rows_per_group > 0 && rows_per_group <= group_rows,
+             MQ_EINVAL, "mq_moe_gemv_q4: bad expert shape");
+  MQ_REQUIRE(rows_per_group % 32 == 0, MQ_EINVAL, "mq_moe_gemv_q4: rows per expert must be a multiple of 32");
+  MQ_REQUIRE(group == 32 || group == 64 || group == 128, MQ_EINVAL, "mq_moe_gemv_q4: group must be 32, 64 or 128");
+  MQ_REQUIRE(k > 0 && k % 32 == 0 && k % group == 0 && wrows > 0 && wrows < (1LL << 31), MQ_EINVAL,
+             "mq_moe_gemv_q4: bad k or weight rows");
+  MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(x, 16) && mq::aligned(y, 4), MQ_EALIGN,
+             "mq_moe_gemv_q4: wq and x must be 16-byte aligned");
+  return mq::gemv::gemv_q4_grouped(wq, ws, wrows, x, y, ids, ngroups, group_rows, rows_per_group, k, group, x_per_group,
+                                   static_cast<cudaStream_t>(stream));
+}
 
 extern "C" int mq_gemv_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y, int64_t n,
                           int64_t k, int group, int batch, int add, void *stream) {

@@ -304,8 +304,8 @@ inline Work carve(uint8_t *base, int64_t tokens, int experts, int topk, int64_t 
   w.tiles = reinterpret_cast<int32_t *>(take(static_cast<size_t>(w.max_tiles) * 3 * 4));
   w.ntiles = reinterpret_cast<int32_t *>(take(4));
   w.xg = reinterpret_cast<__half *>(take(P * d * 2));
-  w.a = reinterpret_cast<__half *>(take(P * fe * 2));
-  w.z = reinterpret_cast<float *>(take(P * d * 4));
+  w.a = reinterpret_cast<__half *>(take(P * fe * 4));  // fp16 between the grouped GEMMs; fp32 on the decode path
+  w.z = reinterpret_cast<float *>(take(P * (d > 2 * fe ? d : 2 * fe) * 4));
   w.bytes = off;
   return w;
 }
@@ -334,6 +334,20 @@ extern "C" int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, co
   const mq::moe::Work w = mq::moe::carve(static_cast<uint8_t *>(workspace), tokens, experts, topk, d, fe);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t P = tokens * topk;
+  if (tokens == 1 && x_dtype == MQ_F32) {
+    // One token (decode): the streaming GEMV over the selected experts' rows, as moe_gate_up /
+    // moe_down do (moek.mojo:200-223): h = [gate|up]_e x, a = silu(gate) * up, z_k = down_e a_k,
+    // y (+)= sum_k w_k z_k. h lives in the z region (dead by the time z is written).
+    float *h = w.z, *a = reinterpret_cast<float *>(w.a), *z = w.z;
+    if (int rc = mq::gemv::gemv_q4_grouped(gu_wq, gu_ws, experts * 2 * fe, static_cast<const float *>(x), h, ids, topk,
+                                           static_cast<int>(2 * fe), static_cast<int>(2 * fe), d, group, 0, s))
+      return rc;
+    if (int rc = mq_moe_silu_mul(h, a, topk, fe, s)) return rc;
+    if (int rc = mq::gemv::gemv_q4_grouped(dn_wq, dn_ws, experts * d, a, z, ids, topk, static_cast<int>(d),
+                                           static_cast<int>(d), fe, group, 1, s))
+      return rc;
+    return mq_moe_combine(z, nullptr, weights, 1, topk, d, add, y, s);
+  }
   if (int rc = mq_moe_group(ids, tokens, topk, experts, mq::moe::kTileM, w.counts, w.offsets, w.order, w.slot_of, w.tiles,
                             w.ntiles, s))
     return rc;

@@ -22,6 +22,7 @@ SIGNATURES = {
     "mq_moe_gather": (c_int, [c_vp, c_int, c_vp, c_i64, c_int, c_i64, c_vp, c_vp]),
     "mq_moe_gemm_q4": (c_int, [c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_i64, c_int, c_vp, c_vp, c_int, c_int,
                                c_vp, c_vp]),
+    "mq_moe_gemv_q4": (c_int, [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_i64, c_int, c_int, c_vp]),
     "mq_moe_silu_mul": (c_int, [c_vp, c_vp, c_i64, c_i64, c_vp]),
     "mq_moe_combine": (c_int, [c_vp, c_vp, c_vp, c_i64, c_int, c_i64, c_int, c_vp, c_vp]),
     "mq_moe_workspace_size": (c_size, [c_i64, c_int, c_int, c_i64, c_i64]),

@@ -9,7 +9,7 @@ import torch
 from ._lib import MQError, lib
 from .kernels import MQ_F16, MQ_F32, _need, _p, _stream, _WORDS
 
-__all__ = ["p_route", "route", "p_expert_lists", "moe_forward", "TILE_M"]
+__all__ = ["p_route", "route", "p_expert_lists", "moe_gemv_q4", "moe_gate_up", "moe_down", "moe_forward", "TILE_M"]
 
 TILE_M = 64  # tokens per expert work tile of the grouped products
 
@@ -49,6 +49,46 @@ def p_expert_lists(ids, experts, tile=TILE_M):
     lib.call("mq_moe_group", _p(ids), tokens, topk, experts, tile, _p(counts), _p(offsets), _p(order), _p(slot_of),
              _p(tiles), _p(ntiles), _stream())
     return counts, offsets, order, slot_of, tiles, ntiles
+
+
+def moe_gemv_q4(wq, ws, ids, x, y, k, group_rows, rows_per_group=None, group=32, x_per_group=False):
+    """The decode GEMV over selected experts: y[i, r] = W[ids[i] * group_rows + r] . x_i for
+    i < len(ids), r < rows_per_group (default group_rows); x_i = x, or x[i] with x_per_group.
+    wq: int4 words [wrows, k/8]; ws fp16 [wrows, k/group]; x fp32; y fp32 [len(ids), rows_per_group]."""
+    rows_per_group = group_rows if rows_per_group is None else rows_per_group
+    _need(wq, "wq", _WORDS)
+    wrows = wq.numel() * 8 // k
+    _need(ws, "ws", (torch.float16,), wrows * k // group)
+    _need(ids, "ids", (torch.int32,))
+    n = ids.numel()
+    _need(x, "x", (torch.float32,), n * k if x_per_group else k)
+    _need(y, "y", (torch.float32,), n * rows_per_group)
+    lib.call("mq_moe_gemv_q4", _p(wq), _p(ws), wrows, _p(x), _p(y), _p(ids), n, group_rows, rows_per_group, k, group,
+             int(bool(x_per_group)), _stream())
+    return y
+
+
+def moe_gate_up(wq, ws, ids, x, a, d, fe, group=32, h=None):
+    """a[e, j] = silu(gate_e[j] . x) * (up_e[j] . x) for the selected experts ids[e]: moe_gate_up of
+    moek.mojo:200-210 (one token). x fp32 [d]; a fp32 [topk, fe]; h: optional fp32 [topk, 2fe] scratch."""
+    topk = ids.numel()
+    h = torch.empty(topk, 2 * fe, dtype=torch.float32, device=x.device) if h is None else h
+    moe_gemv_q4(wq, ws, ids, x, h, d, 2 * fe, group=group)
+    _need(a, "a", (torch.float32,), topk * fe)
+    lib.call("mq_moe_silu_mul", _p(h), _p(a), topk, fe, _stream())
+    return a
+
+
+def moe_down(wq, ws, ids, weights, a, x, d, fe, group=32, z=None):
+    """x[r] += sum_e weights[e] * W_down[ids[e]][r] . a[e]: moe_down of moek.mojo:213-223 (one token),
+    k in order. a fp32 [topk, fe]; x fp32 [d] (the residual stream); z: optional fp32 [topk, d] scratch."""
+    topk = ids.numel()
+    z = torch.empty(topk, d, dtype=torch.float32, device=x.device) if z is None else z
+    moe_gemv_q4(wq, ws, ids, a, z, fe, d, group=group, x_per_group=True)
+    _need(weights, "weights", (torch.float32,), topk)
+    _need(x, "x", (torch.float32,), d)
+    lib.call("mq_moe_combine", _p(z), None, _p(weights), 1, topk, d, 1, _p(x), _stream())
+    return x
 
 
 def moe_forward(x, ids, weights, gu_wq, gu_ws, dn_wq, dn_ws, y, d, fe, group=32, add=False, workspace=None):

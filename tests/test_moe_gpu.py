@@ -8,6 +8,7 @@ import torch
 
 from conftest import GOLDEN, normwise
 from oracle import moe as omoe
+from oracle import q4 as oq4
 
 import mq
 from mq import synth
@@ -83,3 +84,38 @@ def test_moe_forward_baseline_config(cuda, tokens):
     y = run_forward(cuda, m["x"], ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 2048, 768, 32, add_to=r.copy())
     ref = r + omoe.moe_layer(m["x"], ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 32, 768)
     assert normwise(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("group,x_per_group", [(32, False), (32, True), (64, True), (128, False), (128, True)])
+def test_moe_gemv_matches_oracle(cuda, group, x_per_group):
+    """The expert-indirect decode GEMV: rows of the selected experts only, shared or per-expert x."""
+    rng = np.random.default_rng(group + x_per_group)
+    experts, rows, k, n = 16, 192, 768, 8
+    wq, ws = synth.q4_matrix(rng, experts * rows, k, group)
+    ids = rng.choice(experts, n, replace=False).astype(np.int32)
+    ids[3] = ids[5]  # the same expert twice
+    x = rng.standard_normal((n, k) if x_per_group else (k,)).astype(np.float32)
+    y = torch.full((n, rows), float("nan"), device=cuda)
+    mq.moe_gemv_q4(t(wq, cuda), t(ws, cuda), t(ids, cuda), t(x, cuda), y, k, rows, group=group, x_per_group=x_per_group)
+    torch.cuda.synchronize()
+    assert mq.device_status() == 0
+    w = oq4.dequant(wq, ws, group).astype(np.float64).reshape(experts, rows, k)[ids]
+    xx = np.broadcast_to(np.atleast_2d(x), (n, k)).astype(np.float64)
+    ref = np.einsum("erk,ek->er", w, xx)
+    assert normwise(y.cpu().numpy(), ref) <= TOL
+
+
+def test_moe_gate_up_down_decode(cuda):
+    """moe_gate_up then moe_down on one token (the reference's decode pair) against the layer oracle."""
+    m = synth.moe_layer(seed=3, tokens=1)
+    ids, w = omoe.route(m["logits"], 8)
+    x = t(m["x"][0], cuda)
+    a = torch.empty(8, 768, device=cuda)
+    mq.moe_gate_up(t(m["gu_wq"], cuda), t(m["gu_ws"], cuda), t(ids[0], cuda), x, a, 2048, 768)
+    r = np.random.default_rng(4).standard_normal(2048).astype(np.float32)
+    res = t(r, cuda)
+    mq.moe_down(t(m["dn_wq"], cuda), t(m["dn_ws"], cuda), t(ids[0], cuda), t(w[0], cuda), a, res, 2048, 768)
+    torch.cuda.synchronize()
+    assert mq.device_status() == 0
+    ref = r + omoe.moe_layer(m["x"], ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 32, 768)[0]
+    assert normwise(res.cpu().numpy(), ref) <= TOL
