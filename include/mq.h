@@ -98,6 +98,20 @@ MQ_API int mq_gemm_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int
                       int64_t k, int64_t m, int group, int add, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * mq_gemm_q4 for fp32 x without a caller workspace. This entry point has no counterpart in the
+ * reference. Its fp16 copy of x lives in a fixed 4 MiB buffer inside libmq's own device memory
+ * (m * k <= 2097152 activations; larger calls return MQ_EINVAL), so it allocates nothing: for callers
+ * that cannot allocate device memory, such as a binding that passes only the reference's p_gemm_q4
+ * arguments or a host whose own allocator owns the device. The first call on each device looks the
+ * buffer's address up (cudaGetSymbolAddress) with that device current; make that first call before
+ * any stream capture. Every call on a device shares the one buffer: calls that overlap in time (on
+ * two streams or two host threads) race and must be serialised by the caller. Other arguments,
+ * limits and numerics as mq_gemm_q4.
+ */
+MQ_API int mq_gemm_q4_noalloc(const uint32_t *wq, const uint16_t *ws, const float *x, float *y, int64_t n, int64_t k,
+                              int64_t m, int group, int add, void *stream);
+
+/*
  * Ternary GEMV: y[b][i] = sum_k s[k/128][i] * (code(k, i) - 1) * x[b][k], b < batch <= 4.
  * Replaces packed_linear + packed_reduce and the GEMV part of packed_head
  * (bonsai/kernels/kernels.mojo:283-325,437-448,451-489) as called by qwen3/model.mojo:128-135,170-181.

@@ -28,6 +28,7 @@
 // Every wait on an mbarrier is bounded; on a time-out the kernel records a status code
 // (mq_device_status), stops issuing work, drains what is in flight and frees its TMEM.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -505,6 +506,60 @@ int gemm_q4_run(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dty
   }
 }
 
+// mq_gemm_q4_noalloc keeps its fp16 copy of the fp32 activations in this module's own device memory,
+// for callers that have no device allocator to hand: a binding that passes exactly the reference's
+// p_gemm_q4 arguments (wq, ws, x, y, n, k: no scratch buffer), or a host whose memory manager owns
+// every device allocation. One copy per device, shared by every call on that device.
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // m * k * 2 bytes at most
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of this device's copy of g_noalloc_scratch, looked up once per device (with that
+// device current) and cached.
+int noalloc_scratch(void **out) {
+  static std::mutex mu;
+  static void *cache[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_gemm_q4_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(MQ_EUNSUPPORTED, "mq_gemm_q4_noalloc: device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(MQ_ECUDA, "mq_gemm_q4_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    cache[dev] = p;
+  }
+  *out = cache[dev];
+  return MQ_OK;
+}
+
+int gemm_q4_noalloc_run(const uint32_t *wq, const uint16_t *ws, const float *x, float *y, int64_t n, int64_t k,
+                        int64_t m, int group, int add, cudaStream_t stream) {
+  DeviceInfo dev;
+  if (int rc = device_info(&dev)) return rc;
+  void *scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  // The conversion writes all m * k halves the product reads, so nothing in the scratch needs to start at zero.
+  const int64_t n4 = m * k / 4;
+  const int grid = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(dev.sms) * 8));
+  gemm::f32_to_f16_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const float4 *>(x), static_cast<uint2 *>(scratch), n4);
+  if (int rc = check_launch("mq_gemm_q4_noalloc (fp32 -> fp16)")) return rc;
+  const __half *x16 = static_cast<const __half *>(scratch);
+  gemm::Params p{};
+  p.ws = reinterpret_cast<const __half *>(ws);
+  p.y = y;
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.m = static_cast<int>(m);
+  p.add = add != 0;
+  switch (group) {
+    case 32: return gemm::launch<32>(wq, x16, p, stream, dev);
+    case 64: return gemm::launch<64>(wq, x16, p, stream, dev);
+    default: return gemm::launch<128>(wq, x16, p, stream, dev);
+  }
+}
+
 }  // namespace mq
 
 extern "C" size_t mq_gemm_q4_workspace_size(int64_t m, int64_t k, int x_dtype) {
@@ -524,6 +579,25 @@ extern "C" int mq_gemm_q4(const uint32_t *wq, const uint16_t *ws, const void *x,
              "mq_gemm_q4: wq, ws and x must be 16-byte aligned, y 4-byte aligned");
   return mq::gemm_q4_run(wq, ws, x, x_dtype, y, n, k, m, group, add, workspace, workspace_bytes,
                          static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mq_gemm_q4_noalloc(const uint32_t *wq, const uint16_t *ws, const float *x, float *y, int64_t n,
+                                  int64_t k, int64_t m, int group, int add, void *stream) {
+  MQ_REQUIRE(wq && ws && x && y, MQ_EINVAL, "mq_gemm_q4_noalloc: null pointer");
+  MQ_REQUIRE(n > 0 && k > 0 && m > 0 && n < (1LL << 31) && k <= (1 << 20) && m < (1LL << 24), MQ_EINVAL,
+             "mq_gemm_q4_noalloc: bad shape n=%lld k=%lld m=%lld", static_cast<long long>(n), static_cast<long long>(k),
+             static_cast<long long>(m));
+  MQ_REQUIRE(static_cast<size_t>(m) * static_cast<size_t>(k) * 2 <= mq::kNoAllocScratchBytes, MQ_EINVAL,
+             "mq_gemm_q4_noalloc: m * k = %lld activations need %lld bytes of scratch, above its fixed %zu "
+             "(m * k <= %zu); use mq_gemm_q4 with a workspace",
+             static_cast<long long>(m * k), static_cast<long long>(m * k * 2), mq::kNoAllocScratchBytes,
+             mq::kNoAllocScratchBytes / 2);
+  MQ_REQUIRE(group == 32 || group == 64 || group == 128, MQ_EINVAL,
+             "mq_gemm_q4_noalloc: group must be 32, 64 or 128 (got %d)", group);
+  MQ_REQUIRE(k % 256 == 0, MQ_EINVAL, "mq_gemm_q4_noalloc: k=%lld must be a multiple of 256", static_cast<long long>(k));
+  MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(ws, 16) && mq::aligned(x, 16) && mq::aligned(y, 4), MQ_EALIGN,
+             "mq_gemm_q4_noalloc: wq, ws and x must be 16-byte aligned, y 4-byte aligned");
+  return mq::gemm_q4_noalloc_run(wq, ws, x, y, n, k, m, group, add, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int mq_moe_gemm_q4(int mode, const uint32_t *wq, const uint16_t *ws, const uint16_t *xs, int64_t pairs,
