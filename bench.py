@@ -18,7 +18,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -48,53 +47,73 @@ def q4_bytes(n, k, batch):
 
 
 class Clocks:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples the SM clock and the clock-event reasons of one GPU through NVML (read-only queries)
+    every few milliseconds while the timed region runs."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
-    def __init__(self, index):
-        self.index = index
-        self.proc = None
+    def __init__(self, index, period_s=0.004):
+        self.index, self.period = index, period_s
+        self.samples, self.max_mhz, self.nvml, self.handle = [], None, None, None
+
+    def _open(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        handle = None
+        try:  # the CUDA device's own NVML handle (CUDA and NVML indices can differ)
+            handle = pynvml.nvmlDeviceGetHandleByUUID(f"GPU-{torch.cuda.get_device_properties(self.index).uuid}")
+        except Exception:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        self.nvml, self.handle = pynvml, handle
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+        self.reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+
+    def _sample(self):
+        mhz = self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM)
+        self.samples.append((mhz, int(self.reasons_fn(self.handle))))
+
+    def _run(self):
+        while not self.stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            self.stop.wait(self.period)
 
     def __enter__(self):
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            self._open()
+            self._sample()
+        except Exception:
+            self.handle = None
+            return self
+        self.stop = threading.Event()
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
+        if self.handle is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
             try:
-                out, _ = self.proc.communicate(timeout=10)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+                self._sample()
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
-            f = [v.strip() for v in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for name, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = [m for m, _ in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
+        reasons = sorted(name for name, b in self.REASONS.items() if bits & b)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(sm), "source": "nvml"}
 
 
 def init_dist():
@@ -340,17 +359,24 @@ def run_mq(args):
         torch.distributed.destroy_process_group()
 
 
-def moe_bench(mq, synth, dev, stream, world, rank):
-    """Tokens/s of the MoE layer (routing given) on this rank's experts. With N ranks the experts are
-    split expert-parallel (mq/ep.py); at N = 1 every expert is local."""
-    from oracle import moe as omoe  # routing of the synthetic logits only (ids/weights are inputs here)
+def device_route(mq, logits, dev, topk=8):
+    """Routes synthetic router logits on the device (mq.p_route): the MoE layer's ids and weights."""
+    tl = torch.from_numpy(logits).to(dev)
+    ids = torch.empty(tl.shape[0], topk, dtype=torch.int32, device=dev)
+    w = torch.empty(tl.shape[0], topk, device=dev)
+    mq.p_route(tl, ids, w, topk=topk)
+    return ids, w
 
+
+def moe_bench(mq, synth, dev, stream, world, rank):
+    """Tokens/s of the MoE layer (routing given, computed once on the device) with every expert on
+    this GPU."""
     out = {}
     for tokens in (404, 1):
         m = synth.moe_layer(seed=0, tokens=tokens)
-        ids, w = omoe.route(m["logits"], 8)
         tx = torch.from_numpy(m["x"]).to(dev)
-        tids, tw = torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev)
+        tids, tw = device_route(mq, m["logits"], dev)
+        ids = tids.cpu().numpy()
         gw = [torch.from_numpy(m[k].view(np.int32) if m[k].dtype == np.uint32 else m[k]).to(dev)
               for k in ("gu_wq", "gu_ws", "dn_wq", "dn_ws")]
         wbytes = sum(a.numel() * a.element_size() for a in gw)
@@ -452,7 +478,8 @@ def run_reference(args):
 def profile_case(name, launches):
     """A few launches of one kernel on one workload, for ncu captures (no timing, no JSON line).
     Cases: gemv_lm_head (configs[1] head, batch 1), tgemv_head (configs[4] head), gemm_gate_up
-    (configs[2] 8192x2048, 431 tokens), gemm_decode64_head (configs[1] head, batch 64)."""
+    (configs[2] 8192x2048, 431 tokens), gemm_decode64_head (configs[1] head, batch 64), moe_prefill
+    and moe_decode (configs[3], 404 tokens and 1 token)."""
     import mq
     from mq import synth
 
@@ -483,6 +510,15 @@ def profile_case(name, launches):
         ty = torch.empty(x.shape[0], wq.shape[0], device=dev)
         for _ in range(launches):
             mq.p_gemm_q4(tw, ts, tx, ty, wq.shape[0], 2048, x.shape[0], group=GROUP)
+    elif name in ("moe_prefill", "moe_decode"):
+        tokens = 404 if name == "moe_prefill" else 1
+        m = synth.moe_layer(seed=0, tokens=tokens)
+        t = {k: torch.from_numpy(m[k].view(np.int32) if m[k].dtype == np.uint32 else m[k]).to(dev)
+             for k in ("x", "gu_wq", "gu_ws", "dn_wq", "dn_ws")}
+        tids, tw = device_route(mq, m["logits"], dev)
+        y = torch.zeros(tokens, 2048, device=dev)
+        for _ in range(launches):
+            mq.moe_forward(t["x"], tids, tw, t["gu_wq"], t["gu_ws"], t["dn_wq"], t["dn_ws"], y, 2048, 768, group=32)
     else:
         raise SystemExit(f"unknown profile case {name}")
     torch.cuda.synchronize()
