@@ -29,6 +29,28 @@ struct DeviceInfo {
 };
 int device_info(DeviceInfo *out);
 
+// Launches `kern` so that it may start while the previous kernel on `stream` is still finishing
+// (programmatic dependent launch). Such a kernel runs only set-up that touches no global memory
+// (barriers, TMEM, descriptor prefetch) before griddep_wait(); after it, every write of earlier
+// work on the stream is visible, exactly as with an ordinary launch.
+template <typename... KArgs, typename... Args>
+int launch_overlapped(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char *what,
+                      Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) return fail(MQ_ECUDA, "%s: launch: %s", what, cudaGetErrorString(e));
+  return check_launch(what);
+}
+
 namespace gemv {
 // The expert-indirect GEMV of the MoE decode (gemv_q4.cu).
 int gemv_q4_grouped(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const float *x, float *y,
@@ -72,6 +94,12 @@ enum : int {
   kStatusGemvConsumerWait = 6,
   kStatusGemvDrainWait = 7,
 };
+
+// Waits until the kernels this grid depends on (earlier work on its stream) have completed and
+// their writes are visible; a no-op for an ordinary launch.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel on the stream begin launching (its own griddep_wait still orders its accesses).
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void raise_status(int code) { atomicCAS(&g_status, 0, code); }
 

@@ -122,7 +122,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int t = blockIdx.x;
   int tm = t % p.tiles_m, tn = (t / p.tiles_m) % p.tiles_n, split = t / (p.tiles_m * p.tiles_n);
   int n0 = tn * kBM, m0 = tm * p.bn, mcount = p.m - m0, expert = 0;
+  griddep_launch_dependents();
   if (MODE != kDense) {  // grouped: work tile from the device table
+    griddep_wait();      // the table is written by earlier work on the stream
     const int entry = t / p.tiles_n;
     tn = t % p.tiles_n;
     split = 0;
@@ -153,6 +155,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_d = *tmem_slot;
+  if (MODE == kDense) griddep_wait();  // the set-up above touched no global memory
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------------------------------------------------
@@ -401,8 +404,7 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
     if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_gemm_q4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured = smem;
   }
-  kern<<<tiles * p.splitk, kThreads, smem, stream>>>(wmap, xmap, p);
-  return check_launch("mq_gemm_q4");
+  return launch_overlapped(kern, dim3(tiles * p.splitk), dim3(kThreads), smem, stream, "mq_gemm_q4", wmap, xmap, p);
 }
 
 template <int G, int MODE>
@@ -447,8 +449,8 @@ int launch_grouped(const uint32_t *wq, const __half *ws, const __half *xs, int64
     if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_moe_gemm_q4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured = smem;
   }
-  kern<<<max_tiles * p.tiles_n, kThreads, smem, stream>>>(wmap, xmap, p);
-  return check_launch("mq_moe_gemm_q4");
+  return launch_overlapped(kern, dim3(max_tiles * p.tiles_n), dim3(kThreads), smem, stream, "mq_moe_gemm_q4", wmap, xmap,
+                           p);
 }
 
 }  // namespace gemm

@@ -155,6 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_load_2d(dst, &wmap, bar, sk * (kSlotK / 8), wrow);
     if (p.scales_tma) tma_load_2d(dst + kWordBytes, &smap, bar, sk * kScaleHalvesTma, wrow);
   };
+  griddep_launch_dependents();
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(full + s, 1);
     fence_mbar_init();
@@ -162,6 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.scales_tma) prefetch_tmap(&smap);
   }
   __syncwarp();
+  griddep_wait();  // everything above touched no global memory
   for (int s = 0; s < S; ++s) issue(s);  // loads start before x is staged
 
   uint2 *bfrag = reinterpret_cast<uint2 *>(smem + L.bfrag);  // [NT][nsteps][8]
@@ -430,8 +432,7 @@ int launch(const uint32_t *wq, Params p, cudaStream_t stream, const DeviceInfo &
     configured = smem;
   }
   const int grid = std::min(p.nrounds, dev.sms);
-  kern<<<grid, kThreads, smem, stream>>>(wmap, smap, p);
-  return check_launch("mq_gemv_q4");
+  return launch_overlapped(kern, dim3(grid), dim3(kThreads), smem, stream, "mq_gemv_q4", wmap, smap, p);
 }
 
 template <int G>

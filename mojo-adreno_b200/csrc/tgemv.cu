@@ -132,6 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_load_2d(dst, &wmap, bar, tile * kCols, sk * kWordRows);
     if (p.scales_tma) tma_load_2d(dst + kWordBytes, &smap, bar, tile * kCols, sk * kGroups);
   };
+  griddep_launch_dependents();
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(full + s, 1);
     fence_mbar_init();
@@ -139,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.scales_tma) prefetch_tmap(&smap);
   }
   __syncwarp();
+  griddep_wait();  // everything above touched no global memory
   for (int s = 0; s < S; ++s) issue(s);
 
   uint2 *bfrag = reinterpret_cast<uint2 *>(smem + L.bfrag);  // [kb*4 steps][NB][4]
@@ -338,8 +340,7 @@ int launch_sk(const uint32_t *w, Params p, cudaStream_t stream, const DeviceInfo
     configured = smem;
   }
   const int grid = std::min(p.nrounds, dev.sms);
-  kern<<<grid, kThreads, smem, stream>>>(wmap, smap, p);
-  return check_launch("mq_tgemv");
+  return launch_overlapped(kern, dim3(grid), dim3(kThreads), smem, stream, "mq_tgemv", wmap, smap, p);
 }
 
 template <int NB>
