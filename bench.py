@@ -309,7 +309,8 @@ def run_mq(args):
     del b64_graphs
 
     # ---- secondary: Qwen3-30B-A3B MoE layer: 404-token prefill, 1-token decode
-    moe_res = moe_bench(mq, synth, dev, stream, world, rank)
+    moe_res = moe_bench(mq, synth, dev, stream, world, rank) if world == 1 else \
+        moe_bench_ep(mq, synth, dev, stream, world, rank)
 
     head_bytes = q4_bytes(head["n"], head["k"], batch) * (world if world > 1 else 1)
     achieved = q4_bytes(head["n"], head["k"], batch) / (head_ms * 1e-3) / 1e9
@@ -393,6 +394,49 @@ def moe_bench(mq, synth, dev, stream, world, rank):
                                    "experts_touched": int(len(used)),
                                    "expert_weight_GB/s": round(active_bytes / (ms * 1e-3) / 1e9, 1)}
         del graphs, gws
+    return out
+
+
+def moe_bench_ep(mq, synth, dev, stream, world, rank, steps=30):
+    """Tokens/s of the expert-parallel MoE layer (BASELINE configs[3] at N GPUs): rank r owns experts
+    [r * 128 / N, (r + 1) * 128 / N) and routes its share of the tokens; dispatch and combine are NCCL
+    all-to-alls (mq.ExpertParallelMoE). Timed with CUDA events over `steps` layers, including the
+    host read of the split sizes each layer needs, max over ranks."""
+    d, fe, experts, topk = 2048, 768, 128, 8
+    out = {}
+    for tokens in (404, 1):
+        m = synth.moe_layer(seed=0, tokens=tokens)
+        lo_t, hi_t = shard(tokens, world, rank)
+        lo, hi = mq.expert_range(experts, world, rank)
+        parts = (m["gu_wq"][lo * 2 * fe:hi * 2 * fe], m["gu_ws"][lo * 2 * fe:hi * 2 * fe], m["dn_wq"][lo * d:hi * d],
+                 m["dn_ws"][lo * d:hi * d])
+        gw = [torch.from_numpy(np.ascontiguousarray(a.view(np.int32) if a.dtype == np.uint32 else a)).to(dev)
+              for a in parts]
+        copies = rotating_copies(sum(a.numel() * a.element_size() for a in gw))
+        gws = [gw] + [[a.clone() for a in gw] for _ in range(copies - 1)]
+        layers = [mq.ExpertParallelMoE(*g, d, fe, experts, topk=topk, group=32) for g in gws]
+        tx = torch.from_numpy(np.ascontiguousarray(m["x"][lo_t:hi_t])).to(dev)
+        if hi_t > lo_t:
+            tids, tw = device_route(mq, np.ascontiguousarray(m["logits"][lo_t:hi_t]), dev)
+        else:
+            tids = torch.empty(0, topk, dtype=torch.int32, device=dev)
+            tw = torch.empty(0, topk, device=dev)
+        y = torch.empty(hi_t - lo_t, d, device=dev)
+        for i in range(3):
+            layers[i % copies](tx, tids, tw, y)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            layers[i % copies](tx, tids, tw, y)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+        out[f"tokens_{tokens}"] = {"ms": round(ms, 5), "tokens/s": round(tokens / (ms * 1e-3), 1),
+                                   "parallelism": f"expert-parallel x{world} ({experts // world} experts per GPU), "
+                                                  "NCCL all-to-all dispatch and combine"}
+        del layers, gws
     return out
 
 

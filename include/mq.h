@@ -137,10 +137,20 @@ MQ_API int mq_moe_route(const float *logits, int32_t *ids, float *weights, int64
  * p_expert_items (moek.mojo:432-442, 548-557): counts[e]; offsets[e] (exclusive prefix, offsets[experts]
  * = pairs); order[offsets[e] + r] = the r-th pair t * topk + k routed to e, in increasing pair index;
  * slot_of[pair] = its position in order; tiles[3 * i ..] = (expert, first sorted row, rows <= tile)
- * work items in expert order and *ntiles their count (at most experts + ceil(pairs / tile)). */
+ * work items in expert order and *ntiles their count (at most experts + ceil(pairs / tile)).
+ * A pair whose id is outside [0, experts) is left out (slot_of = -1, the unused tail of order = 0)
+ * and reported through mq_device_status. */
 MQ_API int mq_moe_group(const int32_t *ids, int64_t tokens, int topk, int experts, int tile, int32_t *counts,
                         int32_t *offsets, int32_t *order, int32_t *slot_of, int32_t *tiles, int32_t *ntiles,
                         void *stream);
+
+/* Expert-parallel dispatch plan: experts are split into `world` equal contiguous ranges, range r owned
+ * by rank r. The tokens * topk pairs are grouped stably by owning rank: counts[r], offsets[r]
+ * (offsets[world] = pairs), order[offsets[r] + i] = the i-th pair sent to rank r, slot_of[pair] = its
+ * send position, local_ids[pos] = the pair's expert id within its owner (ids - r * experts / world).
+ * No counterpart kernel in the reference (which runs on one device). */
+MQ_API int mq_ep_plan(const int32_t *ids, int64_t tokens, int topk, int experts, int world, int32_t *counts,
+                      int32_t *offsets, int32_t *order, int32_t *slot_of, int32_t *local_ids, void *stream);
 
 /* xg[s] = fp16(x[order[s] / topk]) for s < pairs: the expert-sorted activation rows (p_gather,
  * lfm2moe/kernels/mk.mojo:164-176). x: [tokens][d] fp32 or fp16; d % 8 == 0. */
@@ -158,7 +168,8 @@ MQ_API int mq_moe_gemm_q4(int mode, const uint32_t *wq, const uint16_t *ws, cons
 
 /* The expert-indirect decode GEMV (moe_gate_up / moe_down's products, moek.mojo:200-223):
  * y[i * rows_per_group + r] = W[ids[i] * group_rows + r] . x_i for i < ngroups, r < rows_per_group,
- * with x_i = x (x_per_group == 0) or x + i * k. W: [wrows][k/8] words; x fp32; rows_per_group % 32 == 0. */
+ * with x_i = x (x_per_group == 0) or x + i * k. W: [wrows][k/8] words; x fp32; rows_per_group % 32 == 0.
+ * An id outside the matrix is reported through mq_device_status (and its rows read as expert 0's). */
 MQ_API int mq_moe_gemv_q4(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const float *x, float *y,
                           const int32_t *ids, int ngroups, int group_rows, int rows_per_group, int64_t k, int group,
                           int x_per_group, void *stream);
@@ -167,7 +178,7 @@ MQ_API int mq_moe_gemv_q4(const uint32_t *wq, const uint16_t *ws, int64_t wrows,
 MQ_API int mq_moe_silu_mul(const float *h, float *a, int64_t rows, int64_t fe, void *stream);
 
 /* y[t][c] (+)= sum_k weights[t][k] * z[slot_of[t * topk + k]][c], k in order (p_moe_sum,
- * moek.mojo:479-488); slot_of NULL means row t * topk + k. z, y 16-byte aligned, d % 4 == 0. */
+ * moek.mojo:479-488); slot_of NULL means row t * topk + k; a negative slot_of adds nothing. z, y 16-byte aligned, d % 4 == 0. */
 MQ_API int mq_moe_combine(const float *z, const int32_t *slot_of, const float *weights, int64_t tokens, int topk,
                           int64_t d, int add, float *y, void *stream);
 

@@ -93,6 +93,7 @@ enum : int {
   kStatusGemvProducerWait = 5,
   kStatusGemvConsumerWait = 6,
   kStatusGemvDrainWait = 7,
+  kStatusMoeBadExpertId = 8,  // an expert id outside [0, experts): the pair was left out
 };
 
 // Waits until the kernels this grid depends on (earlier work on its stream) have completed and

@@ -69,8 +69,15 @@ struct Params {
 };
 
 // First weight row of output tile `tile` (the rows themselves, or an expert's rows through ids).
+// An expert id outside the weight matrix is reported and read as expert 0.
 __device__ __forceinline__ int weight_row0(const Params &p, int tile) {
-  return p.ids ? __ldg(p.ids + tile / p.tpg) * p.group_rows + (tile % p.tpg) * 32 : tile * 32;
+  if (!p.ids) return tile * 32;
+  int e = __ldg(p.ids + tile / p.tpg);
+  if (e < 0 || e >= p.wrows / p.group_rows) {
+    raise_status(kStatusMoeBadExpertId);
+    e = 0;
+  }
+  return e * p.group_rows + (tile % p.tpg) * 32;
 }
 
 __device__ __forceinline__ void decode_q4(uint32_t w, uint32_t (&p)[4]) {

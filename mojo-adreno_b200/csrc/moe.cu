@@ -73,22 +73,37 @@ __global__ void route_kernel(const float *__restrict__ logits, int32_t *__restri
 // most `tile` rows per expert -- p_expert_items' items, over the concatenated lists.
 constexpr int kGroupThreads = 1024;
 
-__global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__restrict__ ids, int pairs, int experts,
-                                                              int tile, int32_t *__restrict__ counts,
+// Pairs are bucketed by ids[i] / div (div = 1: by expert; div = experts per rank: by owning rank,
+// the expert-parallel dispatch order). tiles / ntiles may be null (no work tiles). local, when not
+// null, receives ids[i] - bucket * div at the pair's sorted position.
+__global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__restrict__ ids, int div, int pairs,
+                                                              int experts, int tile, int32_t *__restrict__ counts,
                                                               int32_t *__restrict__ offsets, int32_t *__restrict__ order,
                                                               int32_t *__restrict__ slot_of, int32_t *__restrict__ tiles,
-                                                              int32_t *__restrict__ ntiles) {
+                                                              int32_t *__restrict__ ntiles, int32_t *__restrict__ local) {
   extern __shared__ int32_t sh[];
   int32_t *warp_cnt = sh;                        // [32 warps][experts]
   int32_t *base = warp_cnt + 32 * experts;       // [experts] running start within the expert
   int32_t *start = base + experts;               // [experts + 1] offsets
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const unsigned lt_mask = (1u << lane) - 1u;
+  // Bucket of pair i, or -1 (reported, left out) for an id outside [0, experts * div).
+  auto bucket = [&](int i) {
+    const int id = ids[i];
+    if (id < 0 || id >= experts * div) {
+      raise_status(kStatusMoeBadExpertId);
+      return -1;
+    }
+    return id / div;
+  };
 
   // Pass 1: histogram.
   for (int e = threadIdx.x; e < experts; e += kGroupThreads) base[e] = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < pairs; i += kGroupThreads) atomicAdd(&base[ids[i]], 1);
+  for (int i = threadIdx.x; i < pairs; i += kGroupThreads) {
+    const int b = bucket(i);
+    if (b >= 0) atomicAdd(&base[b], 1);
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     int run = 0, nt = 0;
@@ -97,7 +112,7 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
       const int c = base[e];
       counts[e] = c;
       offsets[e] = run;
-      for (int r = 0; r < c; r += tile) {
+      for (int r = 0; tiles && r < c; r += tile) {
         tiles[3 * nt] = e;
         tiles[3 * nt + 1] = run + r;
         tiles[3 * nt + 2] = min(tile, c - r);
@@ -107,17 +122,23 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
     }
     start[experts] = run;
     offsets[experts] = run;
-    *ntiles = nt;
+    if (ntiles) *ntiles = nt;
   }
   __syncthreads();
   for (int e = threadIdx.x; e < experts; e += kGroupThreads) base[e] = start[e];
+  // Positions past the pairs that were kept (only when ids were left out) point at pair 0, so every
+  // entry of order stays a valid pair index.
+  for (int pos = start[experts] + threadIdx.x; pos < pairs; pos += kGroupThreads) {
+    order[pos] = 0;
+    if (local) local[pos] = 0;
+  }
   __syncthreads();
 
   // Pass 2: positions, chunk by chunk of kGroupThreads pairs (stable: ranks follow pair index).
   for (int c0 = 0; c0 < pairs; c0 += kGroupThreads) {
     const int i = c0 + threadIdx.x;
-    const bool live = i < pairs;
-    const int e = live ? ids[i] : -1;
+    const int e = i < pairs ? bucket(i) : -1;
+    const bool live = e >= 0;
     const unsigned same = __match_any_sync(0xffffffffu, e);
     const int rank_in_warp = __popc(same & lt_mask);
     for (int j = threadIdx.x; j < 32 * experts; j += kGroupThreads) warp_cnt[j] = 0;
@@ -135,10 +156,12 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
       base[ex] = run;
     }
     __syncthreads();
+    if (i < pairs && !live) slot_of[i] = -1;  // left out
     if (live) {
       const int pos = warp_cnt[warp * experts + e] + rank_in_warp;
       order[pos] = i;
       slot_of[i] = pos;
+      if (local) local[pos] = ids[i] - e * div;
     }
     __syncthreads();
   }
@@ -186,6 +209,7 @@ __global__ void combine_kernel(const float *__restrict__ z, const int32_t *__res
     for (int k = 0; k < topk; ++k) {
       const float wk = w[static_cast<size_t>(t) * topk + k];
       const int row = slot_of ? slot_of[static_cast<size_t>(t) * topk + k] : t * topk + k;
+      if (row < 0) continue;  // a pair left out of the grouping (invalid expert id)
       const float4 v = *reinterpret_cast<const float4 *>(z + static_cast<size_t>(row) * d + c);
       acc.x += wk * v.x;
       acc.y += wk * v.y;
@@ -234,8 +258,21 @@ extern "C" int mq_moe_group(const int32_t *ids, int64_t tokens, int topk, int ex
   MQ_REQUIRE(tile >= 1, MQ_EINVAL, "mq_moe_group: tile must be >= 1");
   const size_t smem = (32 * experts + 2 * experts + 1) * sizeof(int32_t);
   mq::moe::group_kernel<<<1, mq::moe::kGroupThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      ids, static_cast<int>(tokens * topk), experts, tile, counts, offsets, order, slot_of, tiles, ntiles);
+      ids, 1, static_cast<int>(tokens * topk), experts, tile, counts, offsets, order, slot_of, tiles, ntiles, nullptr);
   return mq::check_launch("mq_moe_group");
+}
+
+extern "C" int mq_ep_plan(const int32_t *ids, int64_t tokens, int topk, int experts, int world, int32_t *counts,
+                          int32_t *offsets, int32_t *order, int32_t *slot_of, int32_t *local_ids, void *stream) {
+  MQ_REQUIRE(ids && counts && offsets && order && slot_of && local_ids, MQ_EINVAL, "mq_ep_plan: null pointer");
+  MQ_REQUIRE(tokens > 0 && topk >= 1 && tokens * topk < (1 << 30), MQ_EINVAL, "mq_ep_plan: bad tokens / topk");
+  MQ_REQUIRE(world >= 1 && world <= 256 && experts >= world && experts % world == 0, MQ_EINVAL,
+             "mq_ep_plan: experts (%d) must be a positive multiple of world (%d)", experts, world);
+  const size_t smem = (32 * world + 2 * world + 1) * sizeof(int32_t);
+  mq::moe::group_kernel<<<1, mq::moe::kGroupThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      ids, experts / world, static_cast<int>(tokens * topk), world, 1, counts, offsets, order, slot_of, nullptr, nullptr,
+      local_ids);
+  return mq::check_launch("mq_ep_plan");
 }
 
 extern "C" int mq_moe_gather(const void *x, int x_dtype, const int32_t *order, int64_t pairs, int topk, int64_t d,

@@ -9,3 +9,4 @@ no sm_100 device is present.
 from ._lib import MQError, lib, library_path  # noqa: F401
 from .kernels import *  # noqa: F401,F403
 from .moe import *  # noqa: F401,F403
+from .ep import ExpertParallelMoE, expert_range  # noqa: F401

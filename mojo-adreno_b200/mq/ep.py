@@ -1,0 +1,141 @@
+"""Expert-parallel MoE layer over torch.distributed (NCCL over NVLink on a B200 node).
+
+The reference runs the whole qwen3moe layer on one device (qwen3moe/kernels/moek.mojo:432-608). Here
+the 128 experts are split into `world` contiguous ranges: rank r owns experts [r * E / world,
+(r + 1) * E / world) and holds only their rows of the gate|up and down matrices (contiguous slices
+of the reference's layout, qwen3moe/export.py:166-169). Each rank routes its own tokens; one layer
+is then:
+
+  1. plan (device): the rank's tokens * topk (token, slot) pairs grouped stably by owning rank
+     (mq_ep_plan), with the expert id local to the owner.
+  2. dispatch: counts, then fp16 activation rows and local expert ids, all-to-all.
+  3. the owner runs its experts on the rows it received (mq_moe_forward with topk = 1, weight 1).
+  4. combine: the fp32 expert outputs return all-to-all in the order they were sent, and the home
+     rank sums them per token with the routing weights in slot order (mq_moe_combine), as p_moe_sum
+     does (moek.mojo:479-488).
+
+Every rank takes the same collective steps in the same order, also when it sends or receives no
+rows. The split sizes are read on the host (one small device-to-host copy per layer), which the
+variable-size all-to-all needs.
+"""
+import torch
+import torch.distributed as dist
+
+from ._lib import MQError, lib
+from .kernels import MQ_F16, MQ_F32, _need, _p, _stream, _WORDS
+from .moe import TILE_M  # noqa: F401  (same grouped-product tile as the one-device layer)
+
+__all__ = ["ExpertParallelMoE", "expert_range"]
+
+
+def expert_range(experts, world, rank):
+    """[first, last) experts owned by `rank`."""
+    if experts % world:
+        raise MQError(-1, f"experts ({experts}) must be a multiple of world ({world})")
+    per = experts // world
+    return rank * per, (rank + 1) * per
+
+
+class DeviceOps:
+    """The layer's device steps, each one libmq entry point on the current CUDA stream."""
+
+    def plan(self, ids, tokens, topk, experts, world):
+        dev = ids.device
+        pairs = tokens * topk
+        counts = torch.empty(world, dtype=torch.int32, device=dev)
+        offsets = torch.empty(world + 1, dtype=torch.int32, device=dev)
+        order = torch.empty(pairs, dtype=torch.int32, device=dev)
+        slot_of = torch.empty(pairs, dtype=torch.int32, device=dev)
+        local = torch.empty(pairs, dtype=torch.int32, device=dev)
+        lib.call("mq_ep_plan", _p(ids), tokens, topk, experts, world, _p(counts), _p(offsets), _p(order), _p(slot_of),
+                 _p(local), _stream())
+        return counts, order, slot_of, local
+
+    def gather(self, x, order, topk, d):
+        pairs = order.numel()
+        xg = torch.empty(pairs, d, dtype=torch.float16, device=x.device)
+        lib.call("mq_moe_gather", _p(x), MQ_F16 if x.dtype == torch.float16 else MQ_F32, _p(order), pairs, topk, d,
+                 _p(xg), _stream())
+        return xg
+
+    def experts(self, rows, local_ids, gu_wq, gu_ws, dn_wq, dn_ws, d, fe, group):
+        from .moe import moe_forward
+
+        r = rows.shape[0]
+        out = torch.empty(r, d, dtype=torch.float32, device=rows.device)
+        ones = torch.ones(r, dtype=torch.float32, device=rows.device)
+        moe_forward(rows, local_ids, ones, gu_wq, gu_ws, dn_wq, dn_ws, out, d, fe, group=group)
+        return out
+
+    def combine(self, ret, slot_of, weights, tokens, topk, d, add, y):
+        lib.call("mq_moe_combine", _p(ret), _p(slot_of), _p(weights), tokens, topk, d, int(bool(add)), _p(y), _stream())
+        return y
+
+
+class ExpertParallelMoE:
+    """One rank's share of an expert-parallel MoE layer.
+
+    gu_wq / gu_ws / dn_wq / dn_ws hold only this rank's experts (expert_range): gate|up words
+    [E_local * 2fe, d/8], down [E_local * d, fe/8], fp16 scales per `group`. `experts` is the
+    layer's total. forward(x, ids, weights, y) takes this rank's tokens: x [T, d] fp32 or fp16, ids
+    int32 and weights fp32 [T, topk] from the router, and writes (or adds into) y fp32 [T, d].
+    """
+
+    def __init__(self, gu_wq, gu_ws, dn_wq, dn_ws, d, fe, experts, topk=8, group=32, pg=None, ops=None):
+        self.pg = pg
+        self.world = dist.get_world_size(pg) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(pg) if dist.is_initialized() else 0
+        self.first, self.last = expert_range(experts, self.world, self.rank)
+        self.d, self.fe, self.experts, self.topk, self.group = d, fe, experts, topk, group
+        local = self.last - self.first
+        self.ops = ops if ops is not None else DeviceOps()
+        if ops is None:
+            _need(gu_wq, "gu_wq", _WORDS, local * 2 * fe * d // 8)
+            _need(gu_ws, "gu_ws", (torch.float16,), local * 2 * fe * d // group)
+            _need(dn_wq, "dn_wq", _WORDS, local * d * fe // 8)
+            _need(dn_ws, "dn_ws", (torch.float16,), local * d * fe // group)
+        self.w = (gu_wq, gu_ws, dn_wq, dn_ws)
+
+    def _a2a(self, out, inp, out_splits, in_splits):
+        if self.world == 1:
+            out.copy_(inp)
+        else:
+            dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.pg)
+        return out
+
+    def forward(self, x, ids, weights, y, add=False):
+        d, topk = self.d, self.topk
+        tokens = x.shape[0]
+        if ids.numel() != tokens * topk or weights.numel() != tokens * topk:
+            raise MQError(-1, f"ids / weights must hold tokens * topk = {tokens * topk} entries")
+        # 1. plan, and the rows to send, in send order (a rank without tokens still joins every exchange)
+        if tokens > 0:
+            counts, order, slot_of, local = self.ops.plan(ids, tokens, topk, self.experts, self.world)
+            send = self.ops.gather(x, order, topk, d)
+        else:
+            counts = torch.zeros(self.world, dtype=torch.int32, device=x.device)
+            slot_of = local = torch.empty(0, dtype=torch.int32, device=x.device)
+            send = torch.empty(0, d, dtype=torch.float16, device=x.device)
+        # 2. dispatch: counts first (the receivers' split sizes), then rows and local expert ids
+        recv_counts = torch.empty_like(counts)
+        self._a2a(recv_counts, counts, [1] * self.world, [1] * self.world)
+        both = torch.cat([counts, recv_counts]).cpu().tolist()
+        send_splits, recv_splits = both[:self.world], both[self.world:]
+        r, sent = sum(recv_splits), sum(send_splits)  # sent < tokens * topk only if ids were out of range
+        rows = torch.empty(r, d, dtype=send.dtype, device=send.device)
+        self._a2a(rows, send[:sent], recv_splits, send_splits)
+        rids = torch.empty(r, dtype=torch.int32, device=local.device)
+        self._a2a(rids, local[:sent], recv_splits, send_splits)
+        # 3. this rank's experts on the rows it received
+        if r > 0:
+            out = self.ops.experts(rows, rids, *self.w, d, self.fe, self.group)
+        else:
+            out = torch.empty(0, d, dtype=torch.float32, device=send.device)
+        # 4. outputs back in send order, then the weighted per-token sum in slot order
+        ret = torch.empty(sent, d, dtype=torch.float32, device=send.device)
+        self._a2a(ret, out, send_splits, recv_splits)
+        if tokens == 0:
+            return y
+        return self.ops.combine(ret, slot_of, weights, tokens, topk, d, add, y)
+
+    __call__ = forward

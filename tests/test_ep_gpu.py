@@ -1,0 +1,73 @@
+"""Expert-parallel MoE on the GPU: the dispatch plan bit-exact against the oracle, the layer at
+world 1 through the device steps, and (with 2 visible GPUs) 2 ranks over NCCL."""
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import normwise
+from oracle import moe as omoe
+from test_ep_cpu import OracleOps
+
+import mq
+from mq import synth
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("tokens,experts,topk,world", [(404, 128, 8, 8), (1, 128, 8, 2), (300, 60, 6, 4), (5, 8, 3, 1)])
+def test_ep_plan_matches_oracle(cuda, tokens, experts, topk, world):
+    rng = np.random.default_rng(tokens + world)
+    ids = np.stack([rng.choice(experts, topk, replace=False) for _ in range(tokens)]).astype(np.int32)
+    tids = torch.from_numpy(ids).to(cuda)
+    counts, order, slot_of, local = mq.ep.DeviceOps().plan(tids, tokens, topk, experts, world)
+    torch.cuda.synchronize()
+    rc, ro, rs, rl = OracleOps().plan(torch.from_numpy(ids), tokens, topk, experts, world)
+    for got, want in ((counts, rc), (order, ro), (slot_of, rs), (local, rl)):
+        np.testing.assert_array_equal(got.cpu().numpy(), want.numpy())
+    assert mq.device_status() == 0
+
+
+def test_ep_plan_reports_out_of_range_ids(cuda):
+    """An expert id past the layer is reported through the device status and left out of the plan."""
+    ids = torch.tensor([[0, 9], [3, 1]], dtype=torch.int32, device=cuda)
+    counts, order, slot_of, local = mq.ep.DeviceOps().plan(ids, 2, 2, 8, 2)
+    torch.cuda.synchronize()
+    assert mq.device_status() == 8
+    assert counts.cpu().tolist() == [3, 0]
+    assert order.cpu().tolist()[:3] == [0, 2, 3]
+
+
+def test_ep_single_rank_device_path(cuda):
+    m = synth.moe_layer(seed=2, tokens=37)
+    ids, w = omoe.route(m["logits"], 8)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a.view(np.int32) if a.dtype == np.uint32 else a)).to(cuda)
+    moe = mq.ExpertParallelMoE(t(m["gu_wq"]), t(m["gu_ws"]), t(m["dn_wq"]), t(m["dn_ws"]), 2048, 768, 128)
+    y = torch.full((37, 2048), float("nan"), device=cuda)
+    moe(t(m["x"]), t(ids), t(w), y)
+    torch.cuda.synchronize()
+    assert mq.device_status() == 0
+    ref = omoe.moe_layer(m["x"], ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 32, 768)
+    assert normwise(y.cpu().numpy(), ref) <= 1e-3
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("tokens", ["24,17", "0,9"])
+def test_expert_parallel_two_gpus(cuda, tokens):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    worker = os.path.join(os.path.dirname(os.path.abspath(__file__)), "ep_gpu_worker.py")
+    env = dict(os.environ, EP_TOKENS=tokens, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "60", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(_port()), worker]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert r.returncode == 0, (r.stdout + r.stderr)[-4000:]
