@@ -48,6 +48,11 @@ extern "C" {
 /* Activation dtypes. */
 #define MQ_F32 0
 #define MQ_F16 1
+#define MQ_BF16 2 /* weights for the packers only */
+
+/* Quantisation methods of mq_quantize_q4. */
+#define MQ_Q4_MAX7 0   /* scale = fp16(max|w| / 7) */
+#define MQ_Q4_SEARCH 1 /* scale searched over max|w| / d, d = 6.5 .. 9 */
 
 /* The message of the last failure on this thread ("" when none). */
 MQ_API const char *mq_last_error(void);
@@ -191,6 +196,31 @@ MQ_API int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, const 
                           const uint16_t *gu_ws, const uint32_t *dn_wq, const uint16_t *dn_ws, float *y, int64_t tokens,
                           int experts, int topk, int64_t d, int64_t fe, int group, int add, void *workspace,
                           size_t workspace_bytes, void *stream);
+
+/* ---- packers: the byte layouts above, produced on the device -------------------------------------- */
+
+/* w [n][k] (fp32, fp16 or bf16 bits) -> int4 words wq [n][k/8] and fp16 scales ws [n][k/group].
+ * MQ_Q4_MAX7 replaces quantize4 (llama/run.py:56-70) and st2bin's q4 (llama/st2bin.c:54-70): values
+ * rounded to fp16 first, scale fp16(max|w| / 7), q = clip(rint(w / scale), -8, 7). MQ_Q4_SEARCH
+ * replaces qwen3moe/convert.c:124-157 (values used as given; scale = the first of fp16(max|w| / d),
+ * d = 6.5, 6.75, .., 9, with the least fp32 squared error). Bytes equal the reference converters'. */
+MQ_API int mq_quantize_q4(const void *w, int w_dtype, int64_t n, int64_t k, int group, int method, uint32_t *wq,
+                          uint16_t *ws, void *stream);
+
+/* GGUF Q4_0 blocks (18 bytes each: fp16 d, 16 bytes of nibbles) -> 4 words and one fp16 scale per
+ * block, G = 32 (lfm2/convert.c:58-71). A row of a [rows][cols] matrix is cols / 32 consecutive blocks. */
+MQ_API int mq_q4_0_to_words(const uint8_t *blocks, int64_t nblocks, uint32_t *wq, uint16_t *ws, void *stream);
+
+/* MLX 2-bit rows (codes [n][k/16], scales and biases [n][k/128] fp16) -> the ternary GEMV's transposed
+ * w [k/16][n] and s [k/128][n] (qwen3/convert.cpp:39-74). With biases, every group must be ternary
+ * (bias == -scale) or MQ_EINVAL "not ternary" is returned and nothing is written; that check
+ * synchronises `stream`. biases may be NULL (no check). */
+MQ_API int mq_pack_ternary(const uint32_t *codes, const uint16_t *scales, const uint16_t *biases, int64_t n, int64_t k,
+                           uint32_t *w, uint16_t *s, void *stream);
+
+/* q[i] = fp16 pair (x[2i], x[2i+1]) (pack_half, qwen3/kernels/qwen3k.mojo:17-20,45-48): fp32
+ * activations -> the ternary GEMV's x. n even. */
+MQ_API int mq_pack_half(const float *x, uint32_t *q, int64_t n, void *stream);
 
 #ifdef __cplusplus
 }

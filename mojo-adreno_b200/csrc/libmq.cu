@@ -8,3 +8,4 @@
 #include "tgemv.cu"
 #include "gemm_q4.cu"
 #include "moe.cu"
+#include "pack.cu"

@@ -10,3 +10,4 @@ from ._lib import MQError, lib, library_path  # noqa: F401
 from .kernels import *  # noqa: F401,F403
 from .moe import *  # noqa: F401,F403
 from .ep import ExpertParallelMoE, expert_range  # noqa: F401
+from .pack import *  # noqa: F401,F403

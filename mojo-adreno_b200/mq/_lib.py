@@ -30,6 +30,10 @@ SIGNATURES = {
     "mq_moe_workspace_size": (c_size, [c_i64, c_int, c_int, c_i64, c_i64]),
     "mq_moe_forward": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_int, c_int, c_i64, c_i64,
                                c_int, c_int, c_vp, c_size, c_vp]),
+    "mq_quantize_q4": (c_int, [c_vp, c_int, c_i64, c_i64, c_int, c_int, c_vp, c_vp, c_vp]),
+    "mq_q4_0_to_words": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp]),
+    "mq_pack_ternary": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp]),
+    "mq_pack_half": (c_int, [c_vp, c_vp, c_i64, c_vp]),
 }
 
 

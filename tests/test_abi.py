@@ -67,6 +67,25 @@ def test_tgemv_rejects_bad_arguments_before_launch():
     assert rc == -1 and "batch" in msg
 
 
+def test_packers_and_ep_plan_reject_bad_arguments_before_launch():
+    P = ctypes.c_void_p
+    ok = P(1 << 20)
+    rc, msg = _status("mq_quantize_q4", ok, 0, 4, 256, 48, 0, ok, ok, None)
+    assert rc == -1 and "group" in msg
+    rc, msg = _status("mq_quantize_q4", ok, 5, 4, 256, 32, 0, ok, ok, None)
+    assert rc == -1 and "w_dtype" in msg
+    rc, msg = _status("mq_quantize_q4", ok, 0, 4, 256, 32, 2, ok, ok, None)
+    assert rc == -1 and "method" in msg
+    rc, msg = _status("mq_q4_0_to_words", P((1 << 20) + 1), 4, ok, ok, None)
+    assert rc == -2 and "aligned" in msg
+    rc, msg = _status("mq_pack_ternary", ok, ok, None, 4, 200, ok, ok, None)
+    assert rc == -1 and "128" in msg
+    rc, msg = _status("mq_pack_half", ok, ok, 7, None)
+    assert rc == -1 and "even" in msg
+    rc, msg = _status("mq_ep_plan", ok, 4, 8, 128, 3, ok, ok, ok, ok, ok, None)
+    assert rc == -1 and "multiple of world" in msg
+
+
 def test_python_ops_refuse_cpu_tensors():
     import torch
 
