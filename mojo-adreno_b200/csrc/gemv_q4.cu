@@ -9,26 +9,21 @@
 //  * Streaming. Each of 16 warps streams its own 32-row x 256-k weight tiles (4 KB, one TMA box of
 //    32 rows x 128 bytes with the 128-byte swizzle) and their fp16 scales from HBM into a private
 //    2-slot shared-memory ring (cp.async.bulk.tensor), refilling a slot as soon as it is consumed:
-//    no hand-off between warps. Persistent CTAs, one per SM, 160 KB of ring per SM. (Sweeping
-//    warps x slots over 8x4, 12x3, 16x1, 16x2, 20x2 and 24x1 on B200 put 16x2 first.)
-//  * Issue budget. At ~6.5 TB/s an SM must retire ~46 weights per clock out of 128 issued lane
-//    instructions. The warp-level tensor op mma.m16n8k16 (fp16 in, fp32 accumulate) does the
-//    multiply-add; a warp covers 32 rows (two m16 tiles) so every activation-fragment, x-sum and
-//    address computation serves twice the weights, and the two tiles give four independent
-//    accumulator chains.
-//  * Decode. A nibble pair masked straight into the mantissa bits of an fp16x2 register is an
-//    exact fp16 subnormal: (u & 0x000F000F) holds u_lo * 2^-24 | u_hi * 2^-24 and
-//    (u & 0x00F000F0) holds 16u * 2^-24 (still below the 2^-14 normal threshold), where
-//    u = nib ^ 8 = value + 8 in 0..15 (offset binary). Per 32-bit word one XOR, one shift and four
-//    ANDs give all eight weights exactly. The factors 2^-24 (and 16) are undone on the activation
-//    side (x/16 in the matching B slots) and in the fp32 epilogue, and the offset is removed with
-//    the precomputed sum of x: sum (u - 8) x = sum u x - 8 sum x.
-//  * Exact per-group scales. Lanes of a quad (lane % 4 == q) read 16 consecutive bytes of a row
-//    (32 weights = one scale group for G=32). The B fragment puts quad q's slots of x in column q
-//    only, so D column q holds quad q's dot product alone and the fp32 epilogue applies each
-//    group's scale to its own partial sum, as the reference does.
-//  * fp32 x fidelity. Columns 4..7 carry the fp16 residual x - fp16(x) (batch <= 2), so products
-//    see ~22 bits of x; the weights are exact integers; accumulation is fp32.
+//    no hand-off between warps. Persistent CTAs, one per SM.
+//  * Issue budget. At ~6.5 TB/s an SM must retire ~46 weights per clock, so the instructions per
+//    packed word decide the speed. The products run on the warp-level int8 tensor op
+//    mma.m16n8k32 (s8 x s8 -> s32, exact): a stored nibble is the 4-bit two's complement of its
+//    value, so a nibble masked into the high half of a byte is the int8 16 * value. Per 32-bit word
+//    (w << 4) & 0xF0F0F0F0 and w & 0xF0F0F0F0 give the even and the odd elements: three integer
+//    operations for eight weights, no offset term. One mma covers two words per lane.
+//  * Activations. x is staged once per CTA as 15-bit fixed point per 32-k group (scale
+//    max|x| / 32512), split into two int8 limbs hi * 256 + lo (balanced, both in range); the
+//    products are exact integers, and the fp32 epilogue applies scale_x * scale_w / 16 per group.
+//    The x quantisation step is 1/65024 of the group's largest |x|.
+//  * Exact per-group scales. The four lanes of a quad (lane % 4 == q) read 16 consecutive bytes of
+//    a row (32 weights = one G=32 group). The B fragment puts quad q's x limbs in columns 2q (hi)
+//    and 2q + 1 (lo) only, so the lane that owns columns 2q, 2q + 1 holds exactly its own group's
+//    two limb sums and combines them without a shuffle.
 //  * Bank conflicts. The 128-byte TMA swizzle XORs a row's 16-byte chunk index with row % 8; mma row
 //    g reads physical row (g >> 1) | (g & 1) << 2, which puts the 8 lanes of every shared-memory
 //    phase on 8 different chunks.
@@ -48,12 +43,13 @@ constexpr int kRows = 32;     // rows of a tile: two m16 tiles
 constexpr int kSlotK = 256;   // k of a slot: 32 words = one 128-byte swizzle row
 constexpr int kWordBytes = kRows * 128;
 constexpr int kScaleHalvesTma = 8;  // a TMA-loaded scale row: 8 halves (16 bytes), G = 32 only
+constexpr float kLimbMax = 32512.f;  // 127 * 256: |x| maps to at most this, so both limbs fit in int8
 
 struct Params {
   const __half *ws;  // scales in global memory (read directly when they are not TMA-loaded)
   const void *x;
   float *y;
-  int n, k, batch, x_f16, add;
+  int n, k, batch, x_f16, add;  // batch: staged x vectors (tokens, or expert slots with xpg)
   int ks;       // warps that split a tile's K range (1 = no reduction between warps)
   int rt;       // tiles per round (rt * ks == kWarps)
   int tiles;    // ceil(n / 32)
@@ -80,23 +76,16 @@ __device__ __forceinline__ int weight_row0(const Params &p, int tile) {
   return e * p.group_rows + (tile % p.tpg) * 32;
 }
 
-__device__ __forceinline__ void decode_q4(uint32_t w, uint32_t (&p)[4]) {
-  const uint32_t u = w ^ 0x88888888u;
-  p[0] = u & 0x000F000Fu;  // nibbles 0 | 4, factor 1
-  p[1] = u & 0x00F000F0u;  // nibbles 1 | 5, factor 16
-  const uint32_t v = u >> 8;
-  p[2] = v & 0x000F000Fu;  // nibbles 2 | 6, factor 1
-  p[3] = v & 0x00F000F0u;  // nibbles 3 | 7, factor 16
-}
-
 __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
 
 // Physical row (within 8) that mma row g reads: keeps the 8 lanes of a phase on distinct chunks.
 __device__ __forceinline__ int phys_row(int g) { return (g >> 1) | ((g & 1) << 2); }
 
-// Shared-memory layout (byte offsets from a 1024-aligned base).
+// Shared-memory layout (byte offsets from a 1024-aligned base): the weight rings, the staged x as
+// mma B fragments [nt][kc * 4 steps][8 columns] (uint2 each), the x scales [nt][kc * 4 groups], the
+// K-split partials and the ring barriers.
 struct Layout {
-  uint32_t slots, bfrag, xsum, red, bars, total;
+  uint32_t slots, bfrag, xs, red, bars, total;
 };
 
 __host__ __device__ inline Layout layout(int k, int batch, int nt, int slots, int slot_bytes) {
@@ -104,11 +93,16 @@ __host__ __device__ inline Layout layout(int k, int batch, int nt, int slots, in
   const int kc = (k + 127) / 128;
   L.slots = 0;
   L.bfrag = kWarps * slots * slot_bytes;
-  L.xsum = L.bfrag + nt * kc * 8 * 8 * 8;
-  L.red = L.xsum + batch * kc * 4 * 4;
+  L.xs = L.bfrag + nt * kc * 4 * 8 * 8;
+  L.red = (L.xs + nt * kc * 4 * 4 + 15) / 16 * 16;
   L.bars = (L.red + kWarps * kRows * batch * 4 + 7) / 8 * 8;
   L.total = L.bars + kWarps * kMaxSlots * 8;
   return L;
+}
+
+__device__ __forceinline__ uint32_t pack_bytes(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 255u) | (static_cast<uint32_t>(b) & 255u) << 8 |
+         (static_cast<uint32_t>(c) & 255u) << 16 | (static_cast<uint32_t>(d) & 255u) << 24;
 }
 
 // The work of one warp, as a sequence of (tile, slot of K) items: round j of this CTA covers
@@ -124,15 +118,16 @@ struct Items {
   }
 };
 
-template <int G, int NT, bool LO>
+template <int G, int NT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_q4_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  const Layout L = layout(p.k, p.batch, p.xpg ? p.batch : NT, p.slots, p.slot_bytes);
   const int K = p.k, N = p.n, B = p.batch, S = p.slots;
+  const int nt = p.xpg ? B : NT;  // x vectors staged
+  const Layout L = layout(K, B, nt, S, p.slot_bytes);
   const int kc = (K + 127) / 128;
-  const int nsteps = kc * 8;
+  const int nsteps = kc * 4;
   const int nslotk = (K + kSlotK - 1) / kSlotK;
   const int spw = (nslotk + p.ks - 1) / p.ks;  // K slots per warp per round
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -173,12 +168,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   griddep_wait();  // everything above touched no global memory
   for (int s = 0; s < S; ++s) issue(s);  // loads start before x is staged
 
-  uint2 *bfrag = reinterpret_cast<uint2 *>(smem + L.bfrag);  // [NT][nsteps][8]
-  float *xsum = reinterpret_cast<float *>(smem + L.xsum);     // [B][kc*4]
+  uint2 *bfrag = reinterpret_cast<uint2 *>(smem + L.bfrag);  // [nt][nsteps][8 columns]
+  float *xs = reinterpret_cast<float *>(smem + L.xs);         // [nt][kc * 4]
   float *red = reinterpret_cast<float *>(smem + L.red);       // [kWarps][32][B]
 
-  // Stage x once per CTA: B fragments (fp16 hi/lo, in the decode's slot order) and quad sums.
-  for (int i = threadIdx.x; i < (p.xpg ? B : NT) * nsteps * 8; i += kThreads) bfrag[i] = make_uint2(0u, 0u);
+  // Stage x once per CTA. Item (t, c, q, j) = the 8 values of word j of quad q in 128-k chunk c of
+  // vector t; the 4 items of a quad (one 32-k group) are 4 consecutive lanes, which share its scale.
+  for (int i = threadIdx.x; i < nt * nsteps * 8; i += kThreads) bfrag[i] = make_uint2(0u, 0u);
+  for (int i = threadIdx.x; i < nt * kc * 4; i += kThreads) xs[i] = 0.f;
   __syncthreads();
   const int nitems = B * kc * 16;
   for (int base = 0; base < nitems; base += kThreads) {
@@ -207,39 +204,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int e = 0; e < 8; ++e) xv[e] = 0.f;
     }
-    float sum = 0.f;
+    float m = 0.f;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sum += xv[e];
-    // Quad sums: the 4 words of a quad are 4 consecutive items in lanes 4m..4m+3.
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(xv[e]));
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (!live) continue;
-    if (j == 0) xsum[t * kc * 4 + c * 4 + q] = sum;
-    float hv[8], lv[8];
+    const float inv = m > 0.f ? kLimbMax / m : 0.f;
+    if (j == 0) xs[(t * kc + c) * 4 + q] = m / kLimbMax * (1.f / 16.f);  // 1/16: weights enter as 16 * value
+    int hi[8], lo[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float xs = (e & 1) ? xv[e] * 0.0625f : xv[e];  // odd nibbles carry a factor 16
-      hv[e] = __half2float(__float2half_rn(xs));
-      lv[e] = xs - hv[e];
+      const int v = static_cast<int>(rintf(xv[e] * inv));
+      hi[e] = (v + 128) >> 8;
+      lo[e] = v - (hi[e] << 8);
     }
-    const int tile = LO ? t : t / 2, col = LO ? q : 4 * (t % 2) + q;
-    uint2 *dst = bfrag + (static_cast<size_t>(tile) * nsteps + c * 8 + 2 * j) * 8;
-    dst[col] = make_uint2(pack_half2(hv[0], hv[4]), pack_half2(hv[1], hv[5]));
-    dst[8 + col] = make_uint2(pack_half2(hv[2], hv[6]), pack_half2(hv[3], hv[7]));
-    if (LO) {
-      dst[4 + col] = make_uint2(pack_half2(lv[0], lv[4]), pack_half2(lv[1], lv[5]));
-      dst[8 + 4 + col] = make_uint2(pack_half2(lv[2], lv[6]), pack_half2(lv[3], lv[7]));
-    }
+    uint2 *dst = bfrag + (static_cast<size_t>(t) * nsteps + c * 4 + j) * 8;
+    dst[2 * q] = make_uint2(pack_bytes(hi[0], hi[2], hi[4], hi[6]), pack_bytes(hi[1], hi[3], hi[5], hi[7]));
+    dst[2 * q + 1] = make_uint2(pack_bytes(lo[0], lo[2], lo[4], lo[6]), pack_bytes(lo[1], lo[3], lo[5], lo[7]));
   }
   __syncthreads();
 
   const int g = lane >> 2, q = lane & 3;
-  const bool act = q == (g & 3);  // lanes whose B fragment is non-zero
-  const int qa = 2 * (q & 1);     // first of the two quads whose columns this lane's D holds
-  const int pr = phys_row(g);     // physical rows pr, pr + 8, pr + 16, pr + 24 of the tile
+  const bool act = q == (g >> 1);  // lanes whose B fragment is non-zero (column g belongs to quad g / 2)
+  const int pr = phys_row(g);      // physical rows pr, pr + 8, pr + 16, pr + 24 of the tile
   const int spr = K / G;
-  const int BO = p.xpg ? 1 : B;   // output vectors (one per token; one in total for per-expert x)
-  const uint2 *bl = bfrag + g;    // this lane's column of the B fragments
+  const int BO = p.xpg ? 1 : B;    // output vectors (one per token; one in total for per-expert x)
+  const uint2 *bl = bfrag + g;     // this lane's column of the B fragments
+  constexpr uint32_t kHigh = 0xF0F0F0F0u;
   uint32_t u = 0, u_abort = 0;
   bool aborted = false;
 
@@ -247,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tile = r * p.rt + items.rtl;
     const int tb = p.xpg ? min(tile, p.tiles - 1) / p.tpg : 0;  // x vector of this tile's expert slot
     const int wrow0 = weight_row0(p, min(tile, p.tiles - 1));
-    float acc[NT][2][2];  // [token tile][row tile][row g, row g + 8]
+    float acc[NT][2][2];  // [token][row tile][row g, row g + 8], this lane's group
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t][0][0] = acc[t][0][1] = acc[t][1][0] = acc[t][1][1] = 0.f;
     if (tile < p.tiles) {
@@ -267,74 +259,51 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int cg = sk * 2 + c;  // global 128-k chunk
             const uint8_t *rowp = sb + pr * 128 + (((c << 2) | q) ^ pr) * 16;
             const uint4 w0 = lds128(rowp), w1 = lds128(rowp + 1024), w2 = lds128(rowp + 2048), w3 = lds128(rowp + 3072);
-            // Scales of rows pr + 8m (m = 0..3) for this lane's two columns (groups of quads qa, qa + 1).
-            float s0[4], s1[4];
+            // Scales of rows pr + 8m (m = 0..3) for this lane's group (quad q of chunk cg).
+            float sw[4];
             if (p.scales_tma) {
-              const uint8_t *sc = sb + kWordBytes + pr * 16 + (4 * c + qa) * 2;
+              const uint8_t *sc = sb + kWordBytes + pr * 16 + (4 * c + q) * 2;
 #pragma unroll
-              for (int m = 0; m < 4; ++m) {
-                const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(sc + m * 8 * 16));
-                s0[m] = v.x;
-                s1[m] = v.y;
-              }
+              for (int m = 0; m < 4; ++m) sw[m] = __half2float(*reinterpret_cast<const __half *>(sc + m * 8 * 16));
             } else {
-              const int i0 = (cg * 128 + 32 * qa) / G, i1 = (cg * 128 + 32 * (qa + 1)) / G;
+              const int gi = (cg * 128 + 32 * q) / G;
 #pragma unroll
               for (int m = 0; m < 4; ++m) {
                 const int row = p.ids ? wrow0 + pr + 8 * m : min(tile * kRows + pr + 8 * m, N - 1);
-                s0[m] = i0 < spr ? __half2float(p.ws[static_cast<size_t>(row) * spr + i0]) : 0.f;
-                s1[m] = i1 < spr ? __half2float(p.ws[static_cast<size_t>(row) * spr + i1]) : 0.f;
+                sw[m] = gi < spr ? __half2float(p.ws[static_cast<size_t>(row) * spr + gi]) : 0.f;
               }
             }
-            // Four independent accumulator chains: (row tile 0, 1) x (words 0-1, 2-3).
-            float d[NT][2][4], e[NT][2][4];
+            int d[NT][2][4];
 #pragma unroll
             for (int t = 0; t < NT; ++t)
 #pragma unroll
-              for (int h = 0; h < 2; ++h)
-#pragma unroll
-                for (int i2 = 0; i2 < 4; ++i2) d[t][h][i2] = e[t][h][i2] = 0.f;
+              for (int h = 0; h < 2; ++h) d[t][h][0] = d[t][h][1] = d[t][h][2] = d[t][h][3] = 0;
             const uint32_t v0[4] = {w0.x, w0.y, w0.z, w0.w}, v1[4] = {w1.x, w1.y, w1.z, w1.w};
             const uint32_t v2[4] = {w2.x, w2.y, w2.z, w2.w}, v3[4] = {w3.x, w3.y, w3.z, w3.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              uint32_t a0[4], a1[4], a2[4], a3[4];
-              decode_q4(v0[j], a0);  // row pr
-              decode_q4(v1[j], a1);  // row pr + 8
-              decode_q4(v2[j], a2);  // row pr + 16
-              decode_q4(v3[j], a3);  // row pr + 24
-              const int s = cg * 8 + 2 * j;
+              // int8 16 * value of the even (lo) and odd (hi) elements of each row's word j
+              const uint32_t e0 = (v0[j] << 4) & kHigh, o0 = v0[j] & kHigh;  // row pr
+              const uint32_t e1 = (v1[j] << 4) & kHigh, o1 = v1[j] & kHigh;  // row pr + 8
+              const uint32_t e2 = (v2[j] << 4) & kHigh, o2 = v2[j] & kHigh;  // row pr + 16
+              const uint32_t e3 = (v3[j] << 4) & kHigh, o3 = v3[j] & kHigh;  // row pr + 24
 #pragma unroll
               for (int t = 0; t < NT; ++t) {
-                const uint2 *bf = bl + (static_cast<size_t>(tb + t) * nsteps + s) * 8;
-                uint2 f0 = make_uint2(0u, 0u), f1 = make_uint2(0u, 0u);
-                if (act) {
-                  f0 = bf[0];
-                  f1 = bf[8];
-                }
-                float(&c0)[4] = j < 2 ? d[t][0] : e[t][0];
-                float(&c1)[4] = j < 2 ? d[t][1] : e[t][1];
-                mma_16816(c0, a0[0], a1[0], a0[1], a1[1], f0.x, f0.y);
-                mma_16816(c1, a2[0], a3[0], a2[1], a3[1], f0.x, f0.y);
-                mma_16816(c0, a0[2], a1[2], a0[3], a1[3], f1.x, f1.y);
-                mma_16816(c1, a2[2], a3[2], a2[3], a3[3], f1.x, f1.y);
+                uint2 f = make_uint2(0u, 0u);
+                if (act) f = bl[(static_cast<size_t>(tb + t) * nsteps + cg * 4 + j) * 8];
+                mma_s8_16832(d[t][0], e0, e1, o0, o1, f.x, f.y);
+                mma_s8_16832(d[t][1], e2, e3, o2, o3, f.x, f.y);
               }
             }
-            // fp32 epilogue: per-column group scale, the 2^24 factor, the offset through the quad sums.
+            // fp32 epilogue: this lane holds columns 2q (hi limb) and 2q + 1 (lo limb) of its group.
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
-              const int tok = LO ? t : 2 * t + (q >> 1);
-              if (tok < (p.xpg ? 1 : B)) {
-                const bool hi = LO ? (q < 2) : true;
-                const float2 xs = *reinterpret_cast<const float2 *>(xsum + (tb + tok) * kc * 4 + cg * 4 + qa);
-                const float x0 = hi ? 8.f * xs.x : 0.f, x1 = hi ? 8.f * xs.y : 0.f;
+              const float xsc = xs[((tb + t) * kc + cg) * 4 + q];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const float dd0 = d[t][h][0] + e[t][h][0], dd1 = d[t][h][1] + e[t][h][1];
-                  const float dd2 = d[t][h][2] + e[t][h][2], dd3 = d[t][h][3] + e[t][h][3];
-                  acc[t][h][0] += s0[2 * h] * fmaf(dd0, 16777216.f, -x0) + s1[2 * h] * fmaf(dd1, 16777216.f, -x1);
-                  acc[t][h][1] += s0[2 * h + 1] * fmaf(dd2, 16777216.f, -x0) + s1[2 * h + 1] * fmaf(dd3, 16777216.f, -x1);
-                }
+              for (int h = 0; h < 2; ++h) {
+                const int r0 = d[t][h][0] * 256 + d[t][h][1], r1 = d[t][h][2] * 256 + d[t][h][3];
+                acc[t][h][0] = fmaf(sw[2 * h] * xsc, static_cast<float>(r0), acc[t][h][0]);
+                acc[t][h][1] = fmaf(sw[2 * h + 1] * xsc, static_cast<float>(r1), acc[t][h][1]);
               }
             }
           }
@@ -343,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!aborted) issue(u + S);
       }
     }
-    // Reduce the quad's lanes, then (when K is split) the warps through shared memory.
+    // Reduce the quad's four groups, then (when K is split) the warps through shared memory.
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
 #pragma unroll
@@ -352,23 +321,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int hh = 0; hh < 2; ++hh) {
           float v = acc[t][h][hh];
           v += __shfl_xor_sync(0xffffffffu, v, 1);
-          if (LO) v += __shfl_xor_sync(0xffffffffu, v, 2);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
           acc[t][h][hh] = v;
         }
-      const int tok = LO ? t : 2 * t + (q >> 1);
-      const bool writer = LO ? (q == 0) : ((q & 1) == 0);
-      if (writer && tok < BO) {
+      if (q == 0 && t < BO) {
 #pragma unroll
         for (int m = 0; m < 4; ++m) {  // rows pr + 8m: (tile h = m / 2, row g or g + 8 = m % 2)
           const float v = acc[t][m >> 1][m & 1];
           if (p.ks == 1) {  // the warp owns whole rows: store directly, no barrier
             const int row = tile * kRows + pr + 8 * m;
             if (tile < p.tiles && row < N && !aborted) {
-              float *out = p.y + static_cast<size_t>(tok) * N + row;
+              float *out = p.y + static_cast<size_t>(t) * N + row;
               *out = p.add ? *out + v : v;
             }
           } else {
-            red[(items.kw * kRows * p.rt + items.rtl * kRows + pr + 8 * m) * BO + tok] = v;
+            red[(items.kw * kRows * p.rt + items.rtl * kRows + pr + 8 * m) * BO + t] = v;
           }
         }
       }
@@ -397,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int G, int NT, bool LO>
+template <int G, int NT>
 int launch(const uint32_t *wq, Params p, cudaStream_t stream, const DeviceInfo &dev) {
   p.scales_tma = G == 32 && (p.k / G) % 8 == 0 && aligned(p.ws, 16);
   p.slot_bytes = ((kWordBytes + (p.scales_tma ? kRows * kScaleHalvesTma * 2 : 0) + 1023) / 1024) * 1024;
@@ -431,7 +398,7 @@ int launch(const uint32_t *wq, Params p, cudaStream_t stream, const DeviceInfo &
   }
   p.rt = kWarps / p.ks;
   p.nrounds = (p.tiles + p.rt - 1) / p.rt;
-  auto kern = gemv_q4_kernel<G, NT, LO>;
+  auto kern = gemv_q4_kernel<G, NT>;
   static size_t configured = 0;
   if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -444,9 +411,9 @@ int launch(const uint32_t *wq, Params p, cudaStream_t stream, const DeviceInfo &
 
 template <int G>
 int dispatch_nt(const uint32_t *wq, const Params &p, cudaStream_t s, const DeviceInfo &dev) {
-  const bool lo = !p.x_f16 && p.batch <= 2;
-  if (lo) return p.batch == 1 ? launch<G, 1, true>(wq, p, s, dev) : launch<G, 2, true>(wq, p, s, dev);
-  return p.batch <= 2 ? launch<G, 1, false>(wq, p, s, dev) : launch<G, 2, false>(wq, p, s, dev);
+  if (p.batch == 1) return launch<G, 1>(wq, p, s, dev);
+  if (p.batch == 2) return launch<G, 2>(wq, p, s, dev);
+  return launch<G, 4>(wq, p, s, dev);
 }
 
 // One GEMV launch over [n, k] with batch <= 4 (also used by the MoE decode).
@@ -495,9 +462,9 @@ int gemv_q4_grouped(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const
   p.tpg = rows_per_group / kRows;
   p.xpg = xpg;
   switch (group) {
-    case 32: return launch<32, 1, true>(wq, p, stream, dev);
-    case 64: return launch<64, 1, true>(wq, p, stream, dev);
-    default: return launch<128, 1, true>(wq, p, stream, dev);
+    case 32: return launch<32, 1>(wq, p, stream, dev);
+    case 64: return launch<64, 1>(wq, p, stream, dev);
+    default: return launch<128, 1>(wq, p, stream, dev);
   }
 }
 
