@@ -159,32 +159,49 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------------------------------------------------
+    // A TMA instruction holds its warp for ~0.2 us on B200 whatever it copies, so the copies of a
+    // stage (W, or gate and up halves of W, and X) go out as ONE instruction executed by lanes 0..2,
+    // each lane with its own map, destination and coordinates.
+    const int nload = MODE == kGateUp ? 3 : 2;
+    const CUtensorMap *lmap = lane == nload - 1 ? &xmap : &wmap;
     if (lane == 0) {
       prefetch_tmap(&wmap);
       prefetch_tmap(&xmap);
-      const uint32_t bytes = kWTileBytes + p.bn * 128;
-      int issued = 0;
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % S;
-        if (i >= S && !*abort_flag && !mbar_wait(&empty[s], ((i / S) - 1) & 1)) {
+    }
+    __syncwarp();
+    const uint32_t bytes = kWTileBytes + p.bn * 128;
+    int issued = 0;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % S;
+      if (i >= S && !__all_sync(0xffffffffu, mbar_wait(&empty[s], ((i / S) - 1) & 1))) {
+        if (lane == 0) {
           raise_status(kStatusGemmTmaWait);
           *abort_flag = 1;
         }
-        if (*abort_flag) break;
-        mbar_expect_tx(&full[s], bytes);
-        if (MODE == kGateUp) {  // 64 gate rows, then the 64 matching up rows
-          tma_load_2d(smem + L.w + s * kWTileBytes, &wmap, &full[s], kblock(i) * (kBK / 8), n0);
-          tma_load_2d(smem + L.w + s * kWTileBytes + kWTileBytes / 2, &wmap, &full[s], kblock(i) * (kBK / 8),
-                      n0 + p.rows_per_expert / 2);
-        } else {
-          tma_load_2d(smem + L.w + s * kWTileBytes, &wmap, &full[s], kblock(i) * (kBK / 8), n0);
-        }
-        tma_load_2d(smem + L.x + s * p.bn * 128, &xmap, &full[s], kblock(i) * kBK, m0);
-        issued = i + 1;
+        break;
       }
-      // Leave no copy in flight: wait (bounded) for the last load issued into each stage.
-      for (int i = max(0, issued - S); i < issued; ++i) mbar_wait(&full[i % S], (i / S) & 1);
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+      if (lane == 0) mbar_expect_tx(&full[s], bytes);
+      __syncwarp();
+      if (lane < nload) {
+        uint8_t *dst;
+        int cx, cy;
+        if (lane == nload - 1) {  // X: bn token rows x 64 k
+          dst = smem + L.x + s * p.bn * 128;
+          cx = kblock(i) * kBK;
+          cy = m0;
+        } else {  // W: 128 rows (dense), or 64 gate rows (lane 0) and the matching 64 up rows (lane 1)
+          dst = smem + L.w + s * kWTileBytes + lane * (kWTileBytes / 2);
+          cx = kblock(i) * (kBK / 8);
+          cy = n0 + lane * (p.rows_per_expert / 2);
+        }
+        tma_load_2d(dst, lmap, &full[s], cx, cy);
+      }
+      issued = i + 1;
     }
+    // Leave no copy in flight: wait (bounded) for the last load issued into each stage.
+    if (lane == 0)
+      for (int i = max(0, issued - S); i < issued; ++i) mbar_wait(&full[i % S], (i / S) & 1);
   } else if (warp == 1) {
     // ---------------- MMA issuer -------------------------------------------------------------
     if (lane == 0) {

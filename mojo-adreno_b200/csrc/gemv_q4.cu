@@ -43,6 +43,7 @@ constexpr int kRows = 32;     // rows of a tile: two m16 tiles
 constexpr int kSlotK = 256;   // k of a slot: 32 words = one 128-byte swizzle row
 constexpr int kWordBytes = kRows * 128;
 constexpr int kScaleHalvesTma = 8;  // a TMA-loaded scale row: 8 halves (16 bytes), G = 32 only
+constexpr int kPrefetchItems = 4;  // items per warp warmed in L2 while earlier kernels finish
 constexpr float kLimbMax = 32512.f;  // 127 * 256: |x| maps to at most this, so both limbs fit in int8
 
 struct Params {
@@ -165,7 +166,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.scales_tma) prefetch_tmap(&smap);
   }
   __syncwarp();
-  griddep_wait();  // everything above touched no global memory
+  // Until the kernels before this one finish, warm L2 with this warp's first kPrefetchItems items
+  // (lane i: item i). Only plain weight tiles: expert ids are written by earlier kernels.
+  if (!p.ids && lane < kPrefetchItems) {
+    int tile, sk;
+    if (items.get(lane, tile, sk)) {
+      tma_prefetch_l2_2d(&wmap, sk * (kSlotK / 8), tile * kRows);
+      if (p.scales_tma) tma_prefetch_l2_2d(&smap, sk * kScaleHalvesTma, tile * kRows);
+    }
+  }
+  griddep_wait();  // everything above wrote no global memory
   for (int s = 0; s < S; ++s) issue(s);  // loads start before x is staged
 
   uint2 *bfrag = reinterpret_cast<uint2 *>(smem + L.bfrag);  // [nt][nsteps][8 columns]
