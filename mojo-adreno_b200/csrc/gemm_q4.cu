@@ -330,15 +330,18 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     } else if (MODE == kGateUp) {
       // Up rows (TMEM lanes 64-127) go through shared memory (the A ring is free now) to the
-      // threads holding the matching gate rows (lanes 0-63): a = silu(gate) * up, fp16.
+      // threads holding the matching gate rows (lanes 0-63): a = silu(gate) * up, fp16. Row r's
+      // column c sits at c ^ (r & 15) (bn is a multiple of 16), so the 32 rows a warp writes or reads
+      // at one column fall in 16 different banks instead of one.
       float *up = reinterpret_cast<float *>(smem + L.a);  // [64 rows][bn]
       if (live && row >= 64) {
+        const int ur = row - 64;
         for (int c0 = 32 * half; c0 < p.bn; c0 += 64) {
           float v[32];
           tmem_ld32(taddr + c0, v);
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (c0 + j < p.bn) up[(row - 64) * p.bn + c0 + j] = v[j];
+            if (c0 + j < p.bn) up[ur * p.bn + ((c0 + j) ^ (ur & 15))] = v[j];
         }
       }
       named_bar_sync(1, 32 * kDeqWarps);
@@ -350,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             if (c0 + j < mcount) {
-              const float g = v[j], u = up[row * p.bn + c0 + j];
+              const float g = v[j], u = up[row * p.bn + ((c0 + j) ^ (row & 15))];
               p.y16[static_cast<size_t>(m0 + c0 + j) * p.n_out + col] = __float2half_rn(g / (1.f + expf(-g)) * u);
             }
           }
