@@ -7,19 +7,19 @@
 // multiplies exactly (codes are small integers, x is fp16) and accumulates in fp32, so its error
 // against exact arithmetic is far below the reference's own.
 //
-// B200 design (HBM-bound: 0.2656 B per weight, ~92 weights per SM clock at 6.5 TB/s, so under
-// 1.4 issued instructions per weight):
+// B200 design (HBM-bound: 0.2656 B per weight, ~92 weights per SM clock at 6.5 TB/s, so the
+// instructions per weight decide the speed):
 //  * Streaming: each of 16 warps TMA-loads its own 32-output x 1024-k tiles of the [k/16][n]
 //    word array (64 word rows of 128 bytes, 128-byte swizzle) and their [k/128][n] scales into a
 //    private shared-memory ring and refills a slot as soon as it is consumed. Persistent CTAs,
 //    one per SM.
-//  * Decode: a 2-bit code pair masked into the mantissa of an fp16x2 register is an exact
-//    subnormal: (w & (0x00030003 << 2j)) holds c * 4^j * 2^-24 for j = 0..3; one shift by 8 gives
-//    the other four pairs. Eight ANDs and one shift per 16 weights; the 4^-j factors go into the
-//    activation (B) slots and 2^24 into the fp32 epilogue; the -1 offset is removed with the
-//    group's sum of x: sum (c - 1) x = sum c x - sum x.
-//  * Multiply: mma.m16n8k16 (fp16 in, fp32 accumulate); one group (128 k) = 8 k16 steps, after
-//    which the group's fp16 scale is applied in fp32.
+//  * Decode: (w >> 2j) & 0x03030303 puts codes j, j + 4, j + 8, j + 12 of a word into the four
+//    bytes of a register as int8 0..2: seven integer operations per 16 weights.
+//  * Multiply: the warp-level int8 tensor op mma.m16n8k32 (s8 x s8 -> s32, exact). x is staged
+//    per CTA as 15-bit fixed point per 128-k group, two int8 limbs hi * 256 + lo; the 8 mma
+//    columns are (token, limb) pairs, so a lane ends a group holding one token's hi and lo sums for
+//    its four outputs. The -1 offset of the codes is removed exactly with the group's integer limb
+//    sums: sum (c - 1) x = sum c x - sum x. The fp32 epilogue applies scale_w * scale_x per group.
 //  * Bank conflicts: lane (g, q) reads word row 4b + q and the 16-byte column chunk
 //    (g >> 1) | (g & 1) << 2; with the swizzle's XOR by row % 8 the 8 lanes of a phase hit 8
 //    distinct chunks.
@@ -54,31 +54,28 @@ struct Params {
   int ks, rt, tiles, nrounds, slots, scales_tma;
 };
 
-// Pairs j = 0..7 of a word: codes (j, j + 8), factor 4^(j % 4), j >= 4 from w >> 8.
-__device__ __forceinline__ void decode_t2(uint32_t w, uint32_t (&q)[8]) {
-  q[0] = w & 0x00030003u;
-  q[1] = w & 0x000C000Cu;
-  q[2] = w & 0x00300030u;
-  q[3] = w & 0x00C000C0u;
-  const uint32_t v = w >> 8;
-  q[4] = v & 0x00030003u;
-  q[5] = v & 0x000C000Cu;
-  q[6] = v & 0x00300030u;
-  q[7] = v & 0x00C000C0u;
+constexpr float kLimbMax = 32512.f;  // 127 * 256: |x| maps to at most this, so both limbs fit in int8
+
+__device__ __forceinline__ uint32_t pack_bytes(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 255u) | (static_cast<uint32_t>(b) & 255u) << 8 |
+         (static_cast<uint32_t>(c) & 255u) << 16 | (static_cast<uint32_t>(d) & 255u) << 24;
 }
 
+// Shared memory: the rings; x as mma B fragments [k/32 steps][2 NB columns][4 lanes] (uint2); per
+// (token, group) the x scale and the integer sums of the hi and lo limbs; K-split partials; barriers.
 struct Layout {
-  uint32_t slots, bfrag, xsum, red, bars, total;
+  uint32_t slots, bfrag, xs, lsum, red, bars, total;
 };
 
 template <int SK>
 __host__ __device__ inline Layout layout(int k, int nb, int slots) {
   Layout L;
-  const int kb = k / 64, kg = k / 128;
+  const int kg = k / 128;
   L.slots = 0;
   L.bfrag = kWarps * slots * Slot<SK>::kSlotBytes;
-  L.xsum = L.bfrag + kb * 4 * nb * 4 * 8;
-  L.red = L.xsum + nb * kg * 4;
+  L.xs = L.bfrag + (k / 32) * 2 * nb * 4 * 8;
+  L.lsum = L.xs + nb * kg * 4;
+  L.red = L.lsum + nb * kg * 2 * 4;
   L.bars = (L.red + kWarps * kCols * nb * 4 + 7) / 8 * 8;
   L.total = L.bars + kWarps * kMaxSlots * 8;
   return L;
@@ -104,7 +101,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const Layout L = layout<SK>(p.k, NB, p.slots);
   const int K = p.k, N = p.n, S = p.slots;
-  const int kb = K / 64, kg = K / 128;
+  const int kg = K / 128;
   const int nslotk = (K + kSlotK - 1) / kSlotK;
   const int spw = (nslotk + p.ks - 1) / p.ks;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -143,57 +140,84 @@ __global__ void __launch_bounds__(kThreads, 1)
   griddep_wait();  // everything above touched no global memory
   for (int s = 0; s < S; ++s) issue(s);
 
-  uint2 *bfrag = reinterpret_cast<uint2 *>(smem + L.bfrag);  // [kb*4 steps][NB][4]
-  float *xsum = reinterpret_cast<float *>(smem + L.xsum);     // [NB][kg]
+  uint2 *bfrag = reinterpret_cast<uint2 *>(smem + L.bfrag);  // [K/32 steps][2 NB][4]
+  float *xs = reinterpret_cast<float *>(smem + L.xs);         // [NB][kg]
+  int *lsum = reinterpret_cast<int *>(smem + L.lsum);         // [NB][kg][hi, lo]
   float *red = reinterpret_cast<float *>(smem + L.red);       // [kWarps][32][NB]
 
-  // Stage x: per step s = 4b + t and lane (column tok, quad q):
-  //   b0 = (x[16(4b+q) + 2t], x[.. + 2t + 8]) / 4^(2t % 4), b1 = (x[.. + 2t + 1], x[.. + 2t + 9]) / 4^((2t+1) % 4)
-  for (int it = threadIdx.x; it < NB * kb * 4; it += kThreads) {
-    const int tok = it / (kb * 4), wr = it % (kb * 4);  // wr = word row k / 16
-    const int b = wr / 4, q = wr % 4;
-    const uint4 *xr = reinterpret_cast<const uint4 *>(p.x + static_cast<size_t>(tok) * K + 16 * wr);
-    const uint4 v0 = xr[0], v1 = xr[1];
-    const __half *h0 = reinterpret_cast<const __half *>(&v0), *h1 = reinterpret_cast<const __half *>(&v1);
+  // Stage x: item (token t, word row wr) = x[16 wr .. 16 wr + 15]; the 8 items of a group are 8
+  // consecutive lanes, which share its scale and limb sums. For step 2b + h (word rows 4b .. 4b + 3,
+  // codes h * 2 + 4i and h * 2 + 1 + 4i) lane q' of column 2t + l holds limb l of x at those codes of
+  // word row 4b + q'.
+  const int nrow = K / 16;
+  for (int base = 0; base < NB * nrow; base += kThreads) {
+    const int it = base + threadIdx.x;
+    const bool live = it < NB * nrow;
+    const int t = live ? it / nrow : 0, wr = it % nrow;
     float xv[16];
+    if (live) {
+      const uint4 *xr = reinterpret_cast<const uint4 *>(p.x + static_cast<size_t>(t) * K + 16 * wr);
+      const uint4 v0 = xr[0], v1 = xr[1];
+      const __half *h0 = reinterpret_cast<const __half *>(&v0), *h1 = reinterpret_cast<const __half *>(&v1);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      xv[e] = __half2float(h0[e]);
-      xv[8 + e] = __half2float(h1[e]);
+      for (int e = 0; e < 8; ++e) {
+        xv[e] = __half2float(h0[e]);
+        xv[8 + e] = __half2float(h1[e]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) xv[e] = 0.f;
+    }
+    float m = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) m = fmaxf(m, fabsf(xv[e]));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float inv = m > 0.f ? kLimbMax / m : 0.f;
+    int hi[16], lo[16], shi = 0, slo = 0;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int v = static_cast<int>(rintf(xv[e] * inv));
+      hi[e] = (v + 128) >> 8;
+      lo[e] = v - (hi[e] << 8);
+      shi += hi[e];
+      slo += lo[e];
     }
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int j0 = 2 * t, j1 = 2 * t + 1;
-      const float f0 = 1.f / static_cast<float>(1 << (2 * (j0 & 3))), f1 = 1.f / static_cast<float>(1 << (2 * (j1 & 3)));
-      bfrag[((4 * b + t) * NB + tok) * 4 + q] =
-          make_uint2(pack_half2(xv[j0] * f0, xv[j0 + 8] * f0), pack_half2(xv[j1] * f1, xv[j1 + 8] * f1));
+    for (int o = 1; o < 8; o <<= 1) {
+      shi += __shfl_xor_sync(0xffffffffu, shi, o);
+      slo += __shfl_xor_sync(0xffffffffu, slo, o);
     }
-  }
-  for (int it = threadIdx.x; it < NB * kg; it += kThreads) {
-    const int tok = it / kg, gi = it % kg;
-    const __half2 *xr = reinterpret_cast<const __half2 *>(p.x + static_cast<size_t>(tok) * K + 128 * gi);
-    float s = 0.f;
-    for (int e = 0; e < 64; ++e) {
-      const float2 v = __half22float2(xr[e]);
-      s += v.x + v.y;
+    if (!live) continue;
+    const int gg = wr / 8;
+    if (wr % 8 == 0) {
+      xs[t * kg + gg] = m / kLimbMax;
+      lsum[(t * kg + gg) * 2] = shi;
+      lsum[(t * kg + gg) * 2 + 1] = slo;
     }
-    xsum[tok * kg + gi] = s;
+    const int b = wr / 4, q = wr % 4;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint2 *dst = bfrag + ((2 * b + h) * 2 * NB + 2 * t) * 4 + q;
+      dst[0] = make_uint2(pack_bytes(hi[2 * h], hi[2 * h + 4], hi[2 * h + 8], hi[2 * h + 12]),
+                          pack_bytes(hi[2 * h + 1], hi[2 * h + 5], hi[2 * h + 9], hi[2 * h + 13]));
+      dst[4] = make_uint2(pack_bytes(lo[2 * h], lo[2 * h + 4], lo[2 * h + 8], lo[2 * h + 12]),
+                          pack_bytes(lo[2 * h + 1], lo[2 * h + 5], lo[2 * h + 9], lo[2 * h + 13]));
+    }
   }
   __syncthreads();
 
   const int g = lane >> 2, q = lane & 3;
-  const bool act = g < NB;
-  const int t0 = 2 * q, t1 = 2 * q + 1;       // D columns (tokens) of this lane
+  const bool act = g < 2 * NB;                // columns (token g / 2, limb g % 2) in use
   const int cgc = (g >> 1) | ((g & 1) << 2);  // this lane's 16-byte column chunk: outputs 4 cgc .. + 3
+  constexpr uint32_t kCode = 0x03030303u;
   uint32_t u = 0, u_abort = 0;
   bool aborted = false;
 
   for (int r = blockIdx.x; r < p.nrounds; r += gridDim.x) {
     const int tile = r * p.rt + items.rtl;
     const int col = tile * kCols + 4 * cgc;
-    float acc[2][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) acc[0][i] = acc[1][i] = 0.f;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // token q, outputs col .. col + 3
     if (tile < p.tiles) {
       for (int i = 0; i < items.per_round; ++i, ++u) {
         const int sk = items.kw * spw + i;
@@ -219,46 +243,33 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int o = 0; o < 4; ++o)
                 sc[o] = col + o < N ? __half2float(p.s[static_cast<size_t>(gg) * N + col + o]) : 0.f;
             }
-            // Four independent accumulator chains: (tile 0, tile 1) x (block h = 0, 1).
-            float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-            float e0[4] = {0.f, 0.f, 0.f, 0.f}, e1[4] = {0.f, 0.f, 0.f, 0.f};
+            int d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};  // tile 0 (outputs col, col + 1), tile 1 (col + 2, col + 3)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int b = 2 * gi + h, wr = 4 * b + q;
+            for (int bh = 0; bh < 2; ++bh) {
+              const int b = 2 * gi + bh, wr = 4 * b + q;
               const uint4 wv = *reinterpret_cast<const uint4 *>(sb + wr * 128 + ((cgc ^ (wr & 7)) << 4));
-              uint32_t qx[8], qy[8], qz[8], qw[8];
-              decode_t2(wv.x, qx);  // output col + 0: tile 0 row g
-              decode_t2(wv.y, qy);  // col + 1: tile 0 row g + 8
-              decode_t2(wv.z, qz);  // col + 2: tile 1 row g
-              decode_t2(wv.w, qw);  // col + 3: tile 1 row g + 8
-              const int bg = sk * (kSlotK / 64) + b;  // global block
+              const int bg = sk * (kSlotK / 64) + b;  // global block of 4 word rows
 #pragma unroll
-              for (int t = 0; t < 4; ++t) {
+              for (int h = 0; h < 2; ++h) {
                 uint2 f = make_uint2(0u, 0u);
-                if (act) f = bfrag[((4 * bg + t) * NB + g) * 4 + q];
-                mma_16816(h ? e0 : d0, qx[2 * t], qy[2 * t], qx[2 * t + 1], qy[2 * t + 1], f.x, f.y);
-                mma_16816(h ? e1 : d1, qz[2 * t], qw[2 * t], qz[2 * t + 1], qw[2 * t + 1], f.x, f.y);
+                if (act) f = bfrag[((2 * bg + h) * 2 * NB + g) * 4 + q];
+                const int j0 = 4 * h, j1 = 4 * h + 2;  // shifts of codes 2h + 4i and 2h + 1 + 4i
+                mma_s8_16832(d0, (wv.x >> j0) & kCode, (wv.y >> j0) & kCode, (wv.x >> j1) & kCode, (wv.y >> j1) & kCode,
+                             f.x, f.y);
+                mma_s8_16832(d1, (wv.z >> j0) & kCode, (wv.w >> j0) & kCode, (wv.z >> j1) & kCode, (wv.w >> j1) & kCode,
+                             f.x, f.y);
               }
             }
-#pragma unroll
-            for (int i2 = 0; i2 < 4; ++i2) {
-              d0[i2] += e0[i2];
-              d1[i2] += e1[i2];
-            }
-            // D: [0] = (row g, col t0), [1] = (row g, col t1), [2] = (row g+8, col t0), [3] = (row g+8, col t1)
-            if (t0 < NB) {
-              const float xs = xsum[t0 * kg + gg];
-              acc[0][0] += sc[0] * fmaf(d0[0], 16777216.f, -xs);
-              acc[0][1] += sc[1] * fmaf(d0[2], 16777216.f, -xs);
-              acc[0][2] += sc[2] * fmaf(d1[0], 16777216.f, -xs);
-              acc[0][3] += sc[3] * fmaf(d1[2], 16777216.f, -xs);
-            }
-            if (t1 < NB) {
-              const float xs = xsum[t1 * kg + gg];
-              acc[1][0] += sc[0] * fmaf(d0[1], 16777216.f, -xs);
-              acc[1][1] += sc[1] * fmaf(d0[3], 16777216.f, -xs);
-              acc[1][2] += sc[2] * fmaf(d1[1], 16777216.f, -xs);
-              acc[1][3] += sc[3] * fmaf(d1[3], 16777216.f, -xs);
+            // D: [0] = (output row g, hi), [1] = (row g, lo), [2] = (row g + 8, hi), [3] = (row g + 8, lo) of token q
+            if (q < NB) {
+              const float xsc = xs[q * kg + gg];
+              const int shi = lsum[(q * kg + gg) * 2], slo = lsum[(q * kg + gg) * 2 + 1];
+              const int r0 = (d0[0] - shi) * 256 + (d0[1] - slo), r1 = (d0[2] - shi) * 256 + (d0[3] - slo);
+              const int r2 = (d1[0] - shi) * 256 + (d1[1] - slo), r3 = (d1[2] - shi) * 256 + (d1[3] - slo);
+              acc[0] = fmaf(sc[0] * xsc, static_cast<float>(r0), acc[0]);
+              acc[1] = fmaf(sc[1] * xsc, static_cast<float>(r1), acc[1]);
+              acc[2] = fmaf(sc[2] * xsc, static_cast<float>(r2), acc[2]);
+              acc[3] = fmaf(sc[3] * xsc, static_cast<float>(r3), acc[3]);
             }
           }
         }
@@ -267,18 +278,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     const int rows = kCols * p.rt;
+    if (q < NB) {
+      if (p.ks == 1) {  // the warp owns whole outputs: store directly, no barrier
+        if (tile < p.tiles && col < N && !aborted)
+          *reinterpret_cast<float4 *>(p.y + static_cast<size_t>(q) * N + col) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      } else {
 #pragma unroll
-    for (int uu = 0; uu < 2; ++uu) {
-      const int tok = 2 * q + uu;
-      if (tok < NB) {
-        if (p.ks == 1) {  // the warp owns whole outputs: store directly, no barrier
-          if (tile < p.tiles && col < N && !aborted)
-            *reinterpret_cast<float4 *>(p.y + static_cast<size_t>(tok) * N + col) =
-                make_float4(acc[uu][0], acc[uu][1], acc[uu][2], acc[uu][3]);
-        } else {
-#pragma unroll
-          for (int o = 0; o < 4; ++o) red[(items.kw * rows + items.rtl * kCols + 4 * cgc + o) * NB + tok] = acc[uu][o];
-        }
+        for (int o = 0; o < 4; ++o) red[(items.kw * rows + items.rtl * kCols + 4 * cgc + o) * NB + q] = acc[o];
       }
     }
     if (p.ks == 1) continue;

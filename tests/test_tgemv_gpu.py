@@ -1,5 +1,6 @@
 """Ternary GEMV parity on the GPU: the kernel against the exact oracle (float64), normwise
-<= 1e-3 as the bar and ~1e-6 expected (codes and fp16 x are exact in the tensor op, fp32 sums)."""
+<= 1e-3 as the bar; the kernel's products and group sums are exact integers on x carried as 15-bit
+fixed point per 128-k group, so its error is far below the bar."""
 import numpy as np
 import pytest
 import torch
@@ -12,7 +13,7 @@ from mq import synth
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
-TIGHT = 2e-5
+TIGHT = 1e-4  # x step: 1/65024 of its 128-k group's largest |x|
 
 
 def run(cuda, x, w, s, n, k):
@@ -69,5 +70,5 @@ def test_tgemv_all_codes(cuda):
     y = run(cuda, x, w, s, n, k)
     ref = ternary.tgemv(x, w, s, n, k)
     assert normwise(y, ref) <= TIGHT
-    # code 1 is weight 0: zero up to the fp32 rounding of the -sum(x) correction
-    assert np.abs(y[0, 8:16]).max() <= 1e-6 * 0.5 * np.abs(x.astype(np.float64)).sum()
+    # code 1 is weight 0: the integer group sums cancel exactly
+    assert np.abs(y[0, 8:16]).max() == 0.0
