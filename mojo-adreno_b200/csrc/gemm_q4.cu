@@ -170,17 +170,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     __syncwarp();
     const uint32_t bytes = kWTileBytes + p.bn * 128;
-    int issued = 0;
+    // The loops of all three roles keep their ring slot, phase and k block as running counters: a
+    // single issuing thread retires only a few instructions per stage's worth of MMA time, so no
+    // division or descriptor rebuild may sit in its path.
+    int s = 0, round = 0, kb = kblock(0), issued = 0;
+    const int kb_end = kb0 + nk;
     for (int i = 0; i < nk; ++i) {
-      const int s = i % S;
-      if (i >= S && !__all_sync(0xffffffffu, mbar_wait(&empty[s], ((i / S) - 1) & 1))) {
+      if (round > 0 && !__all_sync(0xffffffffu, mbar_wait(&empty[s], (round - 1) & 1))) {
         if (lane == 0) {
           raise_status(kStatusGemmTmaWait);
           *abort_flag = 1;
         }
         break;
       }
-      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
       if (lane == 0) mbar_expect_tx(&full[s], bytes);
       __syncwarp();
       if (lane < nload) {
@@ -188,16 +190,21 @@ __global__ void __launch_bounds__(kThreads, 2)
         int cx, cy;
         if (lane == nload - 1) {  // X: bn token rows x 64 k
           dst = smem + L.x + s * p.bn * 128;
-          cx = kblock(i) * kBK;
+          cx = kb * kBK;
           cy = m0;
         } else {  // W: 128 rows (dense), or 64 gate rows (lane 0) and the matching 64 up rows (lane 1)
           dst = smem + L.w + s * kWTileBytes + lane * (kWTileBytes / 2);
-          cx = kblock(i) * (kBK / 8);
+          cx = kb * (kBK / 8);
           cy = n0 + lane * (p.rows_per_expert / 2);
         }
         tma_load_2d(dst, lmap, &full[s], cx, cy);
       }
       issued = i + 1;
+      if (++kb == kb_end) kb = kb0;
+      if (++s == S) {
+        s = 0;
+        ++round;
+      }
     }
     // Leave no copy in flight: wait (bounded) for the last load issued into each stage.
     if (lane == 0)
@@ -206,20 +213,35 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---------------- MMA issuer -------------------------------------------------------------
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16(kBM, p.bn);
+      // Descriptors of slot 0; a slot further is + its byte size / 16 in the address field (the
+      // field holds any shared-memory address of this CTA without carrying into bit 14).
+      const uint64_t da0 = umma_desc_sw128(smem_u32(smem + L.a)), db0 = umma_desc_sw128(smem_u32(smem + L.x));
+      const uint32_t a_step = kATileBytes >> 4, x_step = (p.bn * 128) >> 4;
+      uint64_t da = da0, db = db0;
+      uint32_t ph = 0;
+      int s = 0;
       for (int i = 0; i < nk; ++i) {
-        const int s = i % S;
-        if (!*abort_flag && (!mbar_wait(&full[s], (i / S) & 1) || !mbar_wait(&deq[s], (i / S) & 1))) {
+        if (!mbar_wait(&full[s], ph) || !mbar_wait(&deq[s], ph)) {
           raise_status(kStatusGemmMmaWait);
           *abort_flag = 1;
+          break;
         }
-        if (*abort_flag) break;
         tc_fence_after();
-        const uint64_t da = umma_desc_sw128(smem_u32(smem + L.a + s * kATileBytes));
-        const uint64_t db = umma_desc_sw128(smem_u32(smem + L.x + s * p.bn * 128));
-#pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)  // +32 bytes along K = +2 in the descriptor's address field
-          umma_f16(tmem_d, da + 2 * kk, db + 2 * kk, idesc, (i | kk) != 0);
+        // +32 bytes along K = +2 in the descriptor's address field
+        umma_f16(tmem_d, da, db, idesc, i != 0);
+        umma_f16(tmem_d, da + 2, db + 2, idesc, 1);
+        umma_f16(tmem_d, da + 4, db + 4, idesc, 1);
+        umma_f16(tmem_d, da + 6, db + 6, idesc, 1);
         umma_commit(&empty[s]);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+          da = da0;
+          db = db0;
+        } else {
+          da += a_step;
+          db += x_step;
+        }
       }
       umma_commit(accum);  // also after an abort: it lands once the issued MMAs are done
     }
@@ -251,6 +273,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     };
     uint32_t cur[4], nxt[4];
     load_scales(0, cur);
+    int ds = 0;        // ring slot of the next stage
+    uint32_t dph = 0;  // its phase parity
     const uint32_t xr = row & 7;
     uint8_t *a_row = smem + L.a + row * 128;
     for (int q4 = 0; q4 * 4 < nk; ++q4) {
@@ -259,8 +283,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int u = 0; u < 4; ++u) {
         const int i = 4 * q4 + u;
         if (i >= nk) break;
-        const int s = i % S;
-        if (!*abort_flag && !mbar_wait(&full[s], (i / S) & 1)) {
+        const int s = ds;
+        if (!*abort_flag && !mbar_wait(&full[s], dph)) {
           raise_status(kStatusGemmDeqWait);
           *abort_flag = 1;
         }
@@ -286,6 +310,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           fence_proxy_async_smem();
         }
         mbar_arrive(&deq[s]);
+        if (++ds == S) {
+          ds = 0;
+          dph ^= 1;
+        }
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
