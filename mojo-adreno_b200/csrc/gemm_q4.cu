@@ -221,7 +221,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       uint32_t ph = 0;
       int s = 0;
       for (int i = 0; i < nk; ++i) {
-        if (!mbar_wait(&full[s], ph) || !mbar_wait(&deq[s], ph)) {
+        // deq[s] completes only after every dequant thread saw full[s] (W and X landed) and
+        // released its A writes: one acquire covers both.
+        if (!mbar_wait(&deq[s], ph)) {
           raise_status(kStatusGemmMmaWait);
           *abort_flag = 1;
           break;
