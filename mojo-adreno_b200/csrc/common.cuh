@@ -177,6 +177,11 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
+// Warms L2 with `bytes` (a multiple of 16) of global memory from a 16-byte aligned address.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes) : "memory");
+}
+
 // Warms L2 with a box of a tensor map (no shared memory, no barrier). Safe before griddep_wait:
 // it binds no data, and later loads read whatever the memory then holds.
 __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int x, int y) {

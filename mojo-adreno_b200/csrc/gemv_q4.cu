@@ -175,6 +175,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.scales_tma) tma_prefetch_l2_2d(&smap, sk * kScaleHalvesTma, tile * kRows);
     }
   }
+  // x, too (every CTA reads all of it): if earlier kernels write it, their writes still land in L2,
+  // the point of coherence, before griddep_wait returns.
+  if (threadIdx.x == 32 * (kWarps - 1)) {
+    const size_t xbytes = static_cast<size_t>(p.batch) * K * (p.x_f16 ? 2 : 4);
+    for (size_t off = 0; off < xbytes; off += 65536)
+      prefetch_l2_bulk(static_cast<const uint8_t *>(p.x) + off, static_cast<uint32_t>(min(xbytes - off, size_t(65536))));
+  }
   griddep_wait();  // everything above wrote no global memory
   for (int s = 0; s < S; ++s) issue(s);  // loads start before x is staged
 
