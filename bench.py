@@ -390,7 +390,14 @@ def moe_bench(mq, synth, dev, stream, world, rank):
         ms = max_over_ranks(time_graphs(graphs, 50, stream), world)
         used = np.unique(ids)
         active_bytes = len(used) * (1536 * 2048 + 2048 * 768) * 9 // 16  # int4 + fp16 scales per G=32
+        # the router (fp32 [128, 2048] GEMV) and routing on the device, timed on their own
+        rw = torch.from_numpy((np.random.default_rng(5).standard_normal((128, 2048)) * 0.02).astype(np.float32)).to(dev)
+        rl = torch.empty(tokens, 128, device=dev)
+        rids = torch.empty(tokens, 8, dtype=torch.int32, device=dev)
+        rwts = torch.empty(tokens, 8, device=dev)
+        router_ms = max_over_ranks(time_graphs([graph_of(lambda: mq.router(rw, tx, rids, rwts, 8, rl))], 50, stream), world)
         out[f"tokens_{tokens}"] = {"ms": round(ms, 5), "tokens/s": round(tokens / (ms * 1e-3), 1),
+                                   "router_and_route_ms": round(router_ms, 5),
                                    "experts_touched": int(len(used)),
                                    "expert_weight_GB/s": round(active_bytes / (ms * 1e-3) / 1e9, 1)}
         del graphs, gws

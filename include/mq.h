@@ -132,6 +132,11 @@ MQ_API int mq_tgemv(const uint16_t *x, const uint32_t *w, const uint16_t *s, flo
  * e*2fe .. e*2fe+fe-1, its up rows the next fe; qwen3moe/export.py:166-169) and down [experts * d][fe/8],
  * with fp16 scales per `group` weights of a row. */
 
+/* Router logits in fp32: logits[t][e] = W[e] . x[t] for W [experts][d], x [tokens][d] (gemv_f32 and
+ * p_gemv_f32, qwen3moe/kernels/moek.mojo:143-153, 284-295). d % 4 == 0; w and x 16-byte aligned. */
+MQ_API int mq_moe_router(const float *w, const float *x, float *logits, int64_t tokens, int experts, int64_t d,
+                         void *stream);
+
 /* ids[t][k], weights[t][k]: the top-k experts of each token (the lowest index among equal logits)
  * and softmax over the k chosen logits. Replaces route / p_route (qwen3moe/kernels/moek.mojo:156-197,
  * 385-425). logits: [tokens][experts] fp32, experts <= 256, topk <= 32. */

@@ -229,8 +229,89 @@ inline int grid_for(int64_t work, int threads, const DeviceInfo &dev) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + threads - 1) / threads, static_cast<int64_t>(dev.sms) * 8)));
 }
 
+
+// ---- router: logits[t][e] = W[e] . x[t], fp32 (gemv_f32 / p_gemv_f32, moek.mojo:143-153, 284-295) ----
+// A CTA takes kRouterTokens tokens x 4 * PER experts; x arrives in shared memory 1024 k at a time;
+// each warp owns PER experts. Per chunk a lane first loads its eight float4 of a W row (so their
+// latencies overlap), then multiplies them with the chunk's tokens; the warp sums its lanes in a
+// fixed order at the end. PER = 1 for a handful of tokens (more CTAs), 4 otherwise.
+constexpr int kRouterTokens = 8, kRouterChunk = 1024, kRouterThreads = 128;
+
+template <int PER>
+__global__ void __launch_bounds__(kRouterThreads) router_kernel(const float *__restrict__ w, const float *__restrict__ x,
+                                                                 float *__restrict__ logits, int tokens, int experts, int d) {
+  __shared__ __align__(16) float xs[kRouterTokens][kRouterChunk];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int t0 = blockIdx.x * kRouterTokens, e0 = (blockIdx.y * (kRouterThreads / 32) + warp) * PER;
+  float acc[PER][kRouterTokens];
+#pragma unroll
+  for (int e = 0; e < PER; ++e)
+#pragma unroll
+    for (int t = 0; t < kRouterTokens; ++t) acc[e][t] = 0.f;
+  griddep_wait();
+  for (int k0 = 0; k0 < d; k0 += kRouterChunk) {
+    const int kn = min(kRouterChunk, d - k0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < kRouterTokens * kRouterChunk / 4; i += kRouterThreads) {
+      const int t = i / (kRouterChunk / 4), k = (i % (kRouterChunk / 4)) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (t0 + t < tokens && k < kn) v = *reinterpret_cast<const float4 *>(x + static_cast<size_t>(t0 + t) * d + k0 + k);
+      *reinterpret_cast<float4 *>(&xs[t][k]) = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+      const bool live = e0 + e < experts;
+      const float *wr = w + static_cast<size_t>(live ? e0 + e : 0) * d + k0;
+      float4 wv[kRouterChunk / 128];
+#pragma unroll
+      for (int j = 0; j < kRouterChunk / 128; ++j) {
+        const int k = lane * 4 + 128 * j;
+        wv[j] = live && k < kn ? __ldg(reinterpret_cast<const float4 *>(wr + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < kRouterChunk / 128; ++j) {
+        const int k = lane * 4 + 128 * j;
+#pragma unroll
+        for (int t = 0; t < kRouterTokens; ++t) {
+          const float4 xv = *reinterpret_cast<const float4 *>(&xs[t][k]);
+          acc[e][t] = fmaf(wv[j].x, xv.x, fmaf(wv[j].y, xv.y, fmaf(wv[j].z, xv.z, fmaf(wv[j].w, xv.w, acc[e][t]))));
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < PER; ++e)
+#pragma unroll
+    for (int t = 0; t < kRouterTokens; ++t) {
+      float v = acc[e][t];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0 && e0 + e < experts && t0 + t < tokens) logits[static_cast<size_t>(t0 + t) * experts + e0 + e] = v;
+    }
+}
+
 }  // namespace moe
 }  // namespace mq
+
+extern "C" int mq_moe_router(const float *w, const float *x, float *logits, int64_t tokens, int experts, int64_t d,
+                             void *stream) {
+  MQ_REQUIRE(w && x && logits, MQ_EINVAL, "mq_moe_router: null pointer");
+  MQ_REQUIRE(tokens > 0 && tokens < (1 << 24) && experts >= 1 && experts <= 4096 && d > 0 && d % 4 == 0 && d < (1 << 24),
+             MQ_EINVAL, "mq_moe_router: bad shape (d must be a multiple of 4)");
+  MQ_REQUIRE(mq::aligned(w, 16) && mq::aligned(x, 16) && mq::aligned(logits, 4), MQ_EALIGN,
+             "mq_moe_router: w and x must be 16-byte aligned");
+  const unsigned tt = static_cast<unsigned>((tokens + mq::moe::kRouterTokens - 1) / mq::moe::kRouterTokens);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int warps = mq::moe::kRouterThreads / 32;
+  if (tokens <= 4 * mq::moe::kRouterTokens)  // few tokens: one expert per warp, more CTAs
+    return mq::launch_overlapped(mq::moe::router_kernel<1>, dim3(tt, (experts + warps - 1) / warps),
+                                 dim3(mq::moe::kRouterThreads), 0, st, "mq_moe_router", w, x, logits,
+                                 static_cast<int>(tokens), experts, static_cast<int>(d));
+  return mq::launch_overlapped(mq::moe::router_kernel<4>, dim3(tt, (experts + 4 * warps - 1) / (4 * warps)),
+                               dim3(mq::moe::kRouterThreads), 0, st, "mq_moe_router", w, x, logits,
+                               static_cast<int>(tokens), experts, static_cast<int>(d));
+}
 
 extern "C" int mq_moe_route(const float *logits, int32_t *ids, float *weights, int64_t tokens, int experts, int topk,
                             void *stream) {

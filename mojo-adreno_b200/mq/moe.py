@@ -9,9 +9,37 @@ import torch
 from ._lib import MQError, lib
 from .kernels import MQ_F16, MQ_F32, _need, _p, _stream, _WORDS
 
-__all__ = ["p_route", "route", "p_expert_lists", "moe_gemv_q4", "moe_gate_up", "moe_down", "moe_forward", "TILE_M"]
+__all__ = ["gemv_f32", "p_gemv_f32", "router", "p_route", "route", "p_expert_lists", "moe_gemv_q4", "moe_gate_up", "moe_down", "moe_forward", "TILE_M"]
 
 TILE_M = 64  # tokens per expert work tile of the grouped products
+
+
+def p_gemv_f32(w, x, y, cols, rows=None, tokens=None):
+    """y[t, r] = W[r] . x[t] in fp32 for the router W [rows, cols]: p_gemv_f32 (moek.mojo:284-295) and,
+    for one token, gemv_f32 (:143-153). x [tokens, cols], y [tokens, rows]."""
+    _need(w, "w", (torch.float32,))
+    rows = w.numel() // cols if rows is None else rows
+    _need(x, "x", (torch.float32,))
+    tokens = x.numel() // cols if tokens is None else tokens
+    _need(y, "y", (torch.float32,), tokens * rows)
+    lib.call("mq_moe_router", _p(w), _p(x), _p(y), tokens, rows, cols, _stream())
+    return y
+
+
+def gemv_f32(w, x, y, cols):
+    """The one-token router GEMV (moek.mojo:143-153)."""
+    return p_gemv_f32(w, x, y, cols)
+
+
+def router(w, x, ids, weights, topk=8, logits=None):
+    """The MoE layer's routing on the device: fp32 router logits, then the top-k experts and their
+    softmax weights (the model's gemv_f32 + route, qwen3moe/model.mojo:208-209)."""
+    d = x.shape[-1]
+    tokens = x.numel() // d
+    experts = w.numel() // d
+    logits = torch.empty(tokens, experts, dtype=torch.float32, device=x.device) if logits is None else logits
+    p_gemv_f32(w, x, logits, d, experts, tokens)
+    return p_route(logits, ids, weights, topk)
 
 
 def p_route(logits, ids, weights, topk=8):

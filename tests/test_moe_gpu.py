@@ -119,3 +119,22 @@ def test_moe_gate_up_down_decode(cuda):
     assert mq.device_status() == 0
     ref = r + omoe.moe_layer(m["x"], ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 32, 768)[0]
     assert normwise(res.cpu().numpy(), ref) <= TOL
+
+
+@pytest.mark.parametrize("tokens,experts,d", [(404, 128, 2048), (1, 128, 2048), (7, 60, 768), (33, 128, 4100)])
+def test_router_logits_and_routing(cuda, tokens, experts, d):
+    """The fp32 router GEMV against float64, then routing on its logits bit-exact against the oracle."""
+    rng = np.random.default_rng(tokens + experts + d)
+    w = (rng.standard_normal((experts, d)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((tokens, d)).astype(np.float32)
+    logits = torch.empty(tokens, experts, device=cuda)
+    ids = torch.empty(tokens, 8, dtype=torch.int32, device=cuda)
+    wts = torch.empty(tokens, 8, device=cuda)
+    mq.router(t(w, cuda), t(x, cuda), ids, wts, topk=8, logits=logits)
+    torch.cuda.synchronize()
+    got = logits.cpu().numpy()
+    ref = x.astype(np.float64) @ w.astype(np.float64).T
+    assert normwise(got, ref) <= 1e-5
+    rid, rw = omoe.route(got, 8)
+    np.testing.assert_array_equal(ids.cpu().numpy(), rid)
+    np.testing.assert_allclose(wts.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
