@@ -291,6 +291,23 @@ def run_mq(args):
                          "frac_of_measured_bf16_peak": round(flops / (pms * 1e-3) / 1e12 / tflops_peak, 4)}
         del gp
 
+    # ---- secondary: ternary prefill GEMM (p_gemm_t2), Qwen3-8B projections, 512 rows, fp16 x -----------
+    tprefill = {}
+    trng = np.random.default_rng(11)
+    for name, n, k in synth.QWEN3_TERNARY[:2]:
+        lo, hi = shard(n, world, rank)
+        tw_, ts_ = synth.ternary_matrix(trng, n, k)
+        tx_ = torch.from_numpy(trng.standard_normal((512, k)).astype(np.float16)).to(dev)
+        tw_d = torch.from_numpy(np.ascontiguousarray(tw_[:, lo:hi]).view(np.int32)).to(dev)
+        ts_d = torch.from_numpy(np.ascontiguousarray(ts_[:, lo:hi])).to(dev)
+        ty_ = torch.empty(512, hi - lo, device=dev)
+        gt_ = graph_of(lambda: [mq.p_gemm_t2(tx_, tw_d, ts_d, ty_, hi - lo, k, 512) for _ in range(10)])
+        tms = max_over_ranks(time_graphs([gt_], 10, stream) / 10, world)
+        flops = 2.0 * 512 * n * k
+        tprefill[name] = {"shape": [n, k], "rows": 512, "ms": round(tms, 5), "TFLOP/s": round(flops / (tms * 1e-3) / 1e12, 1),
+                          "frac_of_measured_bf16_peak": round(flops / (tms * 1e-3) / 1e12 / tflops_peak, 4)}
+        del gt_
+
     # ---- secondary: the decode layer at batch 64 through the tensor-core path
     b64 = synth.llama_layer(batch=64, seed=0)
     b64_graphs = []
@@ -346,6 +363,7 @@ def run_mq(args):
             "per_matrix_ms": per_matrix,
             "ternary_gemv": tern,
             "prefill_gemm": prefill,
+            "ternary_prefill_gemm": tprefill,
             "decode_batch64": decode64,
             "moe": moe_res,
             "gpu_launches": args.steps * len(mats),

@@ -127,6 +127,17 @@ MQ_API int mq_gemm_q4_noalloc(const uint32_t *wq, const uint16_t *ws, const floa
 MQ_API int mq_tgemv(const uint16_t *x, const uint32_t *w, const uint16_t *s, float *y, int64_t n, int64_t k,
              int batch, void *stream);
 
+/*
+ * Prefill GEMM over ternary weights on the tcgen05 tensor cores: y[t][c] (+)= sum_k x[t][k] * W[c][k]
+ * for t < m, W in mq_tgemv's transposed layout (w [k/16][n] 2-bit codes, s [k/128][n] fp16 scales).
+ * Replaces p_gemm_t2 (bonsai/kernels/prefill.mojo:155-164, argument order x, w, params, y, n, k).
+ * x: [m][k] fp16 (MQ_F16) or fp32 (MQ_F32, converted to fp16 in `workspace`,
+ * mq_gemm_q4_workspace_size(m, k, MQ_F32) bytes); y: [m][n] fp32. k % 256 == 0, n % 4 == 0.
+ * The weights are exact in fp16; x is rounded to fp16; accumulation is fp32.
+ */
+MQ_API int mq_gemm_t2(const void *x, int x_dtype, const uint32_t *w, const uint16_t *s, float *y, int64_t n, int64_t k,
+                      int64_t m, int add, void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- top-k MoE on int4 experts (Qwen3-MoE layout) ------------------------------------------------
  * Expert weights are one word-layout matrix each: gate|up [experts * 2fe][d/8] (expert e's gate rows
  * e*2fe .. e*2fe+fe-1, its up rows the next fe; qwen3moe/export.py:166-169) and down [experts * d][fe/8],

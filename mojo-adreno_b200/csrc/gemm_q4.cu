@@ -48,7 +48,11 @@ constexpr int kWTileBytes = kBM * 32;
 // a = silu(gate) * up as fp16. MODE 2 (MoE down): per expert, a plain fp32 product. In MODE 1 and 2
 // the tokens are rows of an expert-sorted X and the CTA's (expert, first row, rows) comes from a
 // device tile table (mq_moe_group).
-enum { kDense = 0, kGateUp = 1, kGrouped = 2 };
+// MODE 3: dense Y = X W^T with ternary W in the transposed 2-bit layout of mq_tgemv (word
+// (k / 16) * n + col holds codes k .. k + 15 of output col, weight (code - 1) * s[k / 128][col]):
+// p_gemm_t2 (bonsai/kernels/prefill.mojo:155-164).
+enum { kDense = 0, kGateUp = 1, kGrouped = 2, kTernary = 3 };
+constexpr int kTWTileBytes = 4 * kBM * 4;  // ternary W per stage: 4 word rows x 128 outputs
 
 struct Params {
   const __half *ws;
@@ -81,6 +85,25 @@ __host__ __device__ inline Layout layout(int bn, int stages) {
   L.tmem_slot = L.bars + (3 * kMaxStages + 1) * 8;
   L.total = L.tmem_slot + 16;
   return L;
+}
+
+// fp16 (c - 1) * s for the 8 ternary codes in bits [shift, shift + 16) of w, in k order (16 bytes):
+// codes c0, c1 of a nibble become the fp16 pair (1024 + c0, 1024 + c1), minus 1025, times s (exact).
+__device__ __forceinline__ uint4 dequant_t2(uint32_t w, int shift, __half2 s2) {
+  constexpr uint32_t kOne = 0x3C003C00u;   // fp16x2 (1, 1)
+  constexpr uint32_t kOff = 0xE401E401u;   // fp16x2 (-1025, -1025)
+  const __half2 one = *reinterpret_cast<const __half2 *>(&kOne);
+  const __half2 off = *reinterpret_cast<const __half2 *>(&kOff);
+  uint32_t out[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t t = w >> (shift + 4 * p);
+    const uint32_t h = (t & 3u) | ((t & 0xCu) << 14) | 0x64006400u;
+    __half2 f = __hfma2(*reinterpret_cast<const __half2 *>(&h), one, off);
+    f = __hmul2(f, s2);
+    out[p] = *reinterpret_cast<uint32_t *>(&f);
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
 // fp16 (q - 8) * s for the 8 nibbles of a word, in k order, as 4 half2 (16 bytes).
@@ -123,7 +146,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   int tm = t % p.tiles_m, tn = (t / p.tiles_m) % p.tiles_n, split = t / (p.tiles_m * p.tiles_n);
   int n0 = tn * kBM, m0 = tm * p.bn, mcount = p.m - m0, expert = 0;
   griddep_launch_dependents();
-  if (MODE != kDense) {  // grouped: work tile from the device table
+  if (MODE == kGateUp || MODE == kGrouped) {  // grouped: work tile from the device table
     griddep_wait();      // the table is written by earlier work on the stream
     const int entry = t / p.tiles_n;
     tn = t % p.tiles_n;
@@ -155,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_d = *tmem_slot;
-  if (MODE == kDense) griddep_wait();  // the set-up above touched no global memory
+  if (MODE == kDense || MODE == kTernary) griddep_wait();  // the set-up above touched no global memory
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------------------------------------------------
@@ -169,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tmap(&xmap);
     }
     __syncwarp();
-    const uint32_t bytes = kWTileBytes + p.bn * 128;
+    const uint32_t bytes = (MODE == kTernary ? kTWTileBytes : kWTileBytes) + p.bn * 128;
     // The loops of all three roles keep their ring slot, phase and k block as running counters: a
     // single issuing thread retires only a few instructions per stage's worth of MMA time, so no
     // division or descriptor rebuild may sit in its path.
@@ -192,6 +215,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           dst = smem + L.x + s * p.bn * 128;
           cx = kb * kBK;
           cy = m0;
+        } else if (MODE == kTernary) {  // W: 4 word rows (64 k) x 128 outputs
+          dst = smem + L.w + s * kWTileBytes;
+          cx = n0;
+          cy = kb * (kBK / 16);
         } else {  // W: 128 rows (dense), or 64 gate rows (lane 0) and the matching 64 up rows (lane 1)
           dst = smem + L.w + s * kWTileBytes + lane * (kWTileBytes / 2);
           cx = kb * (kBK / 8);
@@ -262,6 +289,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       dst[0] = dst[1] = dst[2] = dst[3] = 0u;
       if (4 * quad >= nk) return;
       const int kb = kblock(4 * quad);
+      if (MODE == kTernary) {  // scales [k/128][n]: this row's two groups of the quad
+        const size_t g0 = static_cast<size_t>(kb * kBK / 128);
+        const __half2 v = __halves2half2(p.ws[g0 * p.n + grow], p.ws[(g0 + 1) * p.n + grow]);
+        dst[0] = *reinterpret_cast<const uint32_t *>(&v);
+        return;
+      }
       const __half *src = p.ws + static_cast<size_t>(grow) * spr + kb * kBK / G;
       if (kHalvesPerQuad == 8) {
         const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src));
@@ -303,12 +336,21 @@ __global__ void __launch_bounds__(kThreads, 2)
             const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[0]);
             s2 = (u >> 1) ? __high2half2(pair) : __low2half2(pair);
           }
-          const uint4 w = *reinterpret_cast<const uint4 *>(smem + L.w + s * kWTileBytes + row * 32 + half * 16);
-          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
           uint8_t *a = a_row + s * kATileBytes;
+          if (MODE == kTernary) {  // word rows 2 half, 2 half + 1 of this output: codes k = 32 half ..
+            const uint8_t *wt = smem + L.w + s * kWTileBytes + row * 4;
+            const uint32_t w0 = *reinterpret_cast<const uint32_t *>(wt + (2 * half) * kBM * 4);
+            const uint32_t w1 = *reinterpret_cast<const uint32_t *>(wt + (2 * half + 1) * kBM * 4);
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<uint4 *>(a + (((4 * half + c) ^ xr) << 4)) = dequant_word(wv[c], s2);
+            for (int c = 0; c < 4; ++c)
+              *reinterpret_cast<uint4 *>(a + (((4 * half + c) ^ xr) << 4)) = dequant_t2(c < 2 ? w0 : w1, 16 * (c & 1), s2);
+          } else {
+            const uint4 w = *reinterpret_cast<const uint4 *>(smem + L.w + s * kWTileBytes + row * 32 + half * 16);
+            const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              *reinterpret_cast<uint4 *>(a + (((4 * half + c) ^ xr) << 4)) = dequant_word(wv[c], s2);
+          }
           fence_proxy_async_smem();
         }
         mbar_arrive(&deq[s]);
@@ -330,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     tc_fence_after();
     const bool live = __all_sync(0xffffffffu, ok && !*abort_flag && nk > 0);  // tcgen05.ld is warp-collective
     const uint32_t taddr = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16);
-    if (MODE == kDense && live) {
+    if ((MODE == kDense || MODE == kTernary) && live) {
       const int r = n0 + row;
       for (int c0 = 32 * half; c0 < p.bn; c0 += 64) {
         float v[32];
@@ -407,7 +449,7 @@ __global__ void f32_to_f16_kernel(const float4 *__restrict__ x, uint2 *__restric
   }
 }
 
-template <int G>
+template <int G, int MODE = kDense>
 int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream, const DeviceInfo &dev) {
   // Tiles: tokens split as evenly as possible into tiles of a multiple of 16. Up to 128 tokens: one
   // tile, two CTAs per SM (two independent pipelines hide each other's latencies). More: tiles of up
@@ -437,9 +479,15 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
   MQ_REQUIRE(smem <= dev.smem_optin, MQ_EUNSUPPORTED, "mq_gemm_q4: tile of %d tokens needs %zu B of shared memory", p.bn,
              smem);
   CUtensorMap wmap, xmap;
-  if (int rc = encode_tmap_2d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.k / 8, p.n, static_cast<uint64_t>(p.k) / 2,
-                              kBK / 8, kBM, CU_TENSOR_MAP_SWIZZLE_NONE, "mq_gemm_q4 weights"))
+  if (MODE == kTernary) {  // [k/16][n] words: boxes of 128 outputs x 4 word rows
+    if (int rc = encode_tmap_2d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.n, p.k / 16, static_cast<uint64_t>(p.n) * 4,
+                                kBM, kBK / 16, CU_TENSOR_MAP_SWIZZLE_NONE, "mq_gemm_t2 weights"))
+      return rc;
+  } else if (int rc = encode_tmap_2d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.k / 8, p.n,
+                                     static_cast<uint64_t>(p.k) / 2, kBK / 8, kBM, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                     "mq_gemm_q4 weights")) {
     return rc;
+  }
   if (int rc = encode_tmap_2d(&xmap, x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k, p.m, static_cast<uint64_t>(p.k) * 2, kBK,
                               p.bn, CU_TENSOR_MAP_SWIZZLE_128B, "mq_gemm_q4 activations"))
     return rc;
@@ -447,7 +495,7 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
     cudaError_t e = cudaMemsetAsync(p.y, 0, static_cast<size_t>(p.m) * p.n * sizeof(float), stream);
     if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_gemm_q4: zeroing y: %s", cudaGetErrorString(e));
   }
-  auto kern = gemm_q4_kernel<G, kDense>;
+  auto kern = gemm_q4_kernel<G, MODE>;
   static size_t configured = 0;
   if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -650,6 +698,41 @@ extern "C" int mq_gemm_q4_noalloc(const uint32_t *wq, const uint16_t *ws, const 
   MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(ws, 16) && mq::aligned(x, 16) && mq::aligned(y, 4), MQ_EALIGN,
              "mq_gemm_q4_noalloc: wq, ws and x must be 16-byte aligned, y 4-byte aligned");
   return mq::gemm_q4_noalloc_run(wq, ws, x, y, n, k, m, group, add, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mq_gemm_t2(const void *x, int x_dtype, const uint32_t *w, const uint16_t *s, float *y, int64_t n, int64_t k,
+                          int64_t m, int add, void *workspace, size_t workspace_bytes, void *stream) {
+  MQ_REQUIRE(x && w && s && y, MQ_EINVAL, "mq_gemm_t2: null pointer");
+  MQ_REQUIRE(n > 0 && k > 0 && m > 0 && n < (1LL << 31) && k <= (1 << 20) && m < (1LL << 24), MQ_EINVAL,
+             "mq_gemm_t2: bad shape n=%lld k=%lld m=%lld", static_cast<long long>(n), static_cast<long long>(k),
+             static_cast<long long>(m));
+  MQ_REQUIRE(k % 256 == 0 && n % 4 == 0, MQ_EINVAL, "mq_gemm_t2: k must be a multiple of 256 and n of 4");
+  MQ_REQUIRE(x_dtype == MQ_F32 || x_dtype == MQ_F16, MQ_EINVAL, "mq_gemm_t2: x_dtype must be MQ_F32 or MQ_F16");
+  MQ_REQUIRE(mq::aligned(w, 16) && mq::aligned(s, 2) && mq::aligned(x, 16) && mq::aligned(y, 4), MQ_EALIGN,
+             "mq_gemm_t2: w and x must be 16-byte aligned");
+  mq::DeviceInfo dev;
+  if (int rc = mq::device_info(&dev)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const __half *x16 = static_cast<const __half *>(x);
+  if (x_dtype == MQ_F32) {
+    const size_t need = static_cast<size_t>(m) * k * 2;
+    MQ_REQUIRE(workspace && workspace_bytes >= need && mq::aligned(workspace, 16), MQ_EINVAL,
+               "mq_gemm_t2: fp32 activations need a 16-byte aligned workspace of %zu bytes (got %zu)", need,
+               workspace_bytes);
+    const int64_t n4 = m * k / 4;
+    const int grid = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(dev.sms) * 8));
+    mq::gemm::f32_to_f16_kernel<<<grid, 256, 0, st>>>(static_cast<const float4 *>(x), static_cast<uint2 *>(workspace), n4);
+    if (int rc = mq::check_launch("mq_gemm_t2 (fp32 -> fp16)")) return rc;
+    x16 = static_cast<const __half *>(workspace);
+  }
+  mq::gemm::Params p{};
+  p.ws = reinterpret_cast<const __half *>(s);
+  p.y = y;
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.m = static_cast<int>(m);
+  p.add = add != 0;
+  return mq::gemm::launch<128, mq::gemm::kTernary>(w, x16, p, st, dev);
 }
 
 extern "C" int mq_moe_gemm_q4(int mode, const uint32_t *wq, const uint16_t *ws, const uint16_t *xs, int64_t pairs,

@@ -18,6 +18,7 @@ SIGNATURES = {
     "mq_gemm_q4": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_int, c_int, c_vp, c_size, c_vp]),
     "mq_gemm_q4_noalloc": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_int, c_int, c_vp]),
     "mq_tgemv": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_vp]),
+    "mq_gemm_t2": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_int, c_vp, c_size, c_vp]),
     "mq_moe_router": (c_int, [c_vp, c_vp, c_vp, c_i64, c_int, c_i64, c_vp]),
     "mq_moe_route": (c_int, [c_vp, c_vp, c_vp, c_i64, c_int, c_int, c_vp]),
     "mq_moe_group": (c_int, [c_vp, c_i64, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),

@@ -13,7 +13,8 @@ from ._lib import MQError, lib
 
 MQ_F32, MQ_F16 = 0, 1
 
-__all__ = ["MQ_F32", "MQ_F16", "MQError", "gemv_q4", "gemv_add_q4", "p_gemm_q4", "unpack_q4", "project", "device_status"]
+__all__ = ["MQ_F32", "MQ_F16", "MQError", "gemv_q4", "gemv_add_q4", "p_gemm_q4", "p_gemm_t2", "unpack_q4", "project",
+           "device_status"]
 
 
 def _stream():
@@ -118,6 +119,25 @@ def project(x, w, s, y, n, k):
     _need(s, "s", (torch.float16,), k // 128 * n)
     _need(y, "y", (torch.float32,), batch * n)
     lib.call("mq_tgemv", _p(x), _p(w), _p(s), _p(y), n, k, batch, _stream())
+    return y
+
+
+def p_gemm_t2(x, w, s, y, n, k, rows=None, add=False):
+    """Y[t, c] (+)= sum_k X[t, k] W[c, k] for ternary W on the tcgen05 tensor cores: p_gemm_t2(x, w, params,
+    y, n, k) of bonsai/kernels/prefill.mojo:155-164. x: fp32 or fp16 [rows, k]; w: int32/uint32
+    [k/16, n]; s: fp16 [k/128, n]; y: fp32 [rows, n]."""
+    _need(x, "x", (torch.float32, torch.float16))
+    rows = x.numel() // k if rows is None else rows
+    _need(w, "w", _WORDS, k // 16 * n)
+    _need(s, "s", (torch.float16,), k // 128 * n)
+    _need(y, "y", (torch.float32,))
+    if y.numel() < rows * n:
+        raise MQError(-1, f"y: {y.numel()} elements < rows * n = {rows * n}")
+    dt = MQ_F16 if x.dtype == torch.float16 else MQ_F32
+    nbytes = lib.mq_gemm_q4_workspace_size(rows, k, dt)
+    work = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=x.device) if nbytes else None
+    lib.call("mq_gemm_t2", _p(x), dt, _p(w), _p(s), _p(y), n, k, rows, int(bool(add)),
+             _p(work) if work is not None else None, nbytes, _stream())
     return y
 
 
