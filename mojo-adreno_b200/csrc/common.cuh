@@ -177,6 +177,25 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
+// 2-D tiled TMA store (or, with add, an fp32 reduce-add) of the box at (x, y) from shared memory,
+// in the calling thread's bulk group; x times the element size must be a multiple of 16 bytes and
+// both coordinates non-negative. Elements outside the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y, bool add) {
+  if (add)
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+  else
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+// Closes the calling thread's bulk group and waits until its copies are complete (written).
+__device__ __forceinline__ void bulk_commit_and_wait() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // Warms L2 with `bytes` (a multiple of 16) of global memory from a 16-byte aligned address.
 __device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes) : "memory");

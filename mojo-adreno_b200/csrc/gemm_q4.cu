@@ -70,6 +70,7 @@ struct Params {
   int kb_split;  // 64-k blocks per split (a multiple of 4)
   int tiles_n, tiles_m;
   uint32_t tmem_cols;
+  int y_tma;  // MODE 0, 3: write y with TMA stores from a shared-memory tile (y 16-byte aligned, n % 4 == 0)
 };
 
 struct Layout {
@@ -128,7 +129,8 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, __half2 s2) {
 
 template <int G, int MODE>
 __global__ void __launch_bounds__(kThreads, 2)
-    gemm_q4_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, const Params p) {
+    gemm_q4_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                   const __grid_constant__ CUtensorMap ymap, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const Layout L = layout(p.bn, p.stages);
@@ -372,7 +374,28 @@ __global__ void __launch_bounds__(kThreads, 2)
     tc_fence_after();
     const bool live = __all_sync(0xffffffffu, ok && !*abort_flag && nk > 0);  // tcgen05.ld is warp-collective
     const uint32_t taddr = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16);
-    if ((MODE == kDense || MODE == kTernary) && live) {
+    if ((MODE == kDense || MODE == kTernary) && p.y_tma) {
+      // The tile goes to shared memory as [token][128 rows] fp32 (the rings are free: every copy landed
+      // and every MMA finished), then one TMA store -- or an fp32 reduce-add with add or split K --
+      // writes it; the tensor map clips tokens past m and rows past n. Far fewer instructions than a
+      // warp store per 32 values, which left the write-out as a third of the kernel's time.
+      float *tile = reinterpret_cast<float *>(smem + L.a);  // [bn][kBM]
+      if (live) {
+        for (int c0 = 32 * half; c0 < p.bn; c0 += 64) {
+          float v[32];
+          tmem_ld32(taddr + c0, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (c0 + j < p.bn) tile[(c0 + j) * kBM + row] = v[j];
+        }
+      }
+      fence_proxy_async_smem();  // each thread orders its tile writes before the TMA's reads
+      named_bar_sync(1, 32 * kDeqWarps);
+      if (warp == 2 && lane == 0 && live) {  // live is the same in every epilogue warp
+        tma_store_2d(&ymap, tile, n0, m0, p.add || p.splitk > 1);
+        bulk_commit_and_wait();
+      }
+    } else if ((MODE == kDense || MODE == kTernary) && live) {
       const int r = n0 + row;
       for (int c0 = 32 * half; c0 < p.bn; c0 += 64) {
         float v[32];
@@ -502,7 +525,16 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
     if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_gemm_q4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured = smem;
   }
-  return launch_overlapped(kern, dim3(tiles * p.splitk), dim3(kThreads), smem, stream, "mq_gemm_q4", wmap, xmap, p);
+  // y through TMA stores when the tensor map can describe it (16-byte base and row stride) and the
+  // [bn][128] fp32 staging tile fits where the rings were.
+  CUtensorMap ymap = xmap;  // not read unless y_tma
+  p.y_tma = aligned(p.y, 16) && p.n % 4 == 0 && static_cast<size_t>(p.bn) * kBM * 4 <= layout(p.bn, p.stages).bars;
+  if (p.y_tma) {
+    if (int rc = encode_tmap_2d(&ymap, p.y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.n, p.m, static_cast<uint64_t>(p.n) * 4,
+                                kBM, p.bn, CU_TENSOR_MAP_SWIZZLE_NONE, "mq_gemm_q4 output"))
+      return rc;
+  }
+  return launch_overlapped(kern, dim3(tiles * p.splitk), dim3(kThreads), smem, stream, "mq_gemm_q4", wmap, xmap, ymap, p);
 }
 
 template <int G, int MODE>
@@ -547,8 +579,9 @@ int launch_grouped(const uint32_t *wq, const __half *ws, const __half *xs, int64
     if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_moe_gemm_q4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured = smem;
   }
+  p.y_tma = 0;
   return launch_overlapped(kern, dim3(max_tiles * p.tiles_n), dim3(kThreads), smem, stream, "mq_moe_gemm_q4", wmap, xmap,
-                           p);
+                           xmap, p);
 }
 
 }  // namespace gemm
