@@ -90,6 +90,17 @@ MQ_API int mq_gemv_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int
                int64_t n, int64_t k, int group, int batch, int add, void *stream);
 
 /*
+ * Fused gate|up decode GEMV: a[b][j] = silu(W[j] . x[b]) * (W[f + j] . x[b]) for j < f, b < batch,
+ * silu(g) = g / (1 + exp(-g)). Replaces gate_up_q4 (lfm2/kernels/lk.mojo:154-167; argument order
+ * wq, ws, x, a, cols, f): W is the fused [2f][k] gate|up matrix in mq_gemv_q4's layout (gate rows
+ * 0..f-1, up rows f..2f-1), so the SwiGLU costs no extra launch and no fp32 round trip of gate|up.
+ * Each product is computed exactly as mq_gemv_q4 computes that row. f % 16 == 0, 1 <= batch <= 4;
+ * other limits as mq_gemv_q4.
+ */
+MQ_API int mq_gate_up_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *a, int64_t f,
+                         int64_t k, int group, int batch, void *stream);
+
+/*
  * Prefill GEMM over int4 weights on the tcgen05 tensor cores: y[t][r] (+)= sum_c W[r][c] * x[t][c]
  * for t < m tokens. Replaces p_gemm_q4 (llama/kernels/prefill/p_gemm_q4.mojo:26-62, argument order
  * wq, ws, x, y, n, k) and gemm_q4 (lfm2/kernels/lk.mojo:458-495), without their rows % 128 and
@@ -126,6 +137,25 @@ MQ_API int mq_gemm_q4_noalloc(const uint32_t *wq, const uint16_t *ws, const floa
  */
 MQ_API int mq_tgemv(const uint16_t *x, const uint32_t *w, const uint16_t *s, float *y, int64_t n, int64_t k,
              int batch, void *stream);
+
+/*
+ * mq_tgemv plus packed_head's argmax candidates (bonsai/kernels/kernels.mojo:490-517, select != 0):
+ * for each token b and each block of 512 consecutive outputs c (ncand = ceil(n / 512) blocks),
+ * candidates[(b * ncand + c) * 3 + 0..2] = (largest y in the block, its index as a float, 1.0 if any
+ * y in the block is not finite else 0.0); among equal values the lowest index wins. Only outputs
+ * i < n compete (the reference's lanes past n compete with the value 0 at an index >= n).
+ * n <= 4718592; other arguments and limits as mq_tgemv.
+ */
+MQ_API int mq_tgemv_head(const uint16_t *x, const uint32_t *w, const uint16_t *s, float *y, float *candidates,
+                         int64_t n, int64_t k, int batch, void *stream);
+
+/*
+ * Greedy token from head candidates, on the device: index[b] = the index of the best of the ncand
+ * candidates (value, index, flag) of token b, the lowest index among equal values (best_of,
+ * lfm2/kernels/dsk.mojo:442-465; the host loop greedy() of bonsai/bonsai_vk.c:506-515), or -1 when a
+ * candidate's non-finite flag is set (where greedy() stops with "nonfinite logits").
+ */
+MQ_API int mq_head_argmax(const float *candidates, int64_t ncand, int batch, int32_t *index, void *stream);
 
 /*
  * Prefill GEMM over ternary weights on the tcgen05 tensor cores: y[t][c] (+)= sum_k x[t][k] * W[c][k]
@@ -194,6 +224,12 @@ MQ_API int mq_moe_gemm_q4(int mode, const uint32_t *wq, const uint16_t *ws, cons
 MQ_API int mq_moe_gemv_q4(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const float *x, float *y,
                           const int32_t *ids, int ngroups, int group_rows, int rows_per_group, int64_t k, int group,
                           int x_per_group, void *stream);
+
+/* moe_gate_up in one launch (qwen3moe/kernels/moek.mojo:200-210): a[i][j] = silu(W[e_i * 2fe + j] . x) *
+ * (W[e_i * 2fe + fe + j] . x) for i < ngroups, j < fe, e_i = ids[i]; the fused form of mq_moe_gemv_q4
+ * (rows_per_group 2fe) followed by mq_moe_silu_mul, with the same products. fe % 16 == 0, fp32 x. */
+MQ_API int mq_moe_gate_up_q4(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const float *x, float *a,
+                             const int32_t *ids, int ngroups, int64_t fe, int64_t k, int group, void *stream);
 
 /* a[r][j] = silu(h[r][j]) * h[r][fe + j] in fp32 (moe_gate_up's SwiGLU, moek.mojo:200-210). */
 MQ_API int mq_moe_silu_mul(const float *h, float *a, int64_t rows, int64_t fe, void *stream);

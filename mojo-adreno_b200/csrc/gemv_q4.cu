@@ -63,18 +63,25 @@ struct Params {
   const int32_t *ids;
   int group_rows, tpg, xpg;
   int wrows;  // rows of the weight matrix (== n without expert indirection)
+  // Gate|up with the SwiGLU fused (gu != 0): a tile is 16 outputs j; slot rows 0..15 hold the gate
+  // rows of those outputs, rows 16..31 the up rows, gu_off rows further down the matrix, and the
+  // output is silu(gate . x) * (up . x).
+  int gu, gu_off;
 };
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
 
 // First weight row of output tile `tile` (the rows themselves, or an expert's rows through ids).
 // An expert id outside the weight matrix is reported and read as expert 0.
 __device__ __forceinline__ int weight_row0(const Params &p, int tile) {
-  if (!p.ids) return tile * 32;
+  const int tr = p.gu ? kRows / 2 : kRows;  // weight rows (of one kind) per output tile
+  if (!p.ids) return tile * tr;
   int e = __ldg(p.ids + tile / p.tpg);
   if (e < 0 || e >= p.wrows / p.group_rows) {
     raise_status(kStatusMoeBadExpertId);
     e = 0;
   }
-  return e * p.group_rows + (tile % p.tpg) * 32;
+  return e * p.group_rows + (tile % p.tpg) * tr;
 }
 
 __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
@@ -157,6 +164,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_expect_tx(bar, bytes);
     tma_load_2d(dst, &wmap, bar, sk * (kSlotK / 8), wrow);
     if (p.scales_tma) tma_load_2d(dst + kWordBytes, &smap, bar, sk * kScaleHalvesTma, wrow);
+    if (p.gu) {  // 16-row boxes: the up rows into slot rows 16..31
+      tma_load_2d(dst + kWordBytes / 2, &wmap, bar, sk * (kSlotK / 8), wrow + p.gu_off);
+      if (p.scales_tma) tma_load_2d(dst + kWordBytes + 16 * 16, &smap, bar, sk * kScaleHalvesTma, wrow + p.gu_off);
+    }
   };
   griddep_launch_dependents();
   if (lane == 0) {
@@ -171,8 +182,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (!p.ids && lane < kPrefetchItems) {
     int tile, sk;
     if (items.get(lane, tile, sk)) {
-      tma_prefetch_l2_2d(&wmap, sk * (kSlotK / 8), tile * kRows);
-      if (p.scales_tma) tma_prefetch_l2_2d(&smap, sk * kScaleHalvesTma, tile * kRows);
+      for (int b = 0; b <= p.gu; ++b) {
+        const int wrow = weight_row0(p, tile) + b * p.gu_off;
+        tma_prefetch_l2_2d(&wmap, sk * (kSlotK / 8), wrow);
+        if (p.scales_tma) tma_prefetch_l2_2d(&smap, sk * kScaleHalvesTma, wrow);
+      }
     }
   }
   // x, too (every CTA reads all of it): if earlier kernels write it, their writes still land in L2,
@@ -286,7 +300,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int gi = (cg * 128 + 32 * q) / G;
 #pragma unroll
               for (int m = 0; m < 4; ++m) {
-                const int row = p.ids ? wrow0 + pr + 8 * m : min(tile * kRows + pr + 8 * m, N - 1);
+                const int row = p.gu    ? wrow0 + pr + 8 * (m & 1) + (m >> 1) * p.gu_off
+                                : p.ids ? wrow0 + pr + 8 * m
+                                        : min(tile * kRows + pr + 8 * m, N - 1);
                 sw[m] = gi < spr ? __half2float(p.ws[static_cast<size_t>(row) * spr + gi]) : 0.f;
               }
             }
@@ -341,7 +357,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           v += __shfl_xor_sync(0xffffffffu, v, 2);
           acc[t][h][hh] = v;
         }
-      if (q == 0 && t < BO) {
+      if (q == 0 && t < BO && p.gu && p.ks == 1) {  // gate (h = 0) and up (h = 1) of outputs pr, pr + 8
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int j = tile * (kRows / 2) + pr + 8 * hh;
+          if (tile < p.tiles && !aborted) p.y[static_cast<size_t>(t) * N + j] = silu_mul(acc[t][0][hh], acc[t][1][hh]);
+        }
+      } else if (q == 0 && t < BO) {
 #pragma unroll
         for (int m = 0; m < 4; ++m) {  // rows pr + 8m: (tile h = m / 2, row g or g + 8 = m % 2)
           const float v = acc[t][m >> 1][m & 1];
@@ -360,6 +382,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.ks == 1) continue;
     __syncthreads();
     const int rows = kRows * p.rt;
+    if (p.gu) {  // outputs of the round: 16 per tile, gate partials in tile rows 0..15, up in 16..31
+      const int outs = rows / 2;
+      for (int it = threadIdx.x; it < outs * BO; it += kThreads) {
+        const int rl = it / BO, tok = it % BO;
+        const int j = r * outs + rl, pb = (rl / 16) * kRows + rl % 16;
+        if (j < N) {
+          float gs = 0.f, us = 0.f;
+          for (int w = 0; w < p.ks; ++w) {
+            gs += red[(w * rows + pb) * BO + tok];
+            us += red[(w * rows + pb + 16) * BO + tok];
+          }
+          p.y[static_cast<size_t>(tok) * N + j] = silu_mul(gs, us);
+        }
+      }
+      __syncthreads();
+      continue;
+    }
     for (int it = threadIdx.x; it < rows * BO; it += kThreads) {
       const int rl = it / BO, tok = it % BO;
       const int row = r * rows + rl;
@@ -394,12 +433,13 @@ int launch(const uint32_t *wq, Params p, cudaStream_t stream, const DeviceInfo &
   MQ_REQUIRE(p.slots >= 1 && smem <= dev.smem_optin, MQ_EUNSUPPORTED,
              "mq_gemv_q4: k=%d batch=%d needs %zu B of shared memory (max %zu)", p.k, p.batch, smem, dev.smem_optin);
   CUtensorMap wmap, smap;
+  const int box = p.gu ? kRows / 2 : kRows;  // gate|up: two 16-row boxes per slot
   if (int rc = encode_tmap_2d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.k / 8, p.wrows, static_cast<uint64_t>(p.k) / 2,
-                              32, kRows, CU_TENSOR_MAP_SWIZZLE_128B, "mq_gemv_q4 weights"))
+                              32, box, CU_TENSOR_MAP_SWIZZLE_128B, "mq_gemv_q4 weights"))
     return rc;
   if (p.scales_tma) {
     if (int rc = encode_tmap_2d(&smap, p.ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k / G, p.wrows,
-                                static_cast<uint64_t>(p.k / G) * 2, kScaleHalvesTma, kRows, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                static_cast<uint64_t>(p.k / G) * 2, kScaleHalvesTma, box, CU_TENSOR_MAP_SWIZZLE_NONE,
                                 "mq_gemv_q4 scales"))
       return rc;
   } else {
@@ -456,11 +496,36 @@ int gemv_q4_small(const uint32_t *wq, const uint16_t *ws, const void *x, int x_d
   }
 }
 
+// a[t][j] = silu(W[j] . x_t) * (W[f + j] . x_t) for j < f, t < batch <= 4: the fused gate|up GEMV.
+int gemv_q4_gate_up(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *a, int64_t f, int64_t k,
+                    int group, int batch, cudaStream_t stream) {
+  DeviceInfo dev;
+  if (int rc = device_info(&dev)) return rc;
+  Params p{};
+  p.ws = reinterpret_cast<const __half *>(ws);
+  p.x = x;
+  p.y = a;
+  p.n = static_cast<int>(f);
+  p.k = static_cast<int>(k);
+  p.batch = batch;
+  p.x_f16 = x_dtype == MQ_F16;
+  p.tiles = p.n / (kRows / 2);
+  p.wrows = 2 * p.n;
+  p.gu = 1;
+  p.gu_off = p.n;
+  switch (group) {
+    case 32: return dispatch_nt<32>(wq, p, stream, dev);
+    case 64: return dispatch_nt<64>(wq, p, stream, dev);
+    default: return dispatch_nt<128>(wq, p, stream, dev);
+  }
+}
+
 // The expert-indirect GEMV of the MoE decode: y[i * rows_per_group + r] = W[ids[i] * group_rows + r] . x_i
-// for i < ngroups, r < rows_per_group, x_i = x (shared) or x + i * k (xpg). fp32 x.
+// for i < ngroups, r < rows_per_group, x_i = x (shared) or x + i * k (xpg). fp32 x. With gate_up,
+// y[i * rows_per_group + j] = silu(W[e_i * group_rows + j] . x) * (W[e_i * group_rows + rows_per_group + j] . x).
 int gemv_q4_grouped(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const float *x, float *y,
                     const int32_t *ids, int ngroups, int group_rows, int rows_per_group, int64_t k, int group, int xpg,
-                    cudaStream_t stream) {
+                    cudaStream_t stream, int gate_up) {
   DeviceInfo dev;
   if (int rc = device_info(&dev)) return rc;
   Params p{};
@@ -472,12 +537,15 @@ int gemv_q4_grouped(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const
   p.batch = xpg ? ngroups : 1;
   p.x_f16 = 0;
   p.add = 0;
-  p.tiles = p.n / kRows;
   p.wrows = static_cast<int>(wrows);
   p.ids = ids;
   p.group_rows = group_rows;
-  p.tpg = rows_per_group / kRows;
   p.xpg = xpg;
+  p.gu = gate_up != 0;
+  p.gu_off = rows_per_group;
+  const int tr = p.gu ? kRows / 2 : kRows;
+  p.tiles = p.n / tr;
+  p.tpg = rows_per_group / tr;
   switch (group) {
     case 32: return launch<32, 1>(wq, p, stream, dev);
     case 64: return launch<64, 1>(wq, p, stream, dev);
@@ -501,7 +569,39 @@ extern "C" int mq_moe_gemv_q4(const uint32_t *wq, const uint16_t *ws, int64_t wr
   MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(x, 16) && mq::aligned(y, 4), MQ_EALIGN,
              "mq_moe_gemv_q4: wq and x must be 16-byte aligned");
   return mq::gemv::gemv_q4_grouped(wq, ws, wrows, x, y, ids, ngroups, group_rows, rows_per_group, k, group, x_per_group,
-                                   static_cast<cudaStream_t>(stream));
+                                   static_cast<cudaStream_t>(stream), 0);
+}
+
+extern "C" int mq_moe_gate_up_q4(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const float *x, float *a,
+                                 const int32_t *ids, int ngroups, int64_t fe, int64_t k, int group, void *stream) {
+  MQ_REQUIRE(wq && ws && x && a && ids, MQ_EINVAL, "mq_moe_gate_up_q4: null pointer");
+  MQ_REQUIRE(ngroups >= 1 && ngroups <= 64 && fe > 0 && fe % 16 == 0 && fe <= (1 << 20), MQ_EINVAL,
+             "mq_moe_gate_up_q4: bad expert shape (fe %% 16 == 0)");
+  MQ_REQUIRE(group == 32 || group == 64 || group == 128, MQ_EINVAL, "mq_moe_gate_up_q4: group must be 32, 64 or 128");
+  MQ_REQUIRE(k > 0 && k % 32 == 0 && k % group == 0 && k <= (1 << 20) && wrows >= 2 * fe && wrows < (1LL << 31) &&
+                 wrows % (2 * fe) == 0,
+             MQ_EINVAL, "mq_moe_gate_up_q4: bad k or weight rows");
+  MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(ws, 2) && mq::aligned(x, 16) && mq::aligned(a, 4), MQ_EALIGN,
+             "mq_moe_gate_up_q4: wq and x must be 16-byte aligned");
+  return mq::gemv::gemv_q4_grouped(wq, ws, wrows, x, a, ids, ngroups, static_cast<int>(2 * fe), static_cast<int>(fe), k,
+                                   group, 0, static_cast<cudaStream_t>(stream), 1);
+}
+
+extern "C" int mq_gate_up_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *a, int64_t f,
+                             int64_t k, int group, int batch, void *stream) {
+  MQ_REQUIRE(wq && ws && x && a, MQ_EINVAL, "mq_gate_up_q4: null pointer");
+  MQ_REQUIRE(f > 0 && k > 0 && 2 * f < (1LL << 31) && k <= (1 << 20), MQ_EINVAL, "mq_gate_up_q4: bad shape f=%lld k=%lld",
+             static_cast<long long>(f), static_cast<long long>(k));
+  MQ_REQUIRE(f % 16 == 0, MQ_EINVAL, "mq_gate_up_q4: f=%lld must be a multiple of 16", static_cast<long long>(f));
+  MQ_REQUIRE(group == 32 || group == 64 || group == 128, MQ_EINVAL, "mq_gate_up_q4: group must be 32, 64 or 128 (got %d)",
+             group);
+  MQ_REQUIRE(k % 32 == 0 && k % group == 0, MQ_EINVAL, "mq_gate_up_q4: k=%lld must be a multiple of 32 and of group=%d",
+             static_cast<long long>(k), group);
+  MQ_REQUIRE(x_dtype == MQ_F32 || x_dtype == MQ_F16, MQ_EINVAL, "mq_gate_up_q4: x_dtype must be MQ_F32 or MQ_F16");
+  MQ_REQUIRE(batch >= 1 && batch <= 4, MQ_EINVAL, "mq_gate_up_q4: batch must be in 1..4 (got %d)", batch);
+  MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(ws, 2) && mq::aligned(x, 16) && mq::aligned(a, 4), MQ_EALIGN,
+             "mq_gate_up_q4: wq and x must be 16-byte aligned, a 4-byte aligned");
+  return mq::gemv::gemv_q4_gate_up(wq, ws, x, x_dtype, a, f, k, group, batch, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int mq_gemv_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y, int64_t n,

@@ -454,15 +454,14 @@ extern "C" int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, co
   const int64_t P = tokens * topk;
   if (tokens == 1 && x_dtype == MQ_F32) {
     // One token (decode): the streaming GEMV over the selected experts' rows, as moe_gate_up /
-    // moe_down do (moek.mojo:200-223): h = [gate|up]_e x, a = silu(gate) * up, z_k = down_e a_k,
-    // y (+)= sum_k w_k z_k. h lives in the z region (dead by the time z is written).
-    float *h = w.z, *a = reinterpret_cast<float *>(w.a), *z = w.z;
-    if (int rc = mq::gemv::gemv_q4_grouped(gu_wq, gu_ws, experts * 2 * fe, static_cast<const float *>(x), h, ids, topk,
-                                           static_cast<int>(2 * fe), static_cast<int>(2 * fe), d, group, 0, s))
+    // moe_down do (moek.mojo:200-223): a = silu(gate_e x) * (up_e x) in one launch, z_k = down_e a_k,
+    // y (+)= sum_k w_k z_k.
+    float *a = reinterpret_cast<float *>(w.a), *z = w.z;
+    if (int rc = mq::gemv::gemv_q4_grouped(gu_wq, gu_ws, experts * 2 * fe, static_cast<const float *>(x), a, ids, topk,
+                                           static_cast<int>(2 * fe), static_cast<int>(fe), d, group, 0, s, 1))
       return rc;
-    if (int rc = mq_moe_silu_mul(h, a, topk, fe, s)) return rc;
     if (int rc = mq::gemv::gemv_q4_grouped(dn_wq, dn_ws, experts * d, a, z, ids, topk, static_cast<int>(d),
-                                           static_cast<int>(d), fe, group, 1, s))
+                                           static_cast<int>(d), fe, group, 1, s, 0))
       return rc;
     return mq_moe_combine(z, nullptr, weights, 1, topk, d, add, y, s);
   }

@@ -23,7 +23,12 @@
 //  * Bank conflicts: lane (g, q) reads word row 4b + q and the 16-byte column chunk
 //    (g >> 1) | (g & 1) << 2; with the swizzle's XOR by row % 8 the 8 lanes of a phase hit 8
 //    distinct chunks.
+//  * Head argmax (mq_tgemv_head): with the K split off, round r of a CTA is exactly the 512 outputs
+//    of candidate block r. Each warp reduces its 32 outputs to (best, index, non-finite) with
+//    shuffles and leaves them in shared memory; the warp that arrives last at the round's counter
+//    combines the 16 and writes the candidate. No warp waits for another.
 #include <algorithm>
+#include <climits>
 
 #include "common.cuh"
 
@@ -52,7 +57,13 @@ struct Params {
   float *y;
   int n, k, batch;
   int ks, rt, tiles, nrounds, slots, scales_tma;
+  float *cand;      // head argmax candidates [batch][ncand][3], or null
+  int ncand;        // ceil(n / 512)
+  int cand_rounds;  // rounds of one CTA (shared-memory partials per round)
 };
+
+constexpr int kCandOutputs = 512;   // outputs of a candidate block = one round of 16 warps x 32
+constexpr int kMaxCandRounds = 8;   // rounds per CTA with candidates (n <= 8 * 512 * SMs)
 
 constexpr float kLimbMax = 32512.f;  // 127 * 256: |x| maps to at most this, so both limbs fit in int8
 
@@ -63,12 +74,14 @@ __device__ __forceinline__ uint32_t pack_bytes(int a, int b, int c, int d) {
 
 // Shared memory: the rings; x as mma B fragments [k/32 steps][2 NB columns][4 lanes] (uint2); per
 // (token, group) the x scale and the integer sums of the hi and lo limbs; K-split partials; barriers.
+// With candidates: per (round, warp, token) the warp's (best value, index, non-finite, -) as int4,
+// and one arrival counter per round.
 struct Layout {
-  uint32_t slots, bfrag, xs, lsum, red, bars, total;
+  uint32_t slots, bfrag, xs, lsum, red, cpart, ccnt, bars, total;
 };
 
 template <int SK>
-__host__ __device__ inline Layout layout(int k, int nb, int slots) {
+__host__ __device__ inline Layout layout(int k, int nb, int slots, int cand_rounds) {
   Layout L;
   const int kg = k / 128;
   L.slots = 0;
@@ -76,10 +89,15 @@ __host__ __device__ inline Layout layout(int k, int nb, int slots) {
   L.xs = L.bfrag + (k / 32) * 2 * nb * 4 * 8;
   L.lsum = L.xs + nb * kg * 4;
   L.red = L.lsum + nb * kg * 2 * 4;
-  L.bars = (L.red + kWarps * kCols * nb * 4 + 7) / 8 * 8;
+  L.cpart = (L.red + kWarps * kCols * nb * 4 + 15) / 16 * 16;
+  L.ccnt = L.cpart + cand_rounds * kWarps * nb * 16;
+  L.bars = (L.ccnt + cand_rounds * 4 + 7) / 8 * 8;
   L.total = L.bars + kWarps * kMaxSlots * 8;
   return L;
 }
+
+// (v, i) beats (bv, bi): larger value, or the same value at a lower index.
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
 struct Items {
   int rtl, kw, spw, per_round, rt, tiles, grid, cta;
@@ -99,7 +117,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kGroups = Slot<SK>::kGroups, kScaleBytes = Slot<SK>::kScaleBytes, kSlotBytes = Slot<SK>::kSlotBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  const Layout L = layout<SK>(p.k, NB, p.slots);
+  const Layout L = layout<SK>(p.k, NB, p.slots, p.cand_rounds);
   const int K = p.k, N = p.n, S = p.slots;
   const int kg = K / 128;
   const int nslotk = (K + kSlotK - 1) / kSlotK;
@@ -144,6 +162,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   float *xs = reinterpret_cast<float *>(smem + L.xs);         // [NB][kg]
   int *lsum = reinterpret_cast<int *>(smem + L.lsum);         // [NB][kg][hi, lo]
   float *red = reinterpret_cast<float *>(smem + L.red);       // [kWarps][32][NB]
+  int4 *cpart = reinterpret_cast<int4 *>(smem + L.cpart);     // [cand_rounds][kWarps][NB]
+  int *ccnt = reinterpret_cast<int *>(smem + L.ccnt);         // [cand_rounds]
+  for (int i = threadIdx.x; i < p.cand_rounds; i += kThreads) ccnt[i] = 0;  // visible after the staging barrier
 
   // Stage x: item (token t, word row wr) = x[16 wr .. 16 wr + 15]; the 8 items of a group are 8
   // consecutive lanes, which share its scale and limb sums. For step 2b + h (word rows 4b .. 4b + 3,
@@ -214,7 +235,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t u = 0, u_abort = 0;
   bool aborted = false;
 
-  for (int r = blockIdx.x; r < p.nrounds; r += gridDim.x) {
+  int jr = 0;  // this CTA's round count
+  for (int r = blockIdx.x; r < p.nrounds; r += gridDim.x, ++jr) {
     const int tile = r * p.rt + items.rtl;
     const int col = tile * kCols + 4 * cgc;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};  // token q, outputs col .. col + 3
@@ -287,6 +309,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int o = 0; o < 4; ++o) red[(items.kw * rows + items.rtl * kCols + 4 * cgc + o) * NB + q] = acc[o];
       }
     }
+    if (p.cand) {  // ks == 1: this round is candidate block r, this warp its outputs 32 * warp ..
+      float bv = -INFINITY;
+      int bi = INT_MAX, bad = 0;
+      if (q < NB && tile < p.tiles && col < N) {  // n % 4 == 0: all four outputs exist
+#pragma unroll
+        for (int o = 0; o < 4; ++o) {
+          bad |= !isfinite(acc[o]);
+          if (better(acc[o], col + o, bv, bi)) bv = acc[o], bi = col + o;
+        }
+      }
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {  // the 8 lanes of token q
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+        if (better(ov, oi, bv, bi)) bv = ov, bi = oi;
+      }
+      if (lane < NB) {
+        cpart[(jr * kWarps + warp) * NB + lane] = make_int4(__float_as_int(bv), bi, bad, 0);
+        __threadfence_block();
+      }
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = atomicAdd(&ccnt[jr], 1) == kWarps - 1;
+      if (__shfl_sync(0xffffffffu, last, 0)) {  // every warp's partial of this round is in place
+        __threadfence_block();
+        if (lane < NB) {
+          float cv = -INFINITY;
+          int ci = INT_MAX, cbad = 0;
+          for (int w = 0; w < kWarps; ++w) {  // warps in output order
+            const int4 e = cpart[(jr * kWarps + w) * NB + lane];
+            cbad |= e.z;
+            if (better(__int_as_float(e.x), e.y, cv, ci)) cv = __int_as_float(e.x), ci = e.y;
+          }
+          float *c = p.cand + (static_cast<size_t>(lane) * p.ncand + r) * 3;
+          c[0] = cv;
+          c[1] = static_cast<float>(ci);
+          c[2] = cbad ? 1.f : 0.f;
+        }
+      }
+    }
     if (p.ks == 1) continue;
     __syncthreads();
     for (int it = threadIdx.x; it < rows * NB; it += kThreads) {
@@ -311,9 +374,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int NB, int SK>
 int launch_sk(const uint32_t *w, Params p, cudaStream_t stream, const DeviceInfo &dev) {
   using Sl = Slot<SK>;
+  const int nslotk = (p.k + SK - 1) / SK;
+  int ks = 1;  // with candidates a round must be a whole 512-output block: no K split
+  while (!p.cand && ks < kWarps && ks < nslotk && (p.tiles * ks + kWarps - 1) / kWarps < dev.sms) ks *= 2;
+  p.ks = ks;
+  p.rt = kWarps / ks;
+  p.nrounds = (p.tiles + p.rt - 1) / p.rt;
+  const int grid = std::min(p.nrounds, dev.sms);
+  p.cand_rounds = p.cand ? (p.nrounds + grid - 1) / grid : 0;
+  MQ_REQUIRE(p.cand_rounds <= kMaxCandRounds, MQ_EINVAL, "mq_tgemv_head: n=%d exceeds %d outputs on this device", p.n,
+             kMaxCandRounds * kCandOutputs * dev.sms);
   Layout L{};
   for (p.slots = kMaxSlots; p.slots >= 1; --p.slots) {
-    L = layout<SK>(p.k, NB, p.slots);
+    L = layout<SK>(p.k, NB, p.slots, p.cand_rounds);
     if (L.total + 1024 <= dev.smem_optin) break;
   }
   const size_t smem = L.total + 1024;
@@ -332,12 +405,6 @@ int launch_sk(const uint32_t *w, Params p, cudaStream_t stream, const DeviceInfo
   } else {
     smap = wmap;  // not read
   }
-  const int nslotk = (p.k + SK - 1) / SK;
-  int ks = 1;
-  while (ks < kWarps && ks < nslotk && (p.tiles * ks + kWarps - 1) / kWarps < dev.sms) ks *= 2;
-  p.ks = ks;
-  p.rt = kWarps / ks;
-  p.nrounds = (p.tiles + p.rt - 1) / p.rt;
   auto kern = tgemv_kernel<NB, SK>;
   static size_t configured = 0;
   if (smem > configured) {
@@ -345,13 +412,12 @@ int launch_sk(const uint32_t *w, Params p, cudaStream_t stream, const DeviceInfo
     if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_tgemv: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured = smem;
   }
-  const int grid = std::min(p.nrounds, dev.sms);
   return launch_overlapped(kern, dim3(grid), dim3(kThreads), smem, stream, "mq_tgemv", wmap, smap, p);
 }
 
 template <int NB>
 int launch(const uint32_t *w, Params p, cudaStream_t stream, const DeviceInfo &dev) {
-  const Layout big = layout<1024>(p.k, NB, 1);
+  const Layout big = layout<1024>(p.k, NB, 1, p.cand ? kMaxCandRounds : 0);
   if (big.total + 1024 <= dev.smem_optin) return launch_sk<NB, 1024>(w, p, stream, dev);
   return launch_sk<NB, 512>(w, p, stream, dev);
 }
@@ -359,31 +425,90 @@ int launch(const uint32_t *w, Params p, cudaStream_t stream, const DeviceInfo &d
 }  // namespace tg
 }  // namespace mq
 
-extern "C" int mq_tgemv(const uint16_t *x, const uint32_t *w, const uint16_t *s, float *y, int64_t n, int64_t k, int batch,
-                        void *stream) {
+namespace mq {
+namespace tg {
+
+int tgemv_run(const uint16_t *x, const uint32_t *w, const uint16_t *s, float *y, float *cand, int64_t n, int64_t k,
+              int batch, cudaStream_t st) {
   MQ_REQUIRE(x && w && s && y, MQ_EINVAL, "mq_tgemv: null pointer");
   MQ_REQUIRE(n > 0 && k > 0 && n < (1LL << 31) && k <= (1 << 20), MQ_EINVAL, "mq_tgemv: bad shape n=%lld k=%lld",
              static_cast<long long>(n), static_cast<long long>(k));
   MQ_REQUIRE(k % 128 == 0, MQ_EINVAL, "mq_tgemv: k=%lld must be a multiple of 128", static_cast<long long>(k));
   MQ_REQUIRE(n % 4 == 0, MQ_EINVAL, "mq_tgemv: n=%lld must be a multiple of 4", static_cast<long long>(n));
   MQ_REQUIRE(batch >= 1 && batch <= 4, MQ_EINVAL, "mq_tgemv: batch must be in 1..4 (got %d)", batch);
-  MQ_REQUIRE(mq::aligned(w, 16) && mq::aligned(s, 8) && mq::aligned(x, 16) && mq::aligned(y, 4), MQ_EALIGN,
-             "mq_tgemv: w and x must be 16-byte aligned, s 8-byte aligned");
-  mq::DeviceInfo dev;
-  if (int rc = mq::device_info(&dev)) return rc;
-  mq::tg::Params p{};
+  MQ_REQUIRE(mq::aligned(w, 16) && mq::aligned(s, 8) && mq::aligned(x, 16) && mq::aligned(y, 4) && mq::aligned(cand, 4),
+             MQ_EALIGN, "mq_tgemv: w and x must be 16-byte aligned, s 8-byte aligned");
+  DeviceInfo dev;
+  if (int rc = device_info(&dev)) return rc;
+  Params p{};
   p.x = x;
   p.s = reinterpret_cast<const __half *>(s);
   p.y = y;
   p.n = static_cast<int>(n);
   p.k = static_cast<int>(k);
   p.batch = batch;
-  p.tiles = static_cast<int>((n + mq::tg::kCols - 1) / mq::tg::kCols);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  p.tiles = static_cast<int>((n + kCols - 1) / kCols);
+  p.cand = cand;
+  p.ncand = static_cast<int>((n + kCandOutputs - 1) / kCandOutputs);
   switch (batch) {
-    case 1: return mq::tg::launch<1>(w, p, st, dev);
-    case 2: return mq::tg::launch<2>(w, p, st, dev);
-    case 3: return mq::tg::launch<3>(w, p, st, dev);
-    default: return mq::tg::launch<4>(w, p, st, dev);
+    case 1: return launch<1>(w, p, st, dev);
+    case 2: return launch<2>(w, p, st, dev);
+    case 3: return launch<3>(w, p, st, dev);
+    default: return launch<4>(w, p, st, dev);
   }
+}
+
+// index[b] = the best candidate of token b (lowest index among equal values), -1 if any is flagged.
+__global__ void head_argmax_kernel(const float *__restrict__ cand, int ncand, int32_t *__restrict__ index) {
+  __shared__ float sv[32];
+  __shared__ int si[32], sb[32];
+  const float *c = cand + static_cast<size_t>(blockIdx.x) * ncand * 3;
+  float bv = -INFINITY;
+  int bi = INT_MAX, bad = 0;
+  for (int j = threadIdx.x; j < ncand; j += blockDim.x) {
+    const float v = c[3 * j];
+    const int i = static_cast<int>(c[3 * j + 1]);
+    bad |= c[3 * j + 2] != 0.f;
+    if (better(v, i, bv, bi)) bv = v, bi = i;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    if (better(ov, oi, bv, bi)) bv = ov, bi = oi;
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
+  if (lane == 0) sv[warp] = bv, si[warp] = bi, sb[warp] = bad;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < nw; ++w) {
+      bad |= sb[w];
+      if (better(sv[w], si[w], bv, bi)) bv = sv[w], bi = si[w];
+    }
+    index[blockIdx.x] = bad ? -1 : bi;
+  }
+}
+
+}  // namespace tg
+}  // namespace mq
+
+extern "C" int mq_tgemv(const uint16_t *x, const uint32_t *w, const uint16_t *s, float *y, int64_t n, int64_t k, int batch,
+                        void *stream) {
+  return mq::tg::tgemv_run(x, w, s, y, nullptr, n, k, batch, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mq_tgemv_head(const uint16_t *x, const uint32_t *w, const uint16_t *s, float *y, float *candidates,
+                             int64_t n, int64_t k, int batch, void *stream) {
+  MQ_REQUIRE(candidates, MQ_EINVAL, "mq_tgemv_head: null candidates");
+  return mq::tg::tgemv_run(x, w, s, y, candidates, n, k, batch, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mq_head_argmax(const float *candidates, int64_t ncand, int batch, int32_t *index, void *stream) {
+  MQ_REQUIRE(candidates && index, MQ_EINVAL, "mq_head_argmax: null pointer");
+  MQ_REQUIRE(ncand >= 1 && ncand < (1LL << 24) && batch >= 1 && batch <= 65535, MQ_EINVAL,
+             "mq_head_argmax: bad ncand=%lld or batch=%d", static_cast<long long>(ncand), batch);
+  MQ_REQUIRE(mq::aligned(candidates, 4) && mq::aligned(index, 4), MQ_EALIGN, "mq_head_argmax: misaligned pointer");
+  mq::tg::head_argmax_kernel<<<batch, 256, 0, static_cast<cudaStream_t>(stream)>>>(candidates, static_cast<int>(ncand),
+                                                                                  index);
+  return mq::check_launch("mq_head_argmax");
 }

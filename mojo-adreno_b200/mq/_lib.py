@@ -18,6 +18,10 @@ SIGNATURES = {
     "mq_gemm_q4": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_int, c_int, c_vp, c_size, c_vp]),
     "mq_gemm_q4_noalloc": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_int, c_int, c_vp]),
     "mq_tgemv": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_vp]),
+    "mq_tgemv_head": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_vp]),
+    "mq_head_argmax": (c_int, [c_vp, c_i64, c_int, c_vp, c_vp]),
+    "mq_gate_up_q4": (c_int, [c_vp, c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_int, c_int, c_vp]),
+    "mq_moe_gate_up_q4": (c_int, [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_int, c_vp]),
     "mq_gemm_t2": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_int, c_vp, c_size, c_vp]),
     "mq_moe_router": (c_int, [c_vp, c_vp, c_vp, c_i64, c_int, c_i64, c_vp]),
     "mq_moe_route": (c_int, [c_vp, c_vp, c_vp, c_i64, c_int, c_int, c_vp]),

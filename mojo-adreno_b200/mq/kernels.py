@@ -13,8 +13,8 @@ from ._lib import MQError, lib
 
 MQ_F32, MQ_F16 = 0, 1
 
-__all__ = ["MQ_F32", "MQ_F16", "MQError", "gemv_q4", "gemv_add_q4", "p_gemm_q4", "p_gemm_t2", "unpack_q4", "project",
-           "device_status"]
+__all__ = ["MQ_F32", "MQ_F16", "MQError", "gemv_q4", "gemv_add_q4", "gate_up_q4", "p_gemm_q4", "p_gemm_t2", "unpack_q4",
+           "project", "packed_head", "head_argmax", "device_status"]
 
 
 def _stream():
@@ -92,6 +92,22 @@ def gemv_add_q4(wq, ws, x, y, cols, group=64):
     return gemv_q4(wq, ws, x, y, cols, group, add=True)
 
 
+def gate_up_q4(wq, ws, x, a, cols, f, group=32):
+    """a[b, j] = silu(W[j] . x_b) * (W[f + j] . x_b): gate_up_q4(wq, ws, x, a, cols, f) of
+    lfm2/kernels/lk.mojo:154-167, the SwiGLU fused into the GEMV. wq: int32/uint32 [2f, cols/8] (gate
+    rows, then up rows); ws: fp16 [2f, cols/group]; x: fp32 or fp16 [batch <= 4, cols]; a: fp32 [batch, f]."""
+    _need(wq, "wq", _WORDS, 2 * f * cols // 8)
+    _need(ws, "ws", (torch.float16,), 2 * f * cols // group)
+    _need(x, "x", (torch.float32, torch.float16))
+    batch = x.numel() // cols
+    if batch * cols != x.numel():
+        raise MQError(-1, f"x: {x.numel()} elements is not a whole number of rows of {cols}")
+    _need(a, "a", (torch.float32,), batch * f)
+    lib.call("mq_gate_up_q4", _p(wq), _p(ws), _p(x), MQ_F16 if x.dtype == torch.float16 else MQ_F32, _p(a), f, cols,
+             group, batch, _stream())
+    return a
+
+
 def unpack_q4(wq, ws, cols, group, q=None, s=None):
     """The bit-exact decode hook: int8 q [rows, cols] = ((nib ^ 8) - 8) and the scales unchanged
     (the integer step of qwen3moe/reference.py:53-65)."""
@@ -120,6 +136,39 @@ def project(x, w, s, y, n, k):
     _need(y, "y", (torch.float32,), batch * n)
     lib.call("mq_tgemv", _p(x), _p(w), _p(s), _p(y), n, k, batch, _stream())
     return y
+
+
+CAND_BLOCK = 512  # logits per argmax candidate
+
+
+def packed_head(x, w, s, y, candidates, n, k, select=True):
+    """The ternary vocab head: packed_head(x, w, params, y, candidates, width, reduction, select) of
+    bonsai/kernels/kernels.mojo:451-517. y = W x as `project`; with select, candidates [batch, ceil(n/512), 3]
+    fp32 get (best logit, its index, non-finite flag) per 512 logits, the lowest index among equal values."""
+    if not select:
+        return project(x, w, s, y, n, k)
+    _need(x, "x", (torch.float16, torch.int32, torch.uint32))
+    batch = x.numel() * x.element_size() // 2 // k
+    _need(w, "w", _WORDS, k // 16 * n)
+    _need(s, "s", (torch.float16,), k // 128 * n)
+    _need(y, "y", (torch.float32,), batch * n)
+    _need(candidates, "candidates", (torch.float32,), batch * -(-n // CAND_BLOCK) * 3)
+    lib.call("mq_tgemv_head", _p(x), _p(w), _p(s), _p(y), _p(candidates), n, k, batch, _stream())
+    return y, candidates
+
+
+def head_argmax(candidates, index=None):
+    """The greedy token of each token's candidates [batch, ncand, 3] on the device (best_of,
+    lfm2/kernels/dsk.mojo:442-465; greedy() of bonsai/bonsai_vk.c:506-515): int32 [batch], -1 where a
+    candidate is flagged non-finite."""
+    _need(candidates, "candidates", (torch.float32,))
+    batch = candidates.shape[0] if candidates.dim() == 3 else 1
+    ncand = candidates.numel() // 3 // batch
+    if index is None:
+        index = torch.empty(batch, dtype=torch.int32, device=candidates.device)
+    _need(index, "index", (torch.int32,), batch)
+    lib.call("mq_head_argmax", _p(candidates), ncand, batch, _p(index), _stream())
+    return index
 
 
 def p_gemm_t2(x, w, s, y, n, k, rows=None, add=False):

@@ -96,14 +96,17 @@ def moe_gemv_q4(wq, ws, ids, x, y, k, group_rows, rows_per_group=None, group=32,
     return y
 
 
-def moe_gate_up(wq, ws, ids, x, a, d, fe, group=32, h=None):
+def moe_gate_up(wq, ws, ids, x, a, d, fe, group=32):
     """a[e, j] = silu(gate_e[j] . x) * (up_e[j] . x) for the selected experts ids[e]: moe_gate_up of
-    moek.mojo:200-210 (one token). x fp32 [d]; a fp32 [topk, fe]; h: optional fp32 [topk, 2fe] scratch."""
+    moek.mojo:200-210 (one token), one launch with the SwiGLU fused. x fp32 [d]; a fp32 [topk, fe]."""
+    _need(wq, "wq", _WORDS)
+    wrows = wq.numel() * 8 // d
+    _need(ws, "ws", (torch.float16,), wrows * d // group)
+    _need(ids, "ids", (torch.int32,))
+    _need(x, "x", (torch.float32,), d)
     topk = ids.numel()
-    h = torch.empty(topk, 2 * fe, dtype=torch.float32, device=x.device) if h is None else h
-    moe_gemv_q4(wq, ws, ids, x, h, d, 2 * fe, group=group)
     _need(a, "a", (torch.float32,), topk * fe)
-    lib.call("mq_moe_silu_mul", _p(h), _p(a), topk, fe, _stream())
+    lib.call("mq_moe_gate_up_q4", _p(wq), _p(ws), wrows, _p(x), _p(a), _p(ids), topk, fe, d, group, _stream())
     return a
 
 

@@ -32,6 +32,14 @@ def gemv(wq, ws, x, group):
     return x @ w.T
 
 
+def gate_up(wq, ws, x, f, group):
+    """a[b, j] = silu(W[j] . x_b) * (W[f + j] . x_b) in float64 for the fused [2f, k] gate|up matrix:
+    gate_up_q4 of lfm2/kernels/lk.mojo:154-167 (silu(g) = g / (1 + exp(-g)), lk.mojo:33-34)."""
+    h = gemv(wq, ws, x, group)
+    g, u = h[:, :f], h[:, f:2 * f]
+    return g / (1.0 + np.exp(-g)) * u
+
+
 def gemv_reference_order(wq, ws, x, group):
     """fp32, in gemv_q4's own order: per word part = sum_j q_j x_j (fp32), acc += part * scale,
     then a sum over the 64 lanes' accumulators (llama/kernels/gemv_q4.mojo:18-30). Small sizes only."""

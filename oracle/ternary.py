@@ -25,6 +25,45 @@ def tgemv(x16, w, s, n, k):
     return x @ wd.T
 
 
+CAND_BLOCK = 512  # logits of a candidate: 64 lanes x 8 (bonsai/kernels/kernels.mojo:491-517)
+
+
+def head_candidates(y):
+    """packed_head's argmax candidates for logits y [batch, n] (bonsai/kernels/kernels.mojo:490-517):
+    per block of 512 consecutive logits (value, index, non-finite flag) as float32 [batch, ceil(n/512), 3],
+    the lowest index among equal values. Only logits i < n compete (the reference's lanes past n
+    compete with 0 at an index >= n). The value and index of a flagged block are unspecified."""
+    y = np.atleast_2d(np.asarray(y, np.float32))
+    b, n = y.shape
+    nc = -(-n // CAND_BLOCK)
+    out = np.zeros((b, nc, 3), np.float32)
+    for t in range(b):
+        for c in range(nc):
+            blk = y[t, c * CAND_BLOCK:(c + 1) * CAND_BLOCK]
+            bad = not np.isfinite(blk).all()
+            i = int(np.argmax(np.where(np.isnan(blk), -np.inf, blk)))  # first maximum = lowest index
+            out[t, c] = (blk[i], c * CAND_BLOCK + i, 1.0 if bad else 0.0)
+    return out
+
+
+def greedy(cand):
+    """The greedy token of each row of candidates [batch, ncand, 3]: greedy() of bonsai/bonsai_vk.c:506-515
+    (lowest index among equal values) and best_of of lfm2/kernels/dsk.mojo:442-465; -1 where a flag is
+    set (greedy() stops there with "nonfinite logits")."""
+    cand = np.asarray(cand, np.float32).reshape(-1, np.asarray(cand).shape[-2], 3)
+    res = []
+    for c in cand:
+        if (c[:, 2] != 0).any():
+            res.append(-1)
+            continue
+        best = 0
+        for i in range(1, len(c)):
+            if c[i, 0] > c[best, 0] or (c[i, 0] == c[best, 0] and c[i, 1] < c[best, 1]):
+                best = i
+        res.append(int(c[best, 1]))
+    return np.array(res, np.int32)
+
+
 def tgemv_fp16_chains(x16, w, s, n, k):
     """The reference's own arithmetic (batch 1): per 128-group, _group_dot's four fp16 FMA chains
     per activation half (pair % 4), each step rounded to fp16, joined in fp32 as

@@ -67,6 +67,21 @@ def test_tgemv_rejects_bad_arguments_before_launch():
     assert rc == -1 and "batch" in msg
 
 
+def test_fused_epilogues_reject_bad_arguments_before_launch():
+    P = ctypes.c_void_p
+    ok = P(1 << 20)
+    rc, msg = _status("mq_gate_up_q4", ok, ok, ok, 0, ok, 40, 256, 32, 1, None)
+    assert rc == -1 and "multiple of 16" in msg
+    rc, msg = _status("mq_gate_up_q4", ok, ok, ok, 0, ok, 48, 256, 32, 5, None)
+    assert rc == -1 and "batch" in msg
+    rc, msg = _status("mq_moe_gate_up_q4", ok, ok, 96, ok, ok, ok, 2, 40, 256, 32, None)
+    assert rc == -1 and "fe" in msg
+    rc, msg = _status("mq_tgemv_head", ok, ok, ok, ok, None, 64, 256, 1, None)
+    assert rc == -1 and "candidates" in msg
+    rc, msg = _status("mq_head_argmax", ok, 0, 1, ok, None)
+    assert rc == -1 and "ncand" in msg
+
+
 def test_packers_and_ep_plan_reject_bad_arguments_before_launch():
     P = ctypes.c_void_p
     ok = P(1 << 20)

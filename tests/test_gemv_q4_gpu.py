@@ -119,3 +119,42 @@ def test_unpack_bit_exact(cuda):
     torch.cuda.synchronize()
     np.testing.assert_array_equal(q.cpu().numpy(), q4.unpack(wq))
     np.testing.assert_array_equal(s.cpu().numpy().view(np.uint16), ws.view(np.uint16))
+
+
+def _silu_mul_device(cuda, h, f):
+    """silu(h[:, :f]) * h[:, f:] with the library's own SwiGLU kernel (mq_moe_silu_mul)."""
+    th = torch.from_numpy(np.ascontiguousarray(h, np.float32)).to(cuda)
+    ta = torch.empty(h.shape[0], f, device=cuda)
+    mq.lib.call("mq_moe_silu_mul", th.data_ptr(), ta.data_ptr(), h.shape[0], f, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return ta.cpu().numpy()
+
+
+@pytest.mark.parametrize("group", [32, 64, 128])
+@pytest.mark.parametrize("f,k", [(8192, 2048), (1024, 4096), (48, 256)])
+@pytest.mark.parametrize("batch,dtype", [(1, np.float32), (2, np.float16), (4, np.float32)])
+def test_gate_up_fused(cuda, group, f, k, batch, dtype):
+    """gate_up_q4 (lfm2/kernels/lk.mojo:154-167): within the bar of the fp64 oracle, and bit-identical
+    to the unfused pair (mq_gemv_q4 over the 2f rows, then the SwiGLU kernel): the same products."""
+    rng = np.random.default_rng(f + k + group + batch)
+    wq, ws = synth.q4_matrix(rng, 2 * f, k, group)
+    x = rng.standard_normal((batch, k)).astype(dtype)
+    ta = torch.full((batch, f), float("nan"), device=cuda)
+    mq.gate_up_q4(torch.from_numpy(wq.view(np.int32)).to(cuda), torch.from_numpy(ws).to(cuda), torch.from_numpy(x).to(cuda),
+                  ta, k, f, group=group)
+    torch.cuda.synchronize()
+    a = ta.cpu().numpy()
+    ref = q4.gate_up(wq, ws, x.astype(np.float32), f, group)
+    assert np.isfinite(a).all()
+    assert normwise(a, ref) <= TIGHT_F32
+    h = run_gemv(cuda, wq, ws, x, group)
+    np.testing.assert_array_equal(a, _silu_mul_device(cuda, h, f))
+
+
+def test_gate_up_rejects_bad_shapes(cuda):
+    rng = np.random.default_rng(3)
+    wq, ws = synth.q4_matrix(rng, 2 * 40, 256, 32)
+    x = torch.zeros(1, 256, device=cuda)
+    with pytest.raises(mq.MQError, match="multiple of 16"):
+        mq.gate_up_q4(torch.from_numpy(wq.view(np.int32)).to(cuda), torch.from_numpy(ws).to(cuda), x,
+                      torch.empty(1, 40, device=cuda), 256, 40)

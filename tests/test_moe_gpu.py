@@ -121,6 +121,24 @@ def test_moe_gate_up_down_decode(cuda):
     assert normwise(res.cpu().numpy(), ref) <= TOL
 
 
+def test_moe_gate_up_fused_is_the_unfused_pair(cuda):
+    """The fused moe_gate_up (one launch) is bit-identical to the expert GEMV over the 2fe gate|up rows
+    followed by the SwiGLU kernel: the same products in the same order."""
+    m = synth.moe_layer(seed=5, tokens=1)
+    ids, _ = omoe.route(m["logits"], 8)
+    x = t(m["x"][0], cuda)
+    gu_wq, gu_ws, tid = t(m["gu_wq"], cuda), t(m["gu_ws"], cuda), t(ids[0], cuda)
+    a = torch.full((8, 768), float("nan"), device=cuda)
+    mq.moe_gate_up(gu_wq, gu_ws, tid, x, a, 2048, 768)
+    h = torch.empty(8, 2 * 768, device=cuda)
+    mq.moe_gemv_q4(gu_wq, gu_ws, tid, x, h, 2048, 2 * 768)
+    a2 = torch.empty(8, 768, device=cuda)
+    mq.lib.call("mq_moe_silu_mul", h.data_ptr(), a2.data_ptr(), 8, 768, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert mq.device_status() == 0
+    np.testing.assert_array_equal(a.cpu().numpy(), a2.cpu().numpy())
+
+
 @pytest.mark.parametrize("tokens,experts,d", [(404, 128, 2048), (1, 128, 2048), (7, 60, 768), (33, 128, 4100)])
 def test_router_logits_and_routing(cuda, tokens, experts, d):
     """The fp32 router GEMV against float64, then routing on its logits bit-exact against the oracle."""

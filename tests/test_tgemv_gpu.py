@@ -72,3 +72,90 @@ def test_tgemv_all_codes(cuda):
     assert normwise(y, ref) <= TIGHT
     # code 1 is weight 0: the integer group sums cancel exactly
     assert np.abs(y[0, 8:16]).max() == 0.0
+
+
+def run_head(cuda, x, w, s, n, k):
+    b = x.shape[0]
+    ty = torch.full((b, n), float("nan"), device=cuda)
+    tc = torch.full((b, -(-n // 512), 3), float("nan"), device=cuda)
+    mq.packed_head(torch.from_numpy(x).to(cuda), torch.from_numpy(w.view(np.int32)).to(cuda), torch.from_numpy(s).to(cuda),
+                   ty, tc, n, k)
+    idx = mq.head_argmax(tc)
+    torch.cuda.synchronize()
+    return ty.cpu().numpy(), tc.cpu().numpy(), idx.cpu().numpy()
+
+
+def check_candidates(y, cand):
+    """The kernel's candidates equal the oracle's selection over the kernel's own logits, bit for bit
+    (value and index where the block is not flagged)."""
+    ref = ternary.head_candidates(y)
+    np.testing.assert_array_equal(cand[..., 2], ref[..., 2])
+    ok = ref[..., 2] == 0
+    np.testing.assert_array_equal(cand[..., 0][ok], ref[..., 0][ok])
+    np.testing.assert_array_equal(cand[..., 1][ok], ref[..., 1][ok])
+
+
+@pytest.mark.parametrize("n,k,batch", [(151936, 256, 1), (75968, 512, 2), (12288, 1024, 4), (1000, 128, 1), (4, 256, 3)])
+def test_packed_head_candidates(cuda, n, k, batch):
+    """packed_head with select (bonsai/kernels/kernels.mojo:451-517): logits as mq_tgemv, candidates per
+    512 logits, and the device greedy index (best_of, lfm2/kernels/dsk.mojo:442-465) against the oracle."""
+    rng = np.random.default_rng(n + k + batch)
+    x = rng.standard_normal((batch, k)).astype(np.float16)
+    w, s = synth.ternary_matrix(rng, n, k)
+    y, cand, idx = run_head(cuda, x, w, s, n, k)
+    ref = ternary.tgemv(x, w, s, n, k)
+    assert normwise(y, ref) <= TIGHT
+    check_candidates(y, cand)
+    np.testing.assert_array_equal(idx, ternary.greedy(cand))
+    np.testing.assert_array_equal(idx, y.argmax(axis=1))  # numpy's argmax also takes the first maximum
+    for b in range(batch):  # the exact argmax too, where the top two are apart by more than the error
+        top2 = np.sort(ref[b])[-2:]
+        if top2[1] - top2[0] > 4 * TIGHT * np.abs(ref[b]).max():
+            assert idx[b] == ref[b].argmax()
+    if n >= 151936:  # large heads run the same K-unsplit kernel as mq_tgemv: identical logits
+        np.testing.assert_array_equal(y, run(cuda, x, w, s, n, k))
+
+
+def test_packed_head_ties_take_the_lowest_index(cuda):
+    """Equal logits (identical columns give bit-identical sums): within a block and across blocks the
+    lowest index wins, as greedy() and the subgroup reduction of packed_head order them."""
+    rng = np.random.default_rng(21)
+    n, k = 4096, 256
+    x = rng.standard_normal((1, k)).astype(np.float16)
+    w, s = synth.ternary_matrix(rng, n, k)
+    y0 = ternary.tgemv(x, w, s, n, k)[0]
+    top = int(y0.argmax())
+    for dst in (5, 700, 3000, 4095):  # copies of the best column, in and out of its block
+        w[:, dst] = w[:, top]
+        s[:, dst] = s[:, top]
+    y, cand, idx = run_head(cuda, x, w, s, n, k)
+    check_candidates(y, cand)
+    assert idx[0] == min(5, top)
+    assert cand[0, 0, 1] == min(5, top) or top >= 512
+
+
+def test_packed_head_flags_non_finite(cuda):
+    """A non-finite logit flags its block, and the greedy index is -1 (greedy() stops there)."""
+    rng = np.random.default_rng(22)
+    n, k = 2048, 256
+    x = rng.standard_normal((1, k)).astype(np.float16)
+    w, s = synth.ternary_matrix(rng, n, k)
+    s[0, 1300] = np.float16(np.inf)
+    y, cand, idx = run_head(cuda, x, w, s, n, k)
+    assert not np.isfinite(y[0, 1300])
+    np.testing.assert_array_equal(cand[0, :, 2], [0, 0, 1, 0])
+    check_candidates(y, cand)
+    assert idx[0] == -1
+
+
+def test_packed_head_all_negative_tail_stays_in_range(cuda):
+    """A last block that is partly past n and whose logits are all negative still names a real index."""
+    rng = np.random.default_rng(23)
+    n, k = 1000, 128
+    x = np.abs(rng.standard_normal((1, k))).astype(np.float16)
+    w = np.zeros((k // 16, n), np.uint32)  # every code 0: logit = -scale * sum x < 0
+    s = np.abs(rng.standard_normal((k // 128, n))).astype(np.float16) + np.float16(0.1)
+    y, cand, idx = run_head(cuda, x, w, s, n, k)
+    assert (y < 0).all()
+    check_candidates(y, cand)
+    assert 512 <= cand[0, 1, 1] < n and 0 <= idx[0] < n
