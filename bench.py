@@ -226,11 +226,18 @@ def run_mq(args):
                                               head["k"], group=GROUP) for i in range(reps_in_graph)])
     head_ms = time_graphs([head_graph], max(5, args.steps // 100), stream) / reps_in_graph
     head_ms = max_over_ranks(head_ms, world)
+    def cold(m):
+        """Enough copies of one matrix that a graph cycling through them never finds its weights in L2."""
+        mc = rotating_copies(m["wq"].numel() * 4 + m["ws"].numel() * 2)
+        return [m["wq"]] + [m["wq"].clone() for _ in range(mc - 1)], [m["ws"]] + [m["ws"].clone() for _ in range(mc - 1)]
+
     per_matrix = {}
     for m in mats:
-        gm = graph_of(lambda m=m: [mq.gemv_q4(m["wqs"][i % copies], m["wss"][i % copies], m["x"], m["y"], m["k"],
-                                              group=GROUP) for i in range(reps_in_graph)])
-        per_matrix[m["name"]] = round(time_graphs([gm], 10, stream) / reps_in_graph, 5)
+        cw, cs = cold(m)
+        gm = graph_of(lambda m=m, cw=cw, cs=cs: [mq.gemv_q4(w_, s_, m["x"], m["y"], m["k"], group=GROUP)
+                                                 for w_, s_ in zip(cw, cs)])
+        per_matrix[m["name"]] = round(time_graphs([gm], 10, stream) / len(cw), 5)
+        del gm, cw, cs
 
     # ---- end to end through the public API: x from pinned host, logits back, every step ------
     xs_host = [m["x"].cpu().pin_memory() for m in mats]
@@ -271,6 +278,45 @@ def run_mq(args):
         tbytes = n * k // 4 + n * (k // 128) * 2 + 2 * k + 4 * n
         tern[name] = {"shape": [n, k], "ms": round(tms, 5), "GB/s": round(tbytes / (tms * 1e-3) / 1e9, 1)}
         del tws, tss
+
+    # ---- secondary: the fused decode epilogues (one launch each) against their unfused forms -------
+    fused = {}
+    if world == 1:
+        # gate|up with the SwiGLU inside the GEMV (gate_up_q4) vs the GEMV over 2f rows + the SwiGLU kernel
+        gu = mats[2]
+        f = gu["n"] // 2
+        ga = torch.empty(1, f, device=dev)
+        sm = torch.cuda.current_stream().cuda_stream
+        cw, cs = cold(gu)
+        g_f = graph_of(lambda: [mq.gate_up_q4(w_, s_, gu["x"], ga, gu["k"], f, group=GROUP) for w_, s_ in zip(cw, cs)])
+        g_u = graph_of(lambda: [(mq.gemv_q4(w_, s_, gu["x"], gu["y"], gu["k"], group=GROUP),
+                                 mq.lib.call("mq_moe_silu_mul", gu["y"].data_ptr(), ga.data_ptr(), 1, f, sm))
+                                for w_, s_ in zip(cw, cs)])
+        f_ms = time_graphs([g_f], 10, stream) / len(cw)
+        u_ms = time_graphs([g_u], 10, stream) / len(cw)
+        del cw, cs
+        fused["gate_up_q4"] = {"shape": [2 * f, gu["k"]], "fused_ms": round(f_ms, 5), "unfused_ms": round(u_ms, 5),
+                               "GB/s": round(q4_bytes(2 * f, gu["k"], 1) / (f_ms * 1e-3) / 1e9, 1)}
+        del g_f, g_u
+        # the ternary head with packed_head's argmax candidates + the device greedy, vs the logits alone
+        hx, hw, hs = tsyn["head"]
+        hn, hk = hw.shape[1], hx.shape[1]
+        thx = torch.from_numpy(hx).to(dev)
+        thw = [torch.from_numpy(hw.view(np.int32)).to(dev)]
+        ths = [torch.from_numpy(hs).to(dev)]
+        thw.append(thw[0].clone())
+        ths.append(ths[0].clone())
+        thy = torch.empty(1, hn, device=dev)
+        thc = torch.empty(1, -(-hn // 512), 3, device=dev)
+        thi = torch.empty(1, dtype=torch.int32, device=dev)
+        g_h = graph_of(lambda: [(mq.packed_head(thx, thw[i % 2], ths[i % 2], thy, thc, hn, hk), mq.head_argmax(thc, thi))
+                                for i in range(reps_in_graph)])
+        g_p = graph_of(lambda: [mq.project(thx, thw[i % 2], ths[i % 2], thy, hn, hk) for i in range(reps_in_graph)])
+        h_ms = time_graphs([g_h], 10, stream) / reps_in_graph
+        p_ms = time_graphs([g_p], 10, stream) / reps_in_graph
+        fused["packed_head_argmax"] = {"shape": [hn, hk], "head_and_greedy_ms": round(h_ms, 5),
+                                       "logits_only_ms": round(p_ms, 5)}
+        del g_h, g_p, thw, ths
 
     # ---- secondary: int4 prefill GEMM, Llama-3.2-1B shapes, 431 tokens -----
     hbm, tflops_peak, peak_src = peaks()
@@ -362,6 +408,7 @@ def run_mq(args):
                          "peak_source": peak_src, "launch_ms": round(head_ms, 5)},
             "per_matrix_ms": per_matrix,
             "ternary_gemv": tern,
+            "fused_decode_epilogues": fused,
             "prefill_gemm": prefill,
             "ternary_prefill_gemm": tprefill,
             "decode_batch64": decode64,
@@ -548,7 +595,8 @@ def profile_case(name, launches):
     """A few launches of one kernel on one workload, for ncu captures (no timing, no JSON line).
     Cases: gemv_lm_head (configs[1] head, batch 1), tgemv_head (configs[4] head), gemm_gate_up
     (configs[2] 8192x2048, 431 tokens), gemm_decode64_head (configs[1] head, batch 64), moe_prefill
-    and moe_decode (configs[3], 404 tokens and 1 token)."""
+    and moe_decode (configs[3], 404 tokens and 1 token), gemm_t2_gate_up / gemm_t2_down (the ternary
+    prefill GEMM on the Qwen3-8B projections, 512 rows)."""
     import mq
     from mq import synth
 
@@ -579,6 +627,15 @@ def profile_case(name, launches):
         ty = torch.empty(x.shape[0], wq.shape[0], device=dev)
         for _ in range(launches):
             mq.p_gemm_q4(tw, ts, tx, ty, wq.shape[0], 2048, x.shape[0], group=GROUP)
+    elif name in ("gemm_t2_gate_up", "gemm_t2_down"):
+        n, k = {a: (b, c) for a, b, c in synth.QWEN3_TERNARY}[name[len("gemm_t2_"):]]
+        rng = np.random.default_rng(11)
+        w, s = synth.ternary_matrix(rng, n, k)
+        tx = torch.from_numpy(rng.standard_normal((512, k)).astype(np.float16)).to(dev)
+        tw, ts = torch.from_numpy(w.view(np.int32)).to(dev), torch.from_numpy(s).to(dev)
+        ty = torch.empty(512, n, device=dev)
+        for _ in range(launches):
+            mq.p_gemm_t2(tx, tw, ts, ty, n, k, 512)
     elif name in ("moe_prefill", "moe_decode"):
         tokens = 404 if name == "moe_prefill" else 1
         m = synth.moe_layer(seed=0, tokens=tokens)

@@ -80,6 +80,25 @@ int encode_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype
   return MQ_OK;
 }
 
+int encode_tmap_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem_bytes, uint64_t cols,
+                   uint64_t rows, uint64_t planes, uint64_t row_stride_bytes, uint64_t plane_stride_bytes,
+                   uint32_t box_cols, uint32_t box_rows, uint32_t box_planes, CUtensorMapSwizzle swizzle,
+                   const char *what) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MQ_ECUDA, "%s: cuTensorMapEncodeTiled is not available from the driver", what);
+  if (reinterpret_cast<uintptr_t>(base) % 16 || row_stride_bytes % 16 || plane_stride_bytes % 16 ||
+      (box_cols * elem_bytes) % 16)
+    return fail(MQ_EALIGN, "%s: tensor map needs a 16-byte aligned base, strides and box row", what);
+  const cuuint64_t dims[3] = {cols, rows, planes};
+  const cuuint64_t strides[2] = {row_stride_bytes, plane_stride_bytes};
+  const cuuint32_t box[3] = {box_cols, box_rows, box_planes};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MQ_ECUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+  return MQ_OK;
+}
+
 }  // namespace mq
 
 extern "C" {

@@ -72,6 +72,12 @@ int gemm_q4_run(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dty
 int encode_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem_bytes, uint64_t cols,
                    uint64_t rows, uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows,
                    CUtensorMapSwizzle swizzle, const char *what);
+// A 3-D map: `planes` copies of a [rows][cols] matrix, plane_stride_bytes apart (two row blocks of
+// one matrix, fetched by one box).
+int encode_tmap_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem_bytes, uint64_t cols,
+                   uint64_t rows, uint64_t planes, uint64_t row_stride_bytes, uint64_t plane_stride_bytes,
+                   uint32_t box_cols, uint32_t box_rows, uint32_t box_planes, CUtensorMapSwizzle swizzle,
+                   const char *what);
 
 #define MQ_REQUIRE(cond, code, ...)           \
   do {                                        \
@@ -177,6 +183,13 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 // 2-D tiled TMA store (or, with add, an fp32 reduce-add) of the box at (x, y) from shared memory,
 // in the calling thread's bulk group; x times the element size must be a multiple of 16 bytes and
 // both coordinates non-negative. Elements outside the tensor are not written.
@@ -206,6 +219,12 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) 
 __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int x, int y) {
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
                "r"(x), "r"(y)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap *map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z)
                : "memory");
 }
 

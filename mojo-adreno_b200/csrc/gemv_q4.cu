@@ -65,7 +65,8 @@ struct Params {
   int wrows;  // rows of the weight matrix (== n without expert indirection)
   // Gate|up with the SwiGLU fused (gu != 0): a tile is 16 outputs j; slot rows 0..15 hold the gate
   // rows of those outputs, rows 16..31 the up rows, gu_off rows further down the matrix, and the
-  // output is silu(gate . x) * (up . x).
+  // output is silu(gate . x) * (up . x). The maps are then 3-D (words, rows, gate/up plane gu_off
+  // rows apart), so one box still fetches a whole slot.
   int gu, gu_off;
 };
 
@@ -162,11 +163,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *dst = ring + slot * p.slot_bytes;
     const int wrow = weight_row0(p, tile);
     mbar_expect_tx(bar, bytes);
-    tma_load_2d(dst, &wmap, bar, sk * (kSlotK / 8), wrow);
-    if (p.scales_tma) tma_load_2d(dst + kWordBytes, &smap, bar, sk * kScaleHalvesTma, wrow);
-    if (p.gu) {  // 16-row boxes: the up rows into slot rows 16..31
-      tma_load_2d(dst + kWordBytes / 2, &wmap, bar, sk * (kSlotK / 8), wrow + p.gu_off);
-      if (p.scales_tma) tma_load_2d(dst + kWordBytes + 16 * 16, &smap, bar, sk * kScaleHalvesTma, wrow + p.gu_off);
+    if (p.gu) {  // [2 planes][16 rows]: the gate rows into slot rows 0..15, the up rows into 16..31
+      tma_load_3d(dst, &wmap, bar, sk * (kSlotK / 8), wrow, 0);
+      if (p.scales_tma) tma_load_3d(dst + kWordBytes, &smap, bar, sk * kScaleHalvesTma, wrow, 0);
+    } else {
+      tma_load_2d(dst, &wmap, bar, sk * (kSlotK / 8), wrow);
+      if (p.scales_tma) tma_load_2d(dst + kWordBytes, &smap, bar, sk * kScaleHalvesTma, wrow);
     }
   };
   griddep_launch_dependents();
@@ -182,8 +184,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (!p.ids && lane < kPrefetchItems) {
     int tile, sk;
     if (items.get(lane, tile, sk)) {
-      for (int b = 0; b <= p.gu; ++b) {
-        const int wrow = weight_row0(p, tile) + b * p.gu_off;
+      const int wrow = weight_row0(p, tile);
+      if (p.gu) {
+        tma_prefetch_l2_3d(&wmap, sk * (kSlotK / 8), wrow, 0);
+        if (p.scales_tma) tma_prefetch_l2_3d(&smap, sk * kScaleHalvesTma, wrow, 0);
+      } else {
         tma_prefetch_l2_2d(&wmap, sk * (kSlotK / 8), wrow);
         if (p.scales_tma) tma_prefetch_l2_2d(&smap, sk * kScaleHalvesTma, wrow);
       }
@@ -433,18 +438,27 @@ int launch(const uint32_t *wq, Params p, cudaStream_t stream, const DeviceInfo &
   MQ_REQUIRE(p.slots >= 1 && smem <= dev.smem_optin, MQ_EUNSUPPORTED,
              "mq_gemv_q4: k=%d batch=%d needs %zu B of shared memory (max %zu)", p.k, p.batch, smem, dev.smem_optin);
   CUtensorMap wmap, smap;
-  const int box = p.gu ? kRows / 2 : kRows;  // gate|up: two 16-row boxes per slot
-  if (int rc = encode_tmap_2d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.k / 8, p.wrows, static_cast<uint64_t>(p.k) / 2,
-                              32, box, CU_TENSOR_MAP_SWIZZLE_128B, "mq_gemv_q4 weights"))
-    return rc;
-  if (p.scales_tma) {
-    if (int rc = encode_tmap_2d(&smap, p.ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k / G, p.wrows,
-                                static_cast<uint64_t>(p.k / G) * 2, kScaleHalvesTma, box, CU_TENSOR_MAP_SWIZZLE_NONE,
-                                "mq_gemv_q4 scales"))
+  const uint64_t wrow_bytes = static_cast<uint64_t>(p.k) / 2, srow_bytes = static_cast<uint64_t>(p.k / G) * 2;
+  if (p.gu) {  // planes: gate rows r and up rows r + gu_off, for r < wrows - gu_off
+    const uint64_t rows = static_cast<uint64_t>(p.wrows - p.gu_off);
+    if (int rc = encode_tmap_3d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.k / 8, rows, 2, wrow_bytes,
+                                wrow_bytes * p.gu_off, 32, kRows / 2, 2, CU_TENSOR_MAP_SWIZZLE_128B, "mq_gate_up_q4 weights"))
       return rc;
+    if (p.scales_tma)
+      if (int rc = encode_tmap_3d(&smap, p.ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k / G, rows, 2, srow_bytes,
+                                  srow_bytes * p.gu_off, kScaleHalvesTma, kRows / 2, 2, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                  "mq_gate_up_q4 scales"))
+        return rc;
   } else {
-    smap = wmap;  // not read
+    if (int rc = encode_tmap_2d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.k / 8, p.wrows, wrow_bytes, 32, kRows,
+                                CU_TENSOR_MAP_SWIZZLE_128B, "mq_gemv_q4 weights"))
+      return rc;
+    if (p.scales_tma)
+      if (int rc = encode_tmap_2d(&smap, p.ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k / G, p.wrows, srow_bytes,
+                                  kScaleHalvesTma, kRows, CU_TENSOR_MAP_SWIZZLE_NONE, "mq_gemv_q4 scales"))
+        return rc;
   }
+  if (!p.scales_tma) smap = wmap;  // not read
   // Split K across warps (ks divides kWarps) until the rounds cover every SM or K runs out of slots.
   const int nslotk = (p.k + kSlotK - 1) / kSlotK;
   p.ks = 1;
