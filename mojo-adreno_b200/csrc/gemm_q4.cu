@@ -37,10 +37,10 @@ namespace gemm {
 
 constexpr int kBM = 128;  // weight rows per CTA tile (the UMMA M)
 constexpr int kBK = 64;   // k per pipeline stage: one 128-byte fp16 row
-constexpr int kMaxStages = 6;
+constexpr int kMaxStages = 8;  // W/X ring slots in shared memory
+constexpr int kACols = kBK / 2;  // TMEM columns of one dequantised A stage: 64 fp16 per row, as pairs
 constexpr int kDeqWarps = 8;   // two per scheduler: one dequant warp alone cannot hide its latencies
 constexpr int kThreads = 32 * (2 + kDeqWarps);  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 dequant + epilogue
-constexpr int kATileBytes = kBM * 128;
 constexpr int kWTileBytes = kBM * 32;
 
 // MODE 0: dense Y = X W^T. MODE 1 (MoE gate|up): per expert e, rows e * 2fe + [0, fe) are gate and
@@ -64,26 +64,30 @@ struct Params {
   int n_out;              // MODE 1, 2: output columns per token (fe or d)
   int n, k, m;
   int bn;        // tokens per tile (multiple of 16, <= 256)
-  int stages;    // pipeline depth (<= kMaxStages)
+  int stages;    // pipeline depth: W/X ring slots (<= kMaxStages)
+  int astages;   // dequantised A ring slots in TMEM (<= stages)
   int add;       // y += instead of y =
   int splitk;    // CTAs along K (red.add into y)
   int kb_split;  // 64-k blocks per split (a multiple of 4)
   int tiles_n, tiles_m;
-  uint32_t tmem_cols;
+  uint32_t tmem_cols;  // TMEM allocation: the fp32 accumulator, then the A ring
+  uint32_t tmem_a;     // first TMEM column of the A ring
   int y_tma;  // MODE 0, 3: write y with TMA stores from a shared-memory tile (y 16-byte aligned, n % 4 == 0)
 };
 
+// Shared memory: the W/X ring (X tiles, then W tiles) and the barriers. The dequantised A tiles
+// live in tensor memory, next to the accumulator, so they cost no shared-memory bandwidth: written
+// with tcgen05.st, read by tcgen05.mma's A-from-TMEM form.
 struct Layout {
-  uint32_t a, x, w, bars, tmem_slot, total;
+  uint32_t x, w, bars, tmem_slot, total;
 };
 
 __host__ __device__ inline Layout layout(int bn, int stages) {
   Layout L;
-  L.a = 0;
-  L.x = L.a + stages * kATileBytes;
+  L.x = 0;
   L.w = L.x + stages * bn * 128;
   L.bars = L.w + stages * kWTileBytes;
-  L.tmem_slot = L.bars + (3 * kMaxStages + 1) * 8;
+  L.tmem_slot = L.bars + (4 * kMaxStages + 1) * 8;
   L.total = L.tmem_slot + 16;
   return L;
 }
@@ -134,14 +138,18 @@ __global__ void __launch_bounds__(kThreads, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const Layout L = layout(p.bn, p.stages);
+  // full / empty: W and X of a W/X ring slot landed / consumed by the MMA; deq / aempty: an A ring
+  // slot (TMEM) written by the dequant warps / consumed by the MMA.
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);
   uint64_t *deq = full + kMaxStages;
   uint64_t *empty = deq + kMaxStages;
-  uint64_t *accum = empty + kMaxStages;
+  uint64_t *aempty = empty + kMaxStages;
+  uint64_t *accum = aempty + kMaxStages;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.tmem_slot);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.tmem_slot + 8);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int S = p.stages;
+  const int S = p.stages, SA = p.astages;
+  const bool split_rings = SA < S;  // otherwise full[s] already implies that A slot s % SA is free
 
   // Tile: token tiles fastest, so consecutive CTAs share (and L2-reuse) a weight tile.
   const int t = blockIdx.x;
@@ -170,6 +178,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(full + i, 1);
       mbar_init(deq + i, 32 * kDeqWarps);
       mbar_init(empty + i, 1);
+      mbar_init(aempty + i, 1);
     }
     mbar_init(accum, 1);
     *abort_flag = 0;
@@ -242,36 +251,43 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---------------- MMA issuer -------------------------------------------------------------
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16(kBM, p.bn);
-      // Descriptors of slot 0; a slot further is + its byte size / 16 in the address field (the
+      // X descriptor of slot 0; a slot further is + its byte size / 16 in the address field (the
       // field holds any shared-memory address of this CTA without carrying into bit 14).
-      const uint64_t da0 = umma_desc_sw128(smem_u32(smem + L.a)), db0 = umma_desc_sw128(smem_u32(smem + L.x));
-      const uint32_t a_step = kATileBytes >> 4, x_step = (p.bn * 128) >> 4;
-      uint64_t da = da0, db = db0;
+      const uint64_t db0 = umma_desc_sw128(smem_u32(smem + L.x));
+      const uint32_t da0 = tmem_d + p.tmem_a;  // A slot 0 in TMEM; a slot further is kACols columns on
+      const uint32_t x_step = (p.bn * 128) >> 4;
+      uint32_t da = da0;
+      uint64_t db = db0;
       uint32_t ph = 0;
-      int s = 0;
+      int s = 0, as = 0;
       for (int i = 0; i < nk; ++i) {
-        // deq[s] completes only after every dequant thread saw full[s] (W and X landed) and
+        // deq[as] completes only after every dequant thread saw full[s] (W and X landed) and
         // released its A writes: one acquire covers both.
-        if (!mbar_wait(&deq[s], ph)) {
+        if (!mbar_wait(&deq[as], ph)) {
           raise_status(kStatusGemmMmaWait);
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
-        // +32 bytes along K = +2 in the descriptor's address field
-        umma_f16(tmem_d, da, db, idesc, i != 0);
-        umma_f16(tmem_d, da + 2, db + 2, idesc, 1);
-        umma_f16(tmem_d, da + 4, db + 4, idesc, 1);
-        umma_f16(tmem_d, da + 6, db + 6, idesc, 1);
+        // K + 16: 8 TMEM columns of A; +32 bytes = +2 in the X descriptor's address field
+        umma_f16_ts(tmem_d, da, db, idesc, i != 0);
+        umma_f16_ts(tmem_d, da + 8, db + 2, idesc, 1);
+        umma_f16_ts(tmem_d, da + 16, db + 4, idesc, 1);
+        umma_f16_ts(tmem_d, da + 24, db + 6, idesc, 1);
         umma_commit(&empty[s]);
+        if (split_rings) umma_commit(&aempty[as]);
         if (++s == S) {
           s = 0;
-          ph ^= 1;
-          da = da0;
           db = db0;
         } else {
-          da += a_step;
           db += x_step;
+        }
+        if (++as == SA) {
+          as = 0;
+          ph ^= 1;
+          da = da0;
+        } else {
+          da += kACols;
         }
       }
       umma_commit(accum);  // also after an abort: it lands once the issued MMAs are done
@@ -310,22 +326,28 @@ __global__ void __launch_bounds__(kThreads, 2)
     };
     uint32_t cur[4], nxt[4];
     load_scales(0, cur);
-    int ds = 0;        // ring slot of the next stage
+    int ds = 0;        // W/X ring slot of the next stage
     uint32_t dph = 0;  // its phase parity
-    const uint32_t xr = row & 7;
-    uint8_t *a_row = smem + L.a + row * 128;
+    int das = 0, dar = 0;  // A ring slot of the next stage and its round
+    // This thread's 16 TMEM columns of A slot 0 (lane = its row; half h holds K 32h .. 32h + 31).
+    const uint32_t a_t0 = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + p.tmem_a + 16 * half;
     for (int q4 = 0; q4 * 4 < nk; ++q4) {
       load_scales(q4 + 1, nxt);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int i = 4 * q4 + u;
         if (i >= nk) break;
-        const int s = ds;
+        const int s = ds, as = das;
         if (!*abort_flag && !mbar_wait(&full[s], dph)) {
           raise_status(kStatusGemmDeqWait);
           *abort_flag = 1;
         }
-        if (!*abort_flag) {
+        if (split_rings && dar > 0 && !*abort_flag && !mbar_wait(&aempty[as], (dar - 1) & 1)) {
+          raise_status(kStatusGemmDeqWait);
+          *abort_flag = 1;
+        }
+        // tcgen05.st is warp-collective: the warp stores only if every lane may.
+        if (__all_sync(0xffffffffu, !*abort_flag)) {
           // this thread's 32 k of the stage share one group for G >= 32: (s, s) as half2
           __half2 s2;
           if (G == 32) {
@@ -338,27 +360,33 @@ __global__ void __launch_bounds__(kThreads, 2)
             const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[0]);
             s2 = (u >> 1) ? __high2half2(pair) : __low2half2(pair);
           }
-          uint8_t *a = a_row + s * kATileBytes;
+          uint4 q[4];  // 32 fp16 in K order
           if (MODE == kTernary) {  // word rows 2 half, 2 half + 1 of this output: codes k = 32 half ..
             const uint8_t *wt = smem + L.w + s * kWTileBytes + row * 4;
             const uint32_t w0 = *reinterpret_cast<const uint32_t *>(wt + (2 * half) * kBM * 4);
             const uint32_t w1 = *reinterpret_cast<const uint32_t *>(wt + (2 * half + 1) * kBM * 4);
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-              *reinterpret_cast<uint4 *>(a + (((4 * half + c) ^ xr) << 4)) = dequant_t2(c < 2 ? w0 : w1, 16 * (c & 1), s2);
+            for (int c = 0; c < 4; ++c) q[c] = dequant_t2(c < 2 ? w0 : w1, 16 * (c & 1), s2);
           } else {
             const uint4 w = *reinterpret_cast<const uint4 *>(smem + L.w + s * kWTileBytes + row * 32 + half * 16);
             const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-              *reinterpret_cast<uint4 *>(a + (((4 * half + c) ^ xr) << 4)) = dequant_word(wv[c], s2);
+            for (int c = 0; c < 4; ++c) q[c] = dequant_word(wv[c], s2);
           }
-          fence_proxy_async_smem();
+          const uint32_t r[16] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w,
+                                  q[2].x, q[2].y, q[2].z, q[2].w, q[3].x, q[3].y, q[3].z, q[3].w};
+          tmem_st16(a_t0 + as * kACols, r);
+          tmem_wait_st();
         }
-        mbar_arrive(&deq[s]);
+        tc_fence_before();  // orders the TMEM stores before the arrive that the MMA thread acquires
+        mbar_arrive(&deq[as]);
         if (++ds == S) {
           ds = 0;
           dph ^= 1;
+        }
+        if (++das == SA) {
+          das = 0;
+          ++dar;
         }
       }
 #pragma unroll
@@ -379,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       // and every MMA finished), then one TMA store -- or an fp32 reduce-add with add or split K --
       // writes it; the tensor map clips tokens past m and rows past n. Far fewer instructions than a
       // warp store per 32 values, which left the write-out as a third of the kernel's time.
-      float *tile = reinterpret_cast<float *>(smem + L.a);  // [bn][kBM]
+      float *tile = reinterpret_cast<float *>(smem + L.x);  // [bn][kBM]
       if (live) {
         for (int c0 = 32 * half; c0 < p.bn; c0 += 64) {
           float v[32];
@@ -428,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       // threads holding the matching gate rows (lanes 0-63): a = silu(gate) * up, fp16. Row r's
       // column c sits at c ^ (r & 15) (bn is a multiple of 16), so the 32 rows a warp writes or reads
       // at one column fall in 16 different banks instead of one.
-      float *up = reinterpret_cast<float *>(smem + L.a);  // [64 rows][bn]
+      float *up = reinterpret_cast<float *>(smem + L.x);  // [64 rows][bn]
       if (live && row >= 64) {
         const int ur = row - 64;
         for (int c0 = 32 * half; c0 < p.bn; c0 += 64) {
@@ -472,6 +500,15 @@ __global__ void f32_to_f16_kernel(const float4 *__restrict__ x, uint2 *__restric
   }
 }
 
+// TMEM of one CTA (`budget` columns: 512, or 256 with two CTAs per SM): the accumulator's bn
+// columns (rounded to 32), then as many A stages as fit, at most one per W/X slot.
+inline void plan_tmem(Params &p, uint32_t budget) {
+  p.tmem_a = (static_cast<uint32_t>(p.bn) + 31) / 32 * 32;  // bn <= 128 when budget is 256
+  p.astages = std::min<int>(p.stages, (budget - p.tmem_a) / kACols);
+  p.tmem_cols = 32;
+  while (p.tmem_cols < p.tmem_a + p.astages * kACols) p.tmem_cols *= 2;
+}
+
 template <int G, int MODE = kDense>
 int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream, const DeviceInfo &dev) {
   // Tiles: tokens split as evenly as possible into tiles of a multiple of 16. Up to 128 tokens: one
@@ -481,8 +518,6 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
   p.tiles_m = two_per_sm ? 1 : (p.m + 255) / 256;
   p.bn = ((p.m + p.tiles_m - 1) / p.tiles_m + 15) / 16 * 16;
   p.tiles_n = (p.n + kBM - 1) / kBM;
-  p.tmem_cols = 32;
-  while (p.tmem_cols < static_cast<uint32_t>(p.bn)) p.tmem_cols *= 2;
   // Split K (in quads of 64-k blocks) while the grid leaves SMs idle.
   const int nkb = p.k / kBK, quads = nkb / 4;
   const int tiles = p.tiles_m * p.tiles_n;
@@ -498,6 +533,7 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
     L = layout(p.bn, p.stages);
     if (L.total + 1024 <= budget) break;
   }
+  plan_tmem(p, two_per_sm ? 256 : 512);
   const size_t smem = L.total + 1024;
   MQ_REQUIRE(smem <= dev.smem_optin, MQ_EUNSUPPORTED, "mq_gemm_q4: tile of %d tokens needs %zu B of shared memory", p.bn,
              smem);
@@ -528,7 +564,7 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
   // y through TMA stores when the tensor map can describe it (16-byte base and row stride) and the
   // [bn][128] fp32 staging tile fits where the rings were.
   CUtensorMap ymap = xmap;  // not read unless y_tma
-  p.y_tma = aligned(p.y, 16) && p.n % 4 == 0 && static_cast<size_t>(p.bn) * kBM * 4 <= layout(p.bn, p.stages).bars;
+  p.y_tma = aligned(p.y, 16) && p.n % 4 == 0 && static_cast<size_t>(p.bn) * kBM * 4 <= L.bars;
   if (p.y_tma) {
     if (int rc = encode_tmap_2d(&ymap, p.y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.n, p.m, static_cast<uint64_t>(p.n) * 4,
                                 kBM, p.bn, CU_TENSOR_MAP_SWIZZLE_NONE, "mq_gemm_q4 output"))
@@ -557,13 +593,15 @@ int launch_grouped(const uint32_t *wq, const __half *ws, const __half *xs, int64
   p.tiles_n = MODE == kGateUp ? (rows_per_expert / 2) / (kBM / 2) : rows_per_expert / kBM;
   p.splitk = 1;
   p.kb_split = p.k / kBK;
-  p.tmem_cols = 32;
-  while (p.tmem_cols < static_cast<uint32_t>(bn)) p.tmem_cols *= 2;
+  // Two CTAs per SM while both fit their accumulators and A rings in half of TMEM.
+  const bool two_per_sm = bn <= 128;
+  const size_t budget = two_per_sm ? dev.smem_optin / 2 - 1024 : dev.smem_optin;
   Layout L{};
   for (p.stages = kMaxStages; p.stages >= 2; --p.stages) {
     L = layout(p.bn, p.stages);
-    if (L.total + 1024 <= dev.smem_optin / 2 - 1024) break;
+    if (L.total + 1024 <= budget) break;
   }
+  plan_tmem(p, two_per_sm ? 256 : 512);
   const size_t smem = L.total + 1024;
   CUtensorMap wmap, xmap;
   if (int rc = encode_tmap_2d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.k / 8, p.n, static_cast<uint64_t>(p.k) / 2,

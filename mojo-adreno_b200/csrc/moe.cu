@@ -82,11 +82,15 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
                                                               int32_t *__restrict__ slot_of, int32_t *__restrict__ tiles,
                                                               int32_t *__restrict__ ntiles, int32_t *__restrict__ local) {
   extern __shared__ int32_t sh[];
-  int32_t *warp_cnt = sh;                        // [32 warps][experts]
-  int32_t *base = warp_cnt + 32 * experts;       // [experts] running start within the expert
-  int32_t *start = base + experts;               // [experts + 1] offsets
+  int32_t *warp_cnt = sh;                    // [32 warps][experts]: pairs of the warp's range, then their start
+  int32_t *start = warp_cnt + 32 * experts;  // [experts + 1]: bucket totals, then offsets
+  int32_t *tstart = start + experts + 1;     // [experts + 1]: first work tile of each bucket
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const unsigned lt_mask = (1u << lane) - 1u;
+  // Warp w owns the contiguous pairs [lo, hi): ranks within a bucket follow pair index because the
+  // warps' ranges are in pair order and each warp walks its own range in order.
+  const int per = (pairs + 31) / 32;
+  const int lo = min(pairs, warp * per), hi = min(pairs, lo + per);
   // Bucket of pair i, or -1 (reported, left out) for an id outside [0, experts * div).
   auto bucket = [&](int i) {
     const int id = ids[i];
@@ -96,74 +100,96 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
     }
     return id / div;
   };
+  auto tiles_of = [&](int c) { return tiles ? (c + tile - 1) / tile : 0; };
 
-  // Pass 1: histogram.
-  for (int e = threadIdx.x; e < experts; e += kGroupThreads) base[e] = 0;
+  // Pass 1: per-warp histograms.
+  for (int j = threadIdx.x; j < 32 * experts; j += kGroupThreads) warp_cnt[j] = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < pairs; i += kGroupThreads) {
+  for (int i = lo + lane; i < hi; i += 32) {
     const int b = bucket(i);
-    if (b >= 0) atomicAdd(&base[b], 1);
+    if (b >= 0) atomicAdd(&warp_cnt[warp * experts + b], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0, nt = 0;
-    for (int e = 0; e < experts; ++e) {
-      start[e] = run;
-      const int c = base[e];
-      counts[e] = c;
-      offsets[e] = run;
-      for (int r = 0; tiles && r < c; r += tile) {
-        tiles[3 * nt] = e;
-        tiles[3 * nt + 1] = run + r;
-        tiles[3 * nt + 2] = min(tile, c - r);
-        ++nt;
-      }
+  // Per bucket: each warp's start within the bucket (exclusive over warps) and the bucket total.
+  for (int e = threadIdx.x; e < experts; e += kGroupThreads) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = warp_cnt[w * experts + e];
+      warp_cnt[w * experts + e] = run;
       run += c;
     }
-    start[experts] = run;
-    offsets[experts] = run;
-    if (ntiles) *ntiles = nt;
+    start[e] = run;
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < experts; e += kGroupThreads) base[e] = start[e];
+  // Exclusive scans over buckets of the totals and of the work tiles (warp 0, chunk of buckets per lane).
+  if (warp == 0) {
+    const int chunk = (experts + 31) / 32;
+    int csum = 0, ctiles = 0;
+    for (int j = 0; j < chunk; ++j) {
+      const int e = lane * chunk + j;
+      if (e < experts) csum += start[e], ctiles += tiles_of(start[e]);
+    }
+    int inc = csum, tinc = ctiles;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, inc, o), tv = __shfl_up_sync(0xffffffffu, tinc, o);
+      if (lane >= o) inc += v, tinc += tv;
+    }
+    int run = inc - csum, trun = tinc - ctiles;
+    for (int j = 0; j < chunk; ++j) {
+      const int e = lane * chunk + j;
+      if (e < experts) {
+        const int c = start[e];
+        counts[e] = c;
+        offsets[e] = run;
+        start[e] = run;
+        tstart[e] = trun;
+        run += c;
+        trun += tiles_of(c);
+      }
+    }
+    if (lane == 31) {
+      start[experts] = run;
+      offsets[experts] = run;
+      tstart[experts] = trun;
+      if (ntiles) *ntiles = trun;
+    }
+  }
+  __syncthreads();
+  // Work tiles (expert, first row, rows), bucket by bucket.
+  if (tiles) {
+    for (int e = threadIdx.x; e < experts; e += kGroupThreads) {
+      const int c = start[e + 1] - start[e];
+      for (int r = 0, t = tstart[e]; r < c; r += tile, ++t) {
+        tiles[3 * t] = e;
+        tiles[3 * t + 1] = start[e] + r;
+        tiles[3 * t + 2] = min(tile, c - r);
+      }
+    }
+  }
   // Positions past the pairs that were kept (only when ids were left out) point at pair 0, so every
   // entry of order stays a valid pair index.
   for (int pos = start[experts] + threadIdx.x; pos < pairs; pos += kGroupThreads) {
     order[pos] = 0;
     if (local) local[pos] = 0;
   }
-  __syncthreads();
 
-  // Pass 2: positions, chunk by chunk of kGroupThreads pairs (stable: ranks follow pair index).
-  for (int c0 = 0; c0 < pairs; c0 += kGroupThreads) {
-    const int i = c0 + threadIdx.x;
-    const int e = i < pairs ? bucket(i) : -1;
-    const bool live = e >= 0;
-    const unsigned same = __match_any_sync(0xffffffffu, e);
-    const int rank_in_warp = __popc(same & lt_mask);
-    for (int j = threadIdx.x; j < 32 * experts; j += kGroupThreads) warp_cnt[j] = 0;
-    __syncthreads();
-    if (live && rank_in_warp == 0) warp_cnt[warp * experts + e] = __popc(same);
-    __syncthreads();
-    // exclusive scan over warps per expert, added to the running base
-    for (int ex = threadIdx.x; ex < experts; ex += kGroupThreads) {
-      int run = base[ex];
-      for (int w = 0; w < 32; ++w) {
-        const int c = warp_cnt[w * experts + ex];
-        warp_cnt[w * experts + ex] = run;
-        run += c;
-      }
-      base[ex] = run;
-    }
-    __syncthreads();
-    if (i < pairs && !live) slot_of[i] = -1;  // left out
-    if (live) {
-      const int pos = warp_cnt[warp * experts + e] + rank_in_warp;
+  // Pass 2: each warp places its own pairs, 32 at a time, in pair order.
+  int32_t *my_cnt = warp_cnt + warp * experts;
+  for (int base = lo; base < hi; base += 32) {
+    const int i = base + lane;
+    const int b = i < hi ? bucket(i) : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, b);
+    const int rank = __popc(same & lt_mask);
+    const int pos = b >= 0 ? start[b] + my_cnt[b] + rank : 0;
+    __syncwarp();
+    if (b >= 0 && rank == 0) my_cnt[b] += __popc(same);
+    __syncwarp();
+    if (i < hi && b < 0) slot_of[i] = -1;  // left out
+    if (b >= 0) {
       order[pos] = i;
       slot_of[i] = pos;
-      if (local) local[pos] = ids[i] - e * div;
+      if (local) local[pos] = ids[i] - b * div;
     }
-    __syncthreads();
   }
 }
 
@@ -337,7 +363,7 @@ extern "C" int mq_moe_group(const int32_t *ids, int64_t tokens, int topk, int ex
   MQ_REQUIRE(tokens > 0 && topk >= 1 && tokens * topk < (1 << 30), MQ_EINVAL, "mq_moe_group: bad tokens / topk");
   MQ_REQUIRE(experts >= 1 && experts <= 256, MQ_EINVAL, "mq_moe_group: experts must be in 1..256");
   MQ_REQUIRE(tile >= 1, MQ_EINVAL, "mq_moe_group: tile must be >= 1");
-  const size_t smem = (32 * experts + 2 * experts + 1) * sizeof(int32_t);
+  const size_t smem = (32 * experts + 2 * (experts + 1)) * sizeof(int32_t);
   mq::moe::group_kernel<<<1, mq::moe::kGroupThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       ids, 1, static_cast<int>(tokens * topk), experts, tile, counts, offsets, order, slot_of, tiles, ntiles, nullptr);
   return mq::check_launch("mq_moe_group");
@@ -349,7 +375,7 @@ extern "C" int mq_ep_plan(const int32_t *ids, int64_t tokens, int topk, int expe
   MQ_REQUIRE(tokens > 0 && topk >= 1 && tokens * topk < (1 << 30), MQ_EINVAL, "mq_ep_plan: bad tokens / topk");
   MQ_REQUIRE(world >= 1 && world <= 256 && experts >= world && experts % world == 0, MQ_EINVAL,
              "mq_ep_plan: experts (%d) must be a positive multiple of world (%d)", experts, world);
-  const size_t smem = (32 * world + 2 * world + 1) * sizeof(int32_t);
+  const size_t smem = (32 * world + 2 * (world + 1)) * sizeof(int32_t);
   mq::moe::group_kernel<<<1, mq::moe::kGroupThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       ids, experts / world, static_cast<int>(tokens * topk), world, 1, counts, offsets, order, slot_of, nullptr, nullptr,
       local_ids);
