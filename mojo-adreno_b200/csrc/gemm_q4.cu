@@ -329,64 +329,106 @@ __global__ void __launch_bounds__(kThreads, 2)
     int ds = 0;        // W/X ring slot of the next stage
     uint32_t dph = 0;  // its phase parity
     int das = 0, dar = 0;  // A ring slot of the next stage and its round
+    constexpr bool kPairs = MODE == kDense || MODE == kTernary;
     // This thread's 16 TMEM columns of A slot 0 (lane = its row; half h holds K 32h .. 32h + 31).
     const uint32_t a_t0 = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + p.tmem_a + 16 * half;
     for (int q4 = 0; q4 * 4 < nk; ++q4) {
       load_scales(q4 + 1, nxt);
+      // One-matrix modes: two stages per pass, so both tiles' loads, conversions and TMEM stores
+      // overlap and one wait for the stores covers both (the grouped modes, whose stages wait on
+      // their copies instead, measured slower this way).
+      auto dq = [&](int u, int s, uint32_t (&r)[16]) {
+        __half2 s2;
+        if (G == 32) {
+          const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[u]);
+          s2 = half ? __high2half2(pair) : __low2half2(pair);
+        } else if (G == 64) {
+          const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[u >> 1]);
+          s2 = (u & 1) ? __high2half2(pair) : __low2half2(pair);
+        } else {
+          const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[0]);
+          s2 = (u >> 1) ? __high2half2(pair) : __low2half2(pair);
+        }
+        uint4 q[4];
+        if (MODE == kTernary) {
+          const uint8_t *wt = smem + L.w + s * kWTileBytes + row * 4;
+          const uint32_t w0 = *reinterpret_cast<const uint32_t *>(wt + (2 * half) * kBM * 4);
+          const uint32_t w1 = *reinterpret_cast<const uint32_t *>(wt + (2 * half + 1) * kBM * 4);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = 4 * q4 + u;
-        if (i >= nk) break;
-        const int s = ds, as = das;
-        if (!*abort_flag && !mbar_wait(&full[s], dph)) {
+          for (int c = 0; c < 4; ++c) q[c] = dequant_t2(c < 2 ? w0 : w1, 16 * (c & 1), s2);
+        } else {
+          const uint4 w = *reinterpret_cast<const uint4 *>(smem + L.w + s * kWTileBytes + row * 32 + half * 16);
+          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) q[c] = dequant_word(wv[c], s2);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) r[4 * c] = q[c].x, r[4 * c + 1] = q[c].y, r[4 * c + 2] = q[c].z, r[4 * c + 3] = q[c].w;
+      };
+      auto wait_stage = [&](int s, uint32_t ph, int as, int ar) {
+        if (!*abort_flag && !mbar_wait(&full[s], ph)) {
           raise_status(kStatusGemmDeqWait);
           *abort_flag = 1;
         }
-        if (split_rings && dar > 0 && !*abort_flag && !mbar_wait(&aempty[as], (dar - 1) & 1)) {
+        if (split_rings && ar > 0 && !*abort_flag && !mbar_wait(&aempty[as], (ar - 1) & 1)) {
           raise_status(kStatusGemmDeqWait);
           *abort_flag = 1;
         }
-        // tcgen05.st is warp-collective: the warp stores only if every lane may.
-        if (__all_sync(0xffffffffu, !*abort_flag)) {
-          // this thread's 32 k of the stage share one group for G >= 32: (s, s) as half2
-          __half2 s2;
-          if (G == 32) {
-            const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[u]);
-            s2 = half ? __high2half2(pair) : __low2half2(pair);
-          } else if (G == 64) {
-            const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[u >> 1]);
-            s2 = (u & 1) ? __high2half2(pair) : __low2half2(pair);
-          } else {
-            const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[0]);
-            s2 = (u >> 1) ? __high2half2(pair) : __low2half2(pair);
-          }
-          uint4 q[4];  // 32 fp16 in K order
-          if (MODE == kTernary) {  // word rows 2 half, 2 half + 1 of this output: codes k = 32 half ..
-            const uint8_t *wt = smem + L.w + s * kWTileBytes + row * 4;
-            const uint32_t w0 = *reinterpret_cast<const uint32_t *>(wt + (2 * half) * kBM * 4);
-            const uint32_t w1 = *reinterpret_cast<const uint32_t *>(wt + (2 * half + 1) * kBM * 4);
+      };
+      if constexpr (kPairs) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) q[c] = dequant_t2(c < 2 ? w0 : w1, 16 * (c & 1), s2);
-          } else {
-            const uint4 w = *reinterpret_cast<const uint4 *>(smem + L.w + s * kWTileBytes + row * 32 + half * 16);
-            const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int c = 0; c < 4; ++c) q[c] = dequant_word(wv[c], s2);
+        for (int u = 0; u < 4; u += 2) {
+          const int i = 4 * q4 + u;
+          if (i >= nk) break;
+          const bool two = i + 1 < nk;
+          const int s0 = ds, as0 = das, ar0 = dar;
+          const uint32_t ph0 = dph;
+          if (++ds == S) ds = 0, dph ^= 1;
+          if (++das == SA) das = 0, ++dar;
+          int s1 = 0, as1 = 0, ar1 = 0;
+          uint32_t ph1 = 0;
+          if (two) {
+            s1 = ds, as1 = das, ar1 = dar, ph1 = dph;
+            if (++ds == S) ds = 0, dph ^= 1;
+            if (++das == SA) das = 0, ++dar;
           }
-          const uint32_t r[16] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w,
-                                  q[2].x, q[2].y, q[2].z, q[2].w, q[3].x, q[3].y, q[3].z, q[3].w};
-          tmem_st16(a_t0 + as * kACols, r);
-          tmem_wait_st();
+          wait_stage(s0, ph0, as0, ar0);
+          if (two) wait_stage(s1, ph1, as1, ar1);
+          if (__all_sync(0xffffffffu, !*abort_flag)) {
+            uint32_t r0[16], r1[16];
+            dq(u, s0, r0);
+            if (two) dq(u + 1, s1, r1);
+            tmem_st16(a_t0 + as0 * kACols, r0);
+            if (two) tmem_st16(a_t0 + as1 * kACols, r1);
+            tmem_wait_st();
+          }
+          tc_fence_before();
+          mbar_arrive(&deq[as0]);
+          if (two) mbar_arrive(&deq[as1]);
         }
-        tc_fence_before();  // orders the TMEM stores before the arrive that the MMA thread acquires
-        mbar_arrive(&deq[as]);
-        if (++ds == S) {
-          ds = 0;
-          dph ^= 1;
-        }
-        if (++das == SA) {
-          das = 0;
-          ++dar;
+      } else {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int i = 4 * q4 + u;
+          if (i >= nk) break;
+          const int s = ds, as = das;
+          wait_stage(s, dph, as, dar);
+          if (__all_sync(0xffffffffu, !*abort_flag)) {  // tcgen05.st is warp-collective
+            uint32_t r[16];
+            dq(u, s, r);
+            tmem_st16(a_t0 + as * kACols, r);
+            tmem_wait_st();
+          }
+          tc_fence_before();  // orders the TMEM stores before the arrive that the MMA thread acquires
+          mbar_arrive(&deq[as]);
+          if (++ds == S) {
+            ds = 0;
+            dph ^= 1;
+          }
+          if (++das == SA) {
+            das = 0;
+            ++dar;
+          }
         }
       }
 #pragma unroll
