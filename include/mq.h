@@ -44,6 +44,7 @@ extern "C" {
 #define MQ_ECUDA (-3)        /* a CUDA call failed (launch error, no device, ...) */
 #define MQ_EUNSUPPORTED (-4) /* the device is not sm_100 or the size is above a stated maximum */
 #define MQ_ETIMEOUT (-5)     /* a kernel's bounded wait ran out (see mq_device_status) */
+#define MQ_EIO (-6)          /* a file could not be opened or read */
 
 /* Activation dtypes. */
 #define MQ_F32 0
@@ -248,6 +249,15 @@ MQ_API int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, const 
                           const uint16_t *gu_ws, const uint32_t *dn_wq, const uint16_t *dn_ws, float *y, int64_t tokens,
                           int experts, int topk, int64_t d, int64_t fe, int group, int add, void *workspace,
                           size_t workspace_bytes, void *stream);
+
+/* ---- weight files -------------------------------------------------------------------------------- */
+
+/* Reads nbytes at byte `offset` of the file at `path` into device memory at dst, through two pinned
+ * staging buffers whose host-to-device copies run on `stream` while the next chunk is read; returns
+ * when every copy has finished. Replaces M_driver_remote_file (qwen3moe/model.mojo:156-158), which
+ * the reference's manifest loaders call once per tensor. MQ_EIO when the file cannot be opened or
+ * read; MQ_EINVAL when the range passes the end of the file. */
+MQ_API int mq_read_file_to_device(void *dst, int64_t nbytes, const char *path, int64_t offset, void *stream);
 
 /* ---- packers: the byte layouts above, produced on the device -------------------------------------- */
 

@@ -9,3 +9,4 @@
 #include "gemm_q4.cu"
 #include "moe.cu"
 #include "pack.cu"
+#include "io.cu"

@@ -11,3 +11,4 @@ from .kernels import *  # noqa: F401,F403
 from .moe import *  # noqa: F401,F403
 from .ep import ExpertParallelMoE, expert_range  # noqa: F401
 from .pack import *  # noqa: F401,F403
+from .formats import GGUF, Manifest, read_file_to_device, read_gguf  # noqa: F401

@@ -39,6 +39,7 @@ SIGNATURES = {
     "mq_quantize_q4": (c_int, [c_vp, c_int, c_i64, c_i64, c_int, c_int, c_vp, c_vp, c_vp]),
     "mq_q4_0_to_words": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp]),
     "mq_pack_ternary": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp]),
+    "mq_read_file_to_device": (c_int, [c_vp, c_i64, c_char_p, c_i64, c_vp]),
     "mq_pack_half": (c_int, [c_vp, c_vp, c_i64, c_vp]),
 }
 
