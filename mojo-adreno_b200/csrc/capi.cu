@@ -63,9 +63,36 @@ EncodeTiledFn encode_fn() {
 }
 }  // namespace
 
+namespace {
+// The last maps this thread encoded, by their full description: a decode step encodes the same
+// few maps every call, and the driver call costs about as much as the kernel launch. A map holds
+// only the address, sizes and strides it was built from, so an equal description gives an equal map.
+struct TmapKey {
+  const void *base;
+  uint64_t cols, rows, row_stride;
+  uint32_t box_cols, box_rows;
+  int dtype, swizzle;
+  bool operator==(const TmapKey &o) const {
+    return base == o.base && cols == o.cols && rows == o.rows && row_stride == o.row_stride &&
+           box_cols == o.box_cols && box_rows == o.box_rows && dtype == o.dtype && swizzle == o.swizzle;
+  }
+};
+constexpr int kTmapCache = 32;
+thread_local TmapKey t_keys[kTmapCache];
+thread_local CUtensorMap t_maps[kTmapCache];
+thread_local int t_nkeys = 0, t_next = 0;
+}  // namespace
+
 int encode_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem_bytes, uint64_t cols,
                    uint64_t rows, uint64_t row_stride_bytes, uint32_t box_cols, uint32_t box_rows,
                    CUtensorMapSwizzle swizzle, const char *what) {
+  const TmapKey key{base, cols, rows, row_stride_bytes, box_cols, box_rows, static_cast<int>(dtype),
+                    static_cast<int>(swizzle)};
+  for (int i = 0; i < t_nkeys; ++i)
+    if (t_keys[i] == key) {
+      *map = t_maps[i];
+      return MQ_OK;
+    }
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(MQ_ECUDA, "%s: cuTensorMapEncodeTiled is not available from the driver", what);
   if (reinterpret_cast<uintptr_t>(base) % 16 || row_stride_bytes % 16 || (box_cols * elem_bytes) % 16)
@@ -77,6 +104,10 @@ int encode_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype
   CUresult r = fn(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MQ_ECUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+  t_keys[t_next] = key;
+  t_maps[t_next] = *map;
+  t_next = (t_next + 1) % kTmapCache;
+  if (t_nkeys < kTmapCache) ++t_nkeys;
   return MQ_OK;
 }
 

@@ -55,6 +55,7 @@ class MQError(RuntimeError):
 class _Lib:
     def __init__(self):
         self._dll = None
+        self._fns = {}
 
     def load(self):
         if self._dll is None:
@@ -72,7 +73,10 @@ class _Lib:
 
     def call(self, name, *args):
         """Calls entry point `name`; raises MQError on a negative status."""
-        rc = getattr(self.load(), name)(*args)
+        fn = self._fns.get(name)
+        if fn is None:
+            fn = self._fns[name] = getattr(self.load(), name)
+        rc = fn(*args)
         if rc < 0:
             raise MQError(rc, f"{name}: {self.load().mq_last_error().decode()}")
         return rc
