@@ -240,26 +240,54 @@ def run_mq(args):
         del gm, cw, cs
 
     # ---- end to end through the public API: x from pinned host, logits back, every step ------
-    # The step's activations travel as one pinned block in one copy; each GEMV reads its slice.
+    # The step's activations travel as one pinned block in one copy; each GEMV reads its slice. The
+    # copies run on a second stream, double-buffered: step i+1's upload and step i's logits read
+    # overlap the GEMVs, as a serving loop would run them.
     x_host = torch.cat([m["x"].reshape(-1) for m in mats]).cpu().pin_memory()
-    x_dev = torch.empty_like(x_host, device=dev)
-    x_views, at = [], 0
-    for m in mats:
-        x_views.append(x_dev[at:at + m["x"].numel()].view(m["x"].shape))
-        at += m["x"].numel()
-    y_host = torch.empty(mats[-1]["y"].shape, dtype=torch.float32).pin_memory()
+    x_dev = [torch.empty_like(x_host, device=dev) for _ in range(2)]
+    x_views = [[], []]
+    for b in range(2):
+        at = 0
+        for m in mats:
+            x_views[b].append(x_dev[b][at:at + m["x"].numel()].view(m["x"].shape))
+            at += m["x"].numel()
+    y_dev = [torch.empty_like(mats[-1]["y"]) for _ in range(2)]
+    y_host = [torch.empty(mats[-1]["y"].shape, dtype=torch.float32).pin_memory() for _ in range(2)]
     h2d = x_host.numel() * x_host.element_size()
-    d2h = y_host.numel() * 4
+    d2h = y_host[0].numel() * 4
     e2e_steps = max(10, args.steps // 4)
+    copy_stream = torch.cuda.Stream(device=dev)
+    up_done = [torch.cuda.Event() for _ in range(2)]    # x_dev[b] filled
+    used = [torch.cuda.Event() for _ in range(2)]       # the GEMVs that read x_dev[b] / wrote y_dev[b] are done
+    read_done = [torch.cuda.Event() for _ in range(2)]  # y_dev[b] is on the host
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    with torch.cuda.stream(copy_stream):
+        copy_stream.wait_stream(stream)
+        x_dev[0].copy_(x_host, non_blocking=True)
+        up_done[0].record(copy_stream)
     for i in range(e2e_steps):
-        x_dev.copy_(x_host, non_blocking=True)
+        b, nb = i % 2, (i + 1) % 2
+        if i + 1 < e2e_steps:  # next step's upload, once the GEMVs of step i - 1 no longer read x_dev[nb]
+            with torch.cuda.stream(copy_stream):
+                if i >= 1:
+                    copy_stream.wait_event(used[nb])
+                x_dev[nb].copy_(x_host, non_blocking=True)
+                up_done[nb].record(copy_stream)
+        stream.wait_event(up_done[b])
+        if i >= 2:
+            stream.wait_event(read_done[b])  # y_dev[b] of step i - 2 has reached the host
         c = i % copies
-        for m, xv in zip(mats, x_views):
-            mq.gemv_q4(m["wqs"][c], m["wss"][c], xv, m["y"], m["k"], group=GROUP)
-        y_host.copy_(mats[-1]["y"], non_blocking=True)
+        for j, (m, xv) in enumerate(zip(mats, x_views[b])):
+            out = y_dev[b] if j == len(mats) - 1 else m["y"]
+            mq.gemv_q4(m["wqs"][c], m["wss"][c], xv, out, m["k"], group=GROUP)
+        used[b].record(stream)
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(used[b])
+            y_host[b].copy_(y_dev[b], non_blocking=True)
+            read_done[b].record(copy_stream)
+    stream.wait_stream(copy_stream)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / e2e_steps
@@ -407,8 +435,9 @@ def run_mq(args):
                        "step": "the 5 GEMVs of a decode step, recorded once as a CUDA graph and replayed",
                        "l2": f"inputs larger than L2: {copies} rotating weight copies per rank"},
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "note": "mq.gemv_q4 python API call per matrix (no graph); the step's x vectors from pinned host "
-                            "in one copy and the lm_head logits to host, every step"},
+                    "note": "mq.gemv_q4 python API call per matrix (no graph); every step the step's x vectors from "
+                            "pinned host in one copy and the lm_head logits to pinned host, on a copy stream "
+                            "double-buffered against the GEMVs"},
             "roofline": {"bound": "hbm", "kernel": "gemv_q4_kernel<32,1,true> (lm_head shard)",
                          "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "traffic": traffic, "algorithmic_bytes_per_launch": q4_bytes(head["n"], head["k"], batch),
