@@ -209,9 +209,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Stage x once per CTA. Item (t, c, q, j) = the 8 values of word j of quad q in 128-k chunk c of
   // vector t; the 4 items of a quad (one 32-k group) are 4 consecutive lanes, which share its scale.
-  for (int i = threadIdx.x; i < nt * nsteps * 8; i += kThreads) bfrag[i] = make_uint2(0u, 0u);
-  for (int i = threadIdx.x; i < nt * kc * 4; i += kThreads) xs[i] = 0.f;
-  __syncthreads();
+  // Vectors t < B are written whole below (items past K as zeros); only the unused t >= B (NT > B)
+  // are zeroed, so the two passes touch disjoint entries and need no barrier between them.
+  for (int i = B * nsteps * 8 + threadIdx.x; i < nt * nsteps * 8; i += kThreads) bfrag[i] = make_uint2(0u, 0u);
+  for (int i = B * kc * 4 + threadIdx.x; i < nt * kc * 4; i += kThreads) xs[i] = 0.f;
   const int nitems = B * kc * 16;
   for (int base = 0; base < nitems; base += kThreads) {
     const int it = base + threadIdx.x;
