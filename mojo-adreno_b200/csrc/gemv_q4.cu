@@ -214,6 +214,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   for (int i = B * nsteps * 8 + threadIdx.x; i < nt * nsteps * 8; i += kThreads) bfrag[i] = make_uint2(0u, 0u);
   for (int i = B * kc * 4 + threadIdx.x; i < nt * kc * 4; i += kThreads) xs[i] = 0.f;
   const int nitems = B * kc * 16;
+  // Warps with no staging item (32 * warp >= nitems) issue their first loads now: they would only
+  // wait at the staging barrier, which their TMA holds do not outlast. The others issue after it.
+  const bool early = 32 * warp >= nitems;
+  if (early)
+    for (int s = 0; s < S; ++s) issue(s);
   for (int base = 0; base < nitems; base += kThreads) {
     const int it = base + threadIdx.x;
     const bool live = it < nitems;
@@ -261,10 +266,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
 
-  // The first loads go out only now: a TMA instruction holds lane 0's warp for ~0.2 us, and issued
-  // before the staging they held the staging barrier back by up to 2 us (traced); the tiles are
-  // L2-warm from the prefetch above.
-  for (int s = 0; s < S; ++s) issue(s);
+  // The staging warps' first loads go out only now: a TMA instruction holds lane 0's warp for
+  // ~0.2 us, and issued before the staging they held the staging barrier back by up to 2 us
+  // (traced); the tiles are L2-warm from the prefetch above.
+  if (!early)
+    for (int s = 0; s < S; ++s) issue(s);
 
   const int g = lane >> 2, q = lane & 3;
   const bool act = q == (g >> 1);  // lanes whose B fragment is non-zero (column g belongs to quad g / 2)
