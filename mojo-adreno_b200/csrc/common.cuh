@@ -52,10 +52,11 @@ int launch_overlapped(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
 }
 
 namespace gemv {
-// The expert-indirect GEMV of the MoE decode (gemv_q4.cu); gate_up fuses the SwiGLU of gate|up rows.
-int gemv_q4_grouped(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const float *x, float *y,
+// The expert-indirect GEMV of the MoE decode (gemv_q4.cu); gate_up fuses the SwiGLU of gate|up rows;
+// x is fp32, or fp16 with x_f16.
+int gemv_q4_grouped(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const void *x, float *y,
                     const int32_t *ids, int ngroups, int group_rows, int rows_per_group, int64_t k, int group, int xpg,
-                    cudaStream_t stream, int gate_up);
+                    cudaStream_t stream, int gate_up, int x_f16);
 }  // namespace gemv
 
 // The grouped expert GEMM (gemm_q4.cu): mode 1 gate|up + SiLU (fp16 out), mode 2 plain (fp32 out).
@@ -78,6 +79,22 @@ int encode_tmap_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype
                    uint64_t rows, uint64_t planes, uint64_t row_stride_bytes, uint64_t plane_stride_bytes,
                    uint32_t box_cols, uint32_t box_rows, uint32_t box_planes, CUtensorMapSwizzle swizzle,
                    const char *what);
+
+// Raises kern's dynamic shared-memory limit to at least `smem` on the current device, once per
+// device: the attribute belongs to the device's context, so a process that drives several GPUs sets
+// it on each. `seen` is the kernel's own table of the limits already set, by device.
+template <typename Kern>
+int ensure_smem(Kern kern, size_t smem, size_t (&seen)[64], const char *what) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) return fail(MQ_ECUDA, "%s: cudaGetDevice failed", what);
+  if (smem > seen[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return fail(MQ_ECUDA, "%s: cudaFuncSetAttribute: %s", what, cudaGetErrorString(e));
+    seen[dev] = smem;
+  }
+  return MQ_OK;
+}
 
 #define MQ_REQUIRE(cond, code, ...)           \
   do {                                        \

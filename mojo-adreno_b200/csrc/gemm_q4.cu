@@ -597,12 +597,8 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
     if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_gemm_q4: zeroing y: %s", cudaGetErrorString(e));
   }
   auto kern = gemm_q4_kernel<G, MODE>;
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_gemm_q4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured = smem;
-  }
+  static size_t configured[64] = {};
+  if (int rc = ensure_smem(kern, smem, configured, "mq_gemm_q4")) return rc;
   // y through TMA stores when the tensor map can describe it (16-byte base and row stride) and the
   // [bn][128] fp32 staging tile fits where the rings were.
   CUtensorMap ymap = xmap;  // not read unless y_tma
@@ -653,12 +649,8 @@ int launch_grouped(const uint32_t *wq, const __half *ws, const __half *xs, int64
                               p.bn, CU_TENSOR_MAP_SWIZZLE_128B, "mq_moe_gemm_q4 activations"))
     return rc;
   auto kern = gemm_q4_kernel<G, MODE>;
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_moe_gemm_q4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured = smem;
-  }
+  static size_t configured[64] = {};
+  if (int rc = ensure_smem(kern, smem, configured, "mq_moe_gemm_q4")) return rc;
   p.y_tma = 0;
   return launch_overlapped(kern, dim3(max_tiles * p.tiles_n), dim3(kThreads), smem, stream, "mq_moe_gemm_q4", wmap, xmap,
                            xmap, p);

@@ -481,12 +481,8 @@ int launch(const uint32_t *wq, Params p, cudaStream_t stream, const DeviceInfo &
   p.rt = kWarps / p.ks;
   p.nrounds = (p.tiles + p.rt - 1) / p.rt;
   auto kern = gemv_q4_kernel<G, NT>;
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_gemv_q4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured = smem;
-  }
+  static size_t configured[64] = {};
+  if (int rc = ensure_smem(kern, smem, configured, "mq_gemv_q4")) return rc;
   const int grid = std::min(p.nrounds, dev.sms);
   return launch_overlapped(kern, dim3(grid), dim3(kThreads), smem, stream, "mq_gemv_q4", wmap, smap, p);
 }
@@ -546,11 +542,12 @@ int gemv_q4_gate_up(const uint32_t *wq, const uint16_t *ws, const void *x, int x
 }
 
 // The expert-indirect GEMV of the MoE decode: y[i * rows_per_group + r] = W[ids[i] * group_rows + r] . x_i
-// for i < ngroups, r < rows_per_group, x_i = x (shared) or x + i * k (xpg). fp32 x. With gate_up,
-// y[i * rows_per_group + j] = silu(W[e_i * group_rows + j] . x) * (W[e_i * group_rows + rows_per_group + j] . x).
-int gemv_q4_grouped(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const float *x, float *y,
+// for i < ngroups, r < rows_per_group, x_i = x (shared) or x + i * k (xpg); fp32 x, or fp16 with x_f16.
+// With gate_up, y[i * rows_per_group + j] = silu(W[e_i * group_rows + j] . x_i) *
+// (W[e_i * group_rows + rows_per_group + j] . x_i).
+int gemv_q4_grouped(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const void *x, float *y,
                     const int32_t *ids, int ngroups, int group_rows, int rows_per_group, int64_t k, int group, int xpg,
-                    cudaStream_t stream, int gate_up) {
+                    cudaStream_t stream, int gate_up, int x_f16) {
   DeviceInfo dev;
   if (int rc = device_info(&dev)) return rc;
   Params p{};
@@ -560,7 +557,7 @@ int gemv_q4_grouped(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const
   p.n = ngroups * rows_per_group;
   p.k = static_cast<int>(k);
   p.batch = xpg ? ngroups : 1;
-  p.x_f16 = 0;
+  p.x_f16 = x_f16 != 0;
   p.add = 0;
   p.wrows = static_cast<int>(wrows);
   p.ids = ids;
@@ -594,7 +591,7 @@ extern "C" int mq_moe_gemv_q4(const uint32_t *wq, const uint16_t *ws, int64_t wr
   MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(x, 16) && mq::aligned(y, 4), MQ_EALIGN,
              "mq_moe_gemv_q4: wq and x must be 16-byte aligned");
   return mq::gemv::gemv_q4_grouped(wq, ws, wrows, x, y, ids, ngroups, group_rows, rows_per_group, k, group, x_per_group,
-                                   static_cast<cudaStream_t>(stream), 0);
+                                   static_cast<cudaStream_t>(stream), 0, 0);
 }
 
 extern "C" int mq_moe_gate_up_q4(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const float *x, float *a,
@@ -609,7 +606,7 @@ extern "C" int mq_moe_gate_up_q4(const uint32_t *wq, const uint16_t *ws, int64_t
   MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(ws, 2) && mq::aligned(x, 16) && mq::aligned(a, 4), MQ_EALIGN,
              "mq_moe_gate_up_q4: wq and x must be 16-byte aligned");
   return mq::gemv::gemv_q4_grouped(wq, ws, wrows, x, a, ids, ngroups, static_cast<int>(2 * fe), static_cast<int>(fe), k,
-                                   group, 0, static_cast<cudaStream_t>(stream), 1);
+                                   group, 0, static_cast<cudaStream_t>(stream), 1, 0);
 }
 
 extern "C" int mq_gate_up_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *a, int64_t f,

@@ -194,14 +194,14 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
 }
 
 // ---- gather: expert-sorted fp16 copies of the tokens' rows ---------------------------------------
-// xg[s] = fp16(x[order[s] / topk]) (p_gather of lfm2moe/kernels/mk.mojo:164-176).
+// xg[s] = fp16(x[order[s] / topk]) (p_gather of lfm2moe/kernels/mk.mojo:164-176); order null: s / topk.
 __global__ void gather_kernel(const void *__restrict__ x, int x_f16, const int32_t *__restrict__ order, int pairs,
                               int topk, int d, __half *__restrict__ xg) {
   const int vec = d / 8;  // 8 values per thread step
   for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < static_cast<int64_t>(pairs) * vec;
        it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int s = static_cast<int>(it / vec), c = static_cast<int>(it % vec) * 8;
-    const int t = order[s] / topk;
+    const int t = (order ? order[s] : s) / topk;  // no order: the pairs in their own order
     uint4 out;
     if (x_f16) {
       out = *reinterpret_cast<const uint4 *>(static_cast<const __half *>(x) + static_cast<size_t>(t) * d + c);
@@ -419,6 +419,7 @@ namespace mq {
 namespace moe {
 
 constexpr int kTileM = 64;  // tokens per expert work tile in the grouped GEMMs
+constexpr int kSmallPairs = 16;  // up to this many (token, expert) pairs the layer runs on the streaming GEMVs
 
 struct Work {
   int32_t *counts, *offsets, *order, *slot_of, *tiles, *ntiles;
@@ -483,13 +484,31 @@ extern "C" int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, co
     // moe_down do (moek.mojo:200-223): a = silu(gate_e x) * (up_e x) in one launch, z_k = down_e a_k,
     // y (+)= sum_k w_k z_k.
     float *a = reinterpret_cast<float *>(w.a), *z = w.z;
-    if (int rc = mq::gemv::gemv_q4_grouped(gu_wq, gu_ws, experts * 2 * fe, static_cast<const float *>(x), a, ids, topk,
-                                           static_cast<int>(2 * fe), static_cast<int>(fe), d, group, 0, s, 1))
+    if (int rc = mq::gemv::gemv_q4_grouped(gu_wq, gu_ws, experts * 2 * fe, x, a, ids, topk, static_cast<int>(2 * fe),
+                                           static_cast<int>(fe), d, group, 0, s, 1, 0))
       return rc;
     if (int rc = mq::gemv::gemv_q4_grouped(dn_wq, dn_ws, experts * d, a, z, ids, topk, static_cast<int>(d),
-                                           static_cast<int>(d), fe, group, 1, s, 0))
+                                           static_cast<int>(d), fe, group, 1, s, 0, 0))
       return rc;
     return mq_moe_combine(z, nullptr, weights, 1, topk, d, add, y, s);
+  }
+  if (P <= mq::moe::kSmallPairs) {
+    // A few pairs (a small decode batch; an expert-parallel rank's share of one token): the same
+    // streaming GEMVs with each pair's own x, fp16 as the grouped GEMMs take it, instead of grouping
+    // tokens for tensor-core tiles they would barely fill.
+    float *a = reinterpret_cast<float *>(w.a), *z = w.z;
+    mq::DeviceInfo dev;
+    if (int rc = mq::device_info(&dev)) return rc;
+    mq::moe::gather_kernel<<<mq::moe::grid_for(P * (d / 8), 256, dev), 256, 0, s>>>(
+        x, x_dtype == MQ_F16, nullptr, static_cast<int>(P), topk, static_cast<int>(d), w.xg);
+    if (int rc = mq::check_launch("mq_moe_forward gather")) return rc;
+    if (int rc = mq::gemv::gemv_q4_grouped(gu_wq, gu_ws, experts * 2 * fe, w.xg, a, ids, static_cast<int>(P),
+                                           static_cast<int>(2 * fe), static_cast<int>(fe), d, group, 1, s, 1, 1))
+      return rc;
+    if (int rc = mq::gemv::gemv_q4_grouped(dn_wq, dn_ws, experts * d, a, z, ids, static_cast<int>(P), static_cast<int>(d),
+                                           static_cast<int>(d), fe, group, 1, s, 0, 0))
+      return rc;
+    return mq_moe_combine(z, nullptr, weights, tokens, topk, d, add, y, s);
   }
   if (int rc = mq_moe_group(ids, tokens, topk, experts, mq::moe::kTileM, w.counts, w.offsets, w.order, w.slot_of, w.tiles,
                             w.ntiles, s))

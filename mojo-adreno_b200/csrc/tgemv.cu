@@ -416,12 +416,8 @@ int launch_sk(const uint32_t *w, Params p, cudaStream_t stream, const DeviceInfo
     smap = wmap;  // not read
   }
   auto kern = tgemv_kernel<NB, SK>;
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_tgemv: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    configured = smem;
-  }
+  static size_t configured[64] = {};
+  if (int rc = ensure_smem(kern, smem, configured, "mq_tgemv")) return rc;
   return launch_overlapped(kern, dim3(grid), dim3(kThreads), smem, stream, "mq_tgemv", wmap, smap, p);
 }
 

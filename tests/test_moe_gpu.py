@@ -74,7 +74,7 @@ def test_moe_forward_matches_transformers_block(cuda):
     assert normwise(y, z["y"]) <= TOL
 
 
-@pytest.mark.parametrize("tokens", [404, 1, 3])
+@pytest.mark.parametrize("tokens", [404, 1, 2, 3])
 def test_moe_forward_baseline_config(cuda, tokens):
     """Qwen3-30B-A3B MoE layer shapes (hidden 2048, 128 experts, top-8, FE 768,
     int4 G=32); 404 prompt tokens, and 1-token decode."""
@@ -83,6 +83,18 @@ def test_moe_forward_baseline_config(cuda, tokens):
     r = np.random.default_rng(1).standard_normal((tokens, 2048)).astype(np.float32)
     y = run_forward(cuda, m["x"], ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 2048, 768, 32, add_to=r.copy())
     ref = r + omoe.moe_layer(m["x"], ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 32, 768)
+    assert normwise(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("tokens,topk", [(2, 8), (16, 1), (5, 3)])
+def test_moe_forward_small_pairs_fp16(cuda, tokens, topk):
+    """Up to 16 (token, expert) pairs run on the streaming GEMVs with each pair's own fp16 x (a small
+    decode batch, an expert-parallel rank's rows): the layer oracle on the fp16-rounded x."""
+    m = synth.moe_layer(seed=7, tokens=tokens)
+    ids, w = omoe.route(m["logits"], topk)
+    x16 = m["x"].astype(np.float16)
+    y = run_forward(cuda, x16, ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 2048, 768, 32)
+    ref = omoe.moe_layer(x16.astype(np.float32), ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 32, 768)
     assert normwise(y, ref) <= TOL
 
 
