@@ -239,6 +239,19 @@ def run_mq(args):
         per_matrix[m["name"]] = round(time_graphs([gm], 10, stream) / len(cw), 5)
         del gm, cw, cs
 
+    # ---- BASELINE configs[0] on the GPU: the Q4_0 GEMV 8192x2048 (the CPU-runnable case), L2-cold
+    cx, cwq, cws = synth.gemv_config1(seed=0)
+    c0 = dict(wq=torch.from_numpy(cwq.view(np.int32)).to(dev), ws=torch.from_numpy(cws).to(dev))
+    cw, cs = cold(c0)
+    ctx_, cty = torch.from_numpy(cx).to(dev), torch.empty(1, 8192, device=dev)
+    gc = graph_of(lambda: [mq.gemv_q4(w_, s_, ctx_, cty, 2048, group=GROUP) for w_, s_ in zip(cw, cs)])
+    c0_ms = max_over_ranks(time_graphs([gc], 10, stream) / len(cw), world)
+    config0 = {"shape": [8192, 2048], "ms": round(c0_ms, 5),
+               "GB/s": round(q4_bytes(8192, 2048, 1) / (c0_ms * 1e-3) / 1e9, 1),
+               "frac_of_measured_hbm": round(q4_bytes(8192, 2048, 1) / (c0_ms * 1e-3) / 1e9 / peaks()[0], 4),
+               "frac_of_nominal_8tbs": round(q4_bytes(8192, 2048, 1) / (c0_ms * 1e-3) / 1e9 / 8000.0, 4)}
+    del gc, cw, cs, c0
+
     # ---- end to end through the public API: x from pinned host, logits back, every step ------
     # The step's activations travel as one pinned block in one copy; each GEMV reads its slice. The
     # copies run on a second stream, double-buffered: step i+1's upload and step i's logits read
@@ -440,9 +453,11 @@ def run_mq(args):
                             "double-buffered against the GEMVs"},
             "roofline": {"bound": "hbm", "kernel": "gemv_q4_kernel<32,1,true> (lm_head shard)",
                          "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                         "frac_of_nominal_8tbs": round(achieved / 8000.0, 4),
                          "traffic": traffic, "algorithmic_bytes_per_launch": q4_bytes(head["n"], head["k"], batch),
                          "peak_source": peak_src, "launch_ms": round(head_ms, 5)},
             "per_matrix_ms": per_matrix,
+            "gemv_config0": config0,
             "ternary_gemv": tern,
             "fused_decode_epilogues": fused,
             "prefill_gemm": prefill,
@@ -562,25 +577,33 @@ class CpuSample:
         self.bytes = q4_bytes(rows, 2048, 1)
         self.rows = rows
 
-    def run(self):
-        """Returns the seconds one dequantise + matmul of the sample takes."""
+    def run(self, parts=None):
+        """Returns the seconds one dequantise + matmul of the sample takes (and, into `parts`, the
+        dequantise and the matmul apart)."""
         from oracle import q4
 
         t0 = time.perf_counter()
         w = torch.from_numpy(q4.dequant(self.wq, self.ws, GROUP))
+        t1 = time.perf_counter()
         y = self.x @ w.T
-        dt = time.perf_counter() - t0
+        t2 = time.perf_counter()
         assert torch.isfinite(y).all()
-        return dt
+        if parts is not None:
+            parts.append((t1 - t0, t2 - t1))
+        return t2 - t0
 
 
 def cpu_baseline(budget_s=10.0):
     torch.set_num_threads(os.cpu_count())
     smp = CpuSample(8192)
     dt = smp.run()  # warm-up and sizing
-    reps = min(50, max(3, int(budget_s / max(dt, 1e-3))))
-    med = statistics.median(smp.run() for _ in range(reps))
+    reps = min(50, max(5, int(budget_s / max(dt, 1e-3))))
+    parts = []
+    med = statistics.median(smp.run(parts) for _ in range(reps))
     return {"value": round(smp.bytes / med / 1e9, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+            "dequantise_ms": round(1e3 * statistics.median(p[0] for p in parts), 3),
+            "matmul_ms": round(1e3 * statistics.median(p[1] for p in parts), 3),
+            "total_ms": round(1e3 * med, 3),
             "sample": f"{smp.rows}x2048 Q4_0 rows (G=32) of the workload: numpy dequantise (single-threaded, as "
                       f"the reference's) + torch fp32 matmul ({torch.get_num_threads()} threads), median of {reps}",
             "cpu": platform_cpu()}
