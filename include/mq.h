@@ -241,9 +241,11 @@ MQ_API int mq_moe_combine(const float *z, const int32_t *slot_of, const float *w
                           int64_t d, int add, float *y, void *stream);
 
 /* The whole MoE layer for precomputed routing: y (+)= sum_k w[t][k] * down_e(silu(gate_e x_t) * up_e x_t).
- * One fp32 token runs the decode GEMVs (mq_moe_gemv_q4); otherwise group, gather, the two grouped
- * products and the combine run on `stream`. Both use a caller workspace of
- * mq_moe_workspace_size() bytes (256-byte aligned). d % 256 == 0, fe % 256 == 0. */
+ * Up to 16 (token, expert) pairs run on the streaming GEMVs (gate|up with the SwiGLU fused, then down,
+ * each pair with its own x); more run group, gather, the two grouped tensor-core products and the
+ * combine. All on `stream`, with a caller workspace of mq_moe_workspace_size() bytes (256-byte
+ * aligned). d % 256 == 0, fe % 256 == 0. An expert id outside [0, experts) is reported through
+ * mq_device_status; the grouped path leaves its pair out, the GEMV path reads expert 0's rows for it. */
 MQ_API size_t mq_moe_workspace_size(int64_t tokens, int experts, int topk, int64_t d, int64_t fe);
 MQ_API int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, const float *weights, const uint32_t *gu_wq,
                           const uint16_t *gu_ws, const uint32_t *dn_wq, const uint16_t *dn_ws, float *y, int64_t tokens,
