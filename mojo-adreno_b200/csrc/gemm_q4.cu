@@ -14,14 +14,16 @@
 //    tile (BN rows x 128 bytes, 128-byte swizzle, zero-filled past M).
 //  * Warps 2-9 (two threads per weight row, 32 k each) dequantise the stage in registers -- byte permute,
 //    mask into an fp16 mantissa (1024 + u), one fp16x2 FMA to q = u - 8 (exact), one fp16x2
-//    multiply by the group scale (a single rounding) -- and store the fp16 tile in the canonical
-//    K-major 128-byte-swizzle layout the MMA reads.
-//  * Warp 1 owns the TMEM accumulator and one of its threads issues tcgen05.mma kind::f16
-//    (fp16 x fp16 -> fp32, M = 128, N = BN, K = 16, four per stage), committing each stage back to
-//    the producer and the final one to the epilogue.
+//    multiply by the group scale (a single rounding) -- and store the fp16 A tile into TMEM with
+//    tcgen05.st (a TMEM ring of A slots next to the accumulator; each warp writes its own lane
+//    quarter). Shared memory then carries only the W/X ring. The one-matrix modes take two stages
+//    per pass, so one store wait covers both.
+//  * Warp 1 owns the TMEM allocation and one of its threads issues tcgen05.mma kind::f16 with A read
+//    from TMEM (fp16 x fp16 -> fp32, M = 128, N = BN, K = 16, four per stage), committing each stage
+//    back to the producer (and the A slot back to the dequant warps) and the final one to the epilogue.
 //  * Warps 2-9 then move the accumulator out of TMEM (tcgen05.ld 32x32b, one weight row per
-//    thread, the two warps of a TMEM lane quarter taking alternate 32-column chunks) and store fp32 Y
-//    (+= with `add`, red.add when K is split across CTAs).
+//    thread, the two warps of a TMEM lane quarter taking alternate 32-column chunks), stage the fp32
+//    tile in the freed ring and write it with one TMA store (a reduce-add with `add` or split K).
 //  * Each CTA starts its K loop at its own 256-k offset (rotating through K): CTAs that share a
 //    token tile then read different X tiles at any moment instead of all hitting the same L2 lines.
 //  * Numerics: the product uses fp16 X and fp16 q*s (one rounding each); accumulation is fp32.
@@ -494,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (c0 + j < mcount) p.y[static_cast<size_t>(m0 + c0 + j) * p.n_out + r] = v[j];
       }
     } else if (MODE == kGateUp) {
-      // Up rows (TMEM lanes 64-127) go through shared memory (the A ring is free now) to the
+      // Up rows (TMEM lanes 64-127) go through shared memory (the W/X ring is free now) to the
       // threads holding the matching gate rows (lanes 0-63): a = silu(gate) * up, fp16. Row r's
       // column c sits at c ^ (r & 15) (bn is a multiple of 16), so the 32 rows a warp writes or reads
       // at one column fall in 16 different banks instead of one.
