@@ -523,8 +523,8 @@ def moe_bench(mq, synth, dev, stream, world, rank):
 def moe_bench_ep(mq, synth, dev, stream, world, rank, steps=30):
     """Tokens/s of the expert-parallel MoE layer (BASELINE configs[3] at N GPUs): rank r owns experts
     [r * 128 / N, (r + 1) * 128 / N) and routes its share of the tokens; dispatch and combine are NCCL
-    all-to-alls (mq.ExpertParallelMoE). Timed with CUDA events over `steps` layers, including the
-    host read of the split sizes each layer needs, max over ranks."""
+    all-to-alls in the fixed-capacity form (mq.ExpertParallelMoE with max_tokens: static split sizes,
+    no host read). Timed with CUDA events over `steps` layers, max over ranks."""
     d, fe, experts, topk = 2048, 768, 128, 8
     out = {}
     for tokens in (404, 1):
@@ -537,7 +537,8 @@ def moe_bench_ep(mq, synth, dev, stream, world, rank, steps=30):
               for a in parts]
         copies = rotating_copies(sum(a.numel() * a.element_size() for a in gw))
         gws = [gw] + [[a.clone() for a in gw] for _ in range(copies - 1)]
-        layers = [mq.ExpertParallelMoE(*g, d, fe, experts, topk=topk, group=32) for g in gws]
+        max_tokens = max(hi_ - lo_ for lo_, hi_ in (shard(tokens, world, r) for r in range(world)))
+        layers = [mq.ExpertParallelMoE(*g, d, fe, experts, topk=topk, group=32, max_tokens=max_tokens) for g in gws]
         tx = torch.from_numpy(np.ascontiguousarray(m["x"][lo_t:hi_t])).to(dev)
         if hi_t > lo_t:
             tids, tw = device_route(mq, np.ascontiguousarray(m["logits"][lo_t:hi_t]), dev)
@@ -558,7 +559,8 @@ def moe_bench_ep(mq, synth, dev, stream, world, rank, steps=30):
         ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
         out[f"tokens_{tokens}"] = {"ms": round(ms, 5), "tokens/s": round(tokens / (ms * 1e-3), 1),
                                    "parallelism": f"expert-parallel x{world} ({experts // world} experts per GPU), "
-                                                  "NCCL all-to-all dispatch and combine"}
+                                                  "NCCL all-to-all dispatch and combine, fixed capacity "
+                                                  f"{max_tokens * topk} rows per rank pair"}
         del layers, gws
     return out
 

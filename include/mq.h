@@ -200,12 +200,19 @@ MQ_API int mq_moe_group(const int32_t *ids, int64_t tokens, int topk, int expert
  * by rank r. The tokens * topk pairs are grouped stably by owning rank: counts[r], offsets[r]
  * (offsets[world] = pairs), order[offsets[r] + i] = the i-th pair sent to rank r, slot_of[pair] = its
  * send position, local_ids[pos] = the pair's expert id within its owner (ids - r * experts / world).
- * No counterpart kernel in the reference (which runs on one device). */
-MQ_API int mq_ep_plan(const int32_t *ids, int64_t tokens, int topk, int experts, int world, int32_t *counts,
-                      int32_t *offsets, int32_t *order, int32_t *slot_of, int32_t *local_ids, void *stream);
+ * capacity > 0 gives the fixed-capacity layout of an exchange with static split sizes: rank r's
+ * pairs sit at r * capacity + i, offsets[r] = r * capacity, and the other positions of order and
+ * local_ids (world * capacity entries each) hold -1; pairs past a rank's capacity are reported
+ * through mq_device_status (9) and left out (slot_of -1). A negative id means "no expert" and is
+ * left out silently; an id >= experts is reported (8). No counterpart kernel in the reference
+ * (which runs on one device). */
+MQ_API int mq_ep_plan(const int32_t *ids, int64_t tokens, int topk, int experts, int world, int capacity,
+                      int32_t *counts, int32_t *offsets, int32_t *order, int32_t *slot_of, int32_t *local_ids,
+                      void *stream);
 
 /* xg[s] = fp16(x[order[s] / topk]) for s < pairs: the expert-sorted activation rows (p_gather,
- * lfm2moe/kernels/mk.mojo:164-176). x: [tokens][d] fp32 or fp16; d % 8 == 0. */
+ * lfm2moe/kernels/mk.mojo:164-176); a row of zeros where order[s] < 0 (an empty position of a
+ * fixed-capacity layout). x: [tokens][d] fp32 or fp16; d % 8 == 0. */
 MQ_API int mq_moe_gather(const void *x, int x_dtype, const int32_t *order, int64_t pairs, int topk, int64_t d,
                          uint16_t *xg, void *stream);
 

@@ -116,7 +116,8 @@ enum : int {
   kStatusGemvProducerWait = 5,
   kStatusGemvConsumerWait = 6,
   kStatusGemvDrainWait = 7,
-  kStatusMoeBadExpertId = 8,  // an expert id outside [0, experts): the pair was left out
+  kStatusMoeBadExpertId = 8,  // an expert id >= experts: the pair was left out (negative ids mean "none")
+  kStatusEpOverflow = 9,      // more pairs for one rank than the plan's capacity: the excess was left out
 };
 
 // Waits until the kernels this grid depends on (earlier work on its stream) have completed and

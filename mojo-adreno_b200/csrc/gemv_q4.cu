@@ -73,13 +73,16 @@ struct Params {
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
 
 // First weight row of output tile `tile` (the rows themselves, or an expert's rows through ids).
-// An expert id outside the weight matrix is reported and read as expert 0.
+// An expert id past the weight matrix is reported and read as expert 0; a negative id ("no expert",
+// the padding of a fixed-capacity exchange) reads expert 0 silently.
 __device__ __forceinline__ int weight_row0(const Params &p, int tile) {
   const int tr = p.gu ? kRows / 2 : kRows;  // weight rows (of one kind) per output tile
   if (!p.ids) return tile * tr;
   int e = __ldg(p.ids + tile / p.tpg);
-  if (e < 0 || e >= p.wrows / p.group_rows) {
+  if (e >= p.wrows / p.group_rows) {
     raise_status(kStatusMoeBadExpertId);
+    e = 0;
+  } else if (e < 0) {
     e = 0;
   }
   return e * p.group_rows + (tile % p.tpg) * tr;

@@ -75,12 +75,17 @@ constexpr int kGroupThreads = 1024;
 
 // Pairs are bucketed by ids[i] / div (div = 1: by expert; div = experts per rank: by owning rank,
 // the expert-parallel dispatch order). tiles / ntiles may be null (no work tiles). local, when not
-// null, receives ids[i] - bucket * div at the pair's sorted position.
+// null, receives ids[i] - bucket * div at the pair's sorted position. A negative id means "no
+// expert" (the padding of a fixed-capacity exchange): the pair is left out silently.
+// cap > 0: the fixed-capacity layout of an exchange with static split sizes. Bucket b's pairs sit at
+// b * cap .. in pair order, every other position of order and local holds -1, offsets[b] = b * cap,
+// and pairs past a bucket's capacity are reported (kStatusEpOverflow) and left out.
 __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__restrict__ ids, int div, int pairs,
                                                               int experts, int tile, int32_t *__restrict__ counts,
                                                               int32_t *__restrict__ offsets, int32_t *__restrict__ order,
                                                               int32_t *__restrict__ slot_of, int32_t *__restrict__ tiles,
-                                                              int32_t *__restrict__ ntiles, int32_t *__restrict__ local) {
+                                                              int32_t *__restrict__ ntiles, int32_t *__restrict__ local,
+                                                              int cap) {
   extern __shared__ int32_t sh[];
   int32_t *warp_cnt = sh;                    // [32 warps][experts]: pairs of the warp's range, then their start
   int32_t *start = warp_cnt + 32 * experts;  // [experts + 1]: bucket totals, then offsets
@@ -91,10 +96,11 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
   // warps' ranges are in pair order and each warp walks its own range in order.
   const int per = (pairs + 31) / 32;
   const int lo = min(pairs, warp * per), hi = min(pairs, lo + per);
-  // Bucket of pair i, or -1 (reported, left out) for an id outside [0, experts * div).
+  // Bucket of pair i, or -1 (left out) for a negative id and (reported) for an id past experts * div.
   auto bucket = [&](int i) {
     const int id = ids[i];
-    if (id < 0 || id >= experts * div) {
+    if (id < 0) return -1;
+    if (id >= experts * div) {
       raise_status(kStatusMoeBadExpertId);
       return -1;
     }
@@ -155,6 +161,14 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
     }
   }
   __syncthreads();
+  if (cap > 0) {  // fixed-capacity layout: every position empty until pass 2 fills it
+    for (int e = threadIdx.x; e <= experts; e += kGroupThreads) offsets[e] = e * cap;
+    for (int pos = threadIdx.x; pos < experts * cap; pos += kGroupThreads) {
+      order[pos] = -1;
+      if (local) local[pos] = -1;
+    }
+    __syncthreads();
+  }
   // Work tiles (expert, first row, rows), bucket by bucket.
   if (tiles) {
     for (int e = threadIdx.x; e < experts; e += kGroupThreads) {
@@ -168,7 +182,7 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
   }
   // Positions past the pairs that were kept (only when ids were left out) point at pair 0, so every
   // entry of order stays a valid pair index.
-  for (int pos = start[experts] + threadIdx.x; pos < pairs; pos += kGroupThreads) {
+  for (int pos = start[experts] + threadIdx.x; cap == 0 && pos < pairs; pos += kGroupThreads) {
     order[pos] = 0;
     if (local) local[pos] = 0;
   }
@@ -180,12 +194,16 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
     const int b = i < hi ? bucket(i) : -1;
     const unsigned same = __match_any_sync(0xffffffffu, b);
     const int rank = __popc(same & lt_mask);
-    const int pos = b >= 0 ? start[b] + my_cnt[b] + rank : 0;
+    int pos = b >= 0 ? start[b] + my_cnt[b] + rank : 0;
+    if (cap > 0 && b >= 0) {
+      pos = my_cnt[b] + rank < cap ? b * cap + my_cnt[b] + rank : -1;
+      if (pos < 0) raise_status(kStatusEpOverflow);
+    }
     __syncwarp();
     if (b >= 0 && rank == 0) my_cnt[b] += __popc(same);
     __syncwarp();
-    if (i < hi && b < 0) slot_of[i] = -1;  // left out
-    if (b >= 0) {
+    if (i < hi && (b < 0 || pos < 0)) slot_of[i] = -1;  // left out
+    if (b >= 0 && pos >= 0) {
       order[pos] = i;
       slot_of[i] = pos;
       if (local) local[pos] = ids[i] - b * div;
@@ -201,7 +219,12 @@ __global__ void gather_kernel(const void *__restrict__ x, int x_f16, const int32
   for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < static_cast<int64_t>(pairs) * vec;
        it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int s = static_cast<int>(it / vec), c = static_cast<int>(it % vec) * 8;
-    const int t = (order ? order[s] : s) / topk;  // no order: the pairs in their own order
+    const int o = order ? order[s] : s;  // no order: the pairs in their own order
+    if (o < 0) {  // an empty position of a fixed-capacity layout
+      *reinterpret_cast<uint4 *>(xg + static_cast<size_t>(s) * d + c) = make_uint4(0u, 0u, 0u, 0u);
+      continue;
+    }
+    const int t = o / topk;
     uint4 out;
     if (x_f16) {
       out = *reinterpret_cast<const uint4 *>(static_cast<const __half *>(x) + static_cast<size_t>(t) * d + c);
@@ -365,20 +388,23 @@ extern "C" int mq_moe_group(const int32_t *ids, int64_t tokens, int topk, int ex
   MQ_REQUIRE(tile >= 1, MQ_EINVAL, "mq_moe_group: tile must be >= 1");
   const size_t smem = (32 * experts + 2 * (experts + 1)) * sizeof(int32_t);
   mq::moe::group_kernel<<<1, mq::moe::kGroupThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      ids, 1, static_cast<int>(tokens * topk), experts, tile, counts, offsets, order, slot_of, tiles, ntiles, nullptr);
+      ids, 1, static_cast<int>(tokens * topk), experts, tile, counts, offsets, order, slot_of, tiles, ntiles, nullptr, 0);
   return mq::check_launch("mq_moe_group");
 }
 
-extern "C" int mq_ep_plan(const int32_t *ids, int64_t tokens, int topk, int experts, int world, int32_t *counts,
-                          int32_t *offsets, int32_t *order, int32_t *slot_of, int32_t *local_ids, void *stream) {
+extern "C" int mq_ep_plan(const int32_t *ids, int64_t tokens, int topk, int experts, int world, int capacity,
+                          int32_t *counts, int32_t *offsets, int32_t *order, int32_t *slot_of, int32_t *local_ids,
+                          void *stream) {
   MQ_REQUIRE(ids && counts && offsets && order && slot_of && local_ids, MQ_EINVAL, "mq_ep_plan: null pointer");
   MQ_REQUIRE(tokens > 0 && topk >= 1 && tokens * topk < (1 << 30), MQ_EINVAL, "mq_ep_plan: bad tokens / topk");
   MQ_REQUIRE(world >= 1 && world <= 256 && experts >= world && experts % world == 0, MQ_EINVAL,
              "mq_ep_plan: experts (%d) must be a positive multiple of world (%d)", experts, world);
+  MQ_REQUIRE(capacity >= 0 && static_cast<int64_t>(capacity) * world < (1 << 30), MQ_EINVAL,
+             "mq_ep_plan: bad capacity %d", capacity);
   const size_t smem = (32 * world + 2 * (world + 1)) * sizeof(int32_t);
   mq::moe::group_kernel<<<1, mq::moe::kGroupThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       ids, experts / world, static_cast<int>(tokens * topk), world, 1, counts, offsets, order, slot_of, nullptr, nullptr,
-      local_ids);
+      local_ids, capacity);
   return mq::check_launch("mq_ep_plan");
 }
 

@@ -15,8 +15,14 @@ is then:
      does (moek.mojo:479-488).
 
 Every rank takes the same collective steps in the same order, also when it sends or receives no
-rows. The split sizes are read on the host (one small device-to-host copy per layer), which the
-variable-size all-to-all needs.
+rows. Two exchange forms:
+
+- compact (default): only the pairs travel; the split sizes are exchanged first and read on the host
+  (one small device-to-host copy per layer), which the variable-size all-to-all needs.
+- fixed capacity (max_tokens given): every rank sends max_tokens * topk row slots to every rank, its
+  pairs first and empty slots (expert id -1, zero rows) after them. The split sizes are static, so
+  the layer needs no host read and stays asynchronous on the stream; the price is the empty slots'
+  bytes on NVLink (the experts skip them).
 """
 import torch
 import torch.distributed as dist
@@ -39,16 +45,18 @@ def expert_range(experts, world, rank):
 class DeviceOps:
     """The layer's device steps, each one libmq entry point on the current CUDA stream."""
 
-    def plan(self, ids, tokens, topk, experts, world):
+    def plan(self, ids, tokens, topk, experts, world, capacity=0):
+        """capacity 0: the compact send order; > 0: the fixed-capacity layout (world * capacity slots)."""
         dev = ids.device
         pairs = tokens * topk
+        slots = world * capacity if capacity else pairs
         counts = torch.empty(world, dtype=torch.int32, device=dev)
         offsets = torch.empty(world + 1, dtype=torch.int32, device=dev)
-        order = torch.empty(pairs, dtype=torch.int32, device=dev)
+        order = torch.empty(slots, dtype=torch.int32, device=dev)
         slot_of = torch.empty(pairs, dtype=torch.int32, device=dev)
-        local = torch.empty(pairs, dtype=torch.int32, device=dev)
-        lib.call("mq_ep_plan", _p(ids), tokens, topk, experts, world, _p(counts), _p(offsets), _p(order), _p(slot_of),
-                 _p(local), _stream())
+        local = torch.empty(slots, dtype=torch.int32, device=dev)
+        lib.call("mq_ep_plan", _p(ids), tokens, topk, experts, world, capacity, _p(counts), _p(offsets), _p(order),
+                 _p(slot_of), _p(local), _stream())
         return counts, order, slot_of, local
 
     def gather(self, x, order, topk, d):
@@ -59,13 +67,19 @@ class DeviceOps:
         return xg
 
     def experts(self, rows, local_ids, gu_wq, gu_ws, dn_wq, dn_ws, d, fe, group):
+        """Each row through its expert (local id); rows with id -1 are skipped (their outputs unused)."""
         from .moe import moe_forward
 
         r = rows.shape[0]
         out = torch.empty(r, d, dtype=torch.float32, device=rows.device)
-        ones = torch.ones(r, dtype=torch.float32, device=rows.device)
+        ones = self._ones.get((r, rows.device))
+        if ones is None:
+            ones = self._ones[(r, rows.device)] = torch.ones(r, dtype=torch.float32, device=rows.device)
         moe_forward(rows, local_ids, ones, gu_wq, gu_ws, dn_wq, dn_ws, out, d, fe, group=group)
         return out
+
+    def __init__(self):
+        self._ones = {}
 
     def combine(self, ret, slot_of, weights, tokens, topk, d, add, y):
         lib.call("mq_moe_combine", _p(ret), _p(slot_of), _p(weights), tokens, topk, d, int(bool(add)), _p(y), _stream())
@@ -81,12 +95,14 @@ class ExpertParallelMoE:
     int32 and weights fp32 [T, topk] from the router, and writes (or adds into) y fp32 [T, d].
     """
 
-    def __init__(self, gu_wq, gu_ws, dn_wq, dn_ws, d, fe, experts, topk=8, group=32, pg=None, ops=None):
+    def __init__(self, gu_wq, gu_ws, dn_wq, dn_ws, d, fe, experts, topk=8, group=32, pg=None, ops=None,
+                 max_tokens=None):
         self.pg = pg
         self.world = dist.get_world_size(pg) if dist.is_initialized() else 1
         self.rank = dist.get_rank(pg) if dist.is_initialized() else 0
         self.first, self.last = expert_range(experts, self.world, self.rank)
         self.d, self.fe, self.experts, self.topk, self.group = d, fe, experts, topk, group
+        self.capacity = max_tokens * topk if max_tokens else 0  # row slots per rank pair (fixed-capacity form)
         local = self.last - self.first
         self.ops = ops if ops is not None else DeviceOps()
         if ops is None:
@@ -108,6 +124,8 @@ class ExpertParallelMoE:
         tokens = x.shape[0]
         if ids.numel() != tokens * topk or weights.numel() != tokens * topk:
             raise MQError(-1, f"ids / weights must hold tokens * topk = {tokens * topk} entries")
+        if self.capacity:
+            return self._forward_fixed(x, ids, weights, y, add)
         # 1. plan, and the rows to send, in send order (a rank without tokens still joins every exchange)
         if tokens > 0:
             counts, order, slot_of, local = self.ops.plan(ids, tokens, topk, self.experts, self.world)
@@ -134,6 +152,30 @@ class ExpertParallelMoE:
         # 4. outputs back in send order, then the weighted per-token sum in slot order
         ret = torch.empty(sent, d, dtype=torch.float32, device=send.device)
         self._a2a(ret, out, send_splits, recv_splits)
+        if tokens == 0:
+            return y
+        return self.ops.combine(ret, slot_of, weights, tokens, topk, d, add, y)
+
+    def _forward_fixed(self, x, ids, weights, y, add):
+        """The fixed-capacity exchange: static split sizes, no host read."""
+        d, topk, world, cap = self.d, self.topk, self.world, self.capacity
+        tokens = x.shape[0]
+        if tokens * topk > cap:
+            raise MQError(-1, f"{tokens} tokens exceed max_tokens = {cap // topk}")
+        splits = [cap] * world
+        if tokens > 0:
+            _, order, slot_of, local = self.ops.plan(ids, tokens, topk, self.experts, world, cap)
+            send = self.ops.gather(x, order, topk, d)
+        else:
+            order = local = torch.full((world * cap,), -1, dtype=torch.int32, device=x.device)
+            send = torch.zeros(world * cap, d, dtype=torch.float16, device=x.device)
+        rows = torch.empty_like(send)
+        self._a2a(rows, send, splits, splits)
+        rids = torch.empty_like(local)
+        self._a2a(rids, local, splits, splits)
+        out = self.ops.experts(rows, rids, *self.w, d, self.fe, self.group)
+        ret = torch.empty_like(out)
+        self._a2a(ret, out, splits, splits)
         if tokens == 0:
             return y
         return self.ops.combine(ret, slot_of, weights, tokens, topk, d, add, y)

@@ -36,7 +36,7 @@ def main():
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a.view(np.int32) if a.dtype == np.uint32 else a)).to(dev)
         moe = mq.ExpertParallelMoE(t(m["gu_wq"][lo * 2 * fe:hi * 2 * fe]), t(m["gu_ws"][lo * 2 * fe:hi * 2 * fe]),
                                    t(m["dn_wq"][lo * d:hi * d]), t(m["dn_ws"][lo * d:hi * d]), d, fe, experts, topk=topk,
-                                   group=group)
+                                   group=group, max_tokens=int(os.environ.get("EP_MAX_TOKENS") or 0) or None)
         ys = []
         for _ in range(2):  # two layers in a row through the same buffers
             y = torch.full((counts[rank], d), float("nan"), device=dev)

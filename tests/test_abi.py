@@ -97,7 +97,7 @@ def test_packers_and_ep_plan_reject_bad_arguments_before_launch():
     assert rc == -1 and "128" in msg
     rc, msg = _status("mq_pack_half", ok, ok, 7, None)
     assert rc == -1 and "even" in msg
-    rc, msg = _status("mq_ep_plan", ok, 4, 8, 128, 3, ok, ok, ok, ok, ok, None)
+    rc, msg = _status("mq_ep_plan", ok, 4, 8, 128, 3, 0, ok, ok, ok, ok, ok, None)
     assert rc == -1 and "multiple of world" in msg
 
 
