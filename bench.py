@@ -255,7 +255,10 @@ def run_mq(args):
     # ---- end to end through the public API: x from pinned host, logits back, every step ------
     # The step's activations travel as one pinned block in one copy; each GEMV reads its slice. The
     # copies run on a second stream, double-buffered: step i+1's upload and step i's logits read
-    # overlap the GEMVs, as a serving loop would run them.
+    # overlap the GEMVs, as a serving loop would run them. The GEMVs are issued two ways: eagerly
+    # (five mq.gemv_q4 calls per step, which the host issues more slowly than they run) and as a CUDA graph of
+    # those same calls, recorded once per (activation buffer, weight copy) and replayed per step,
+    # as the device-resident step above is; the copies and the cross-stream waits stay per step.
     x_host = torch.cat([m["x"].reshape(-1) for m in mats]).cpu().pin_memory()
     x_dev = [torch.empty_like(x_host, device=dev) for _ in range(2)]
     x_views = [[], []]
@@ -273,38 +276,48 @@ def run_mq(args):
     up_done = [torch.cuda.Event() for _ in range(2)]    # x_dev[b] filled
     used = [torch.cuda.Event() for _ in range(2)]       # the GEMVs that read x_dev[b] / wrote y_dev[b] are done
     read_done = [torch.cuda.Event() for _ in range(2)]  # y_dev[b] is on the host
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    with torch.cuda.stream(copy_stream):
-        copy_stream.wait_stream(stream)
-        x_dev[0].copy_(x_host, non_blocking=True)
-        up_done[0].record(copy_stream)
-    for i in range(e2e_steps):
-        b, nb = i % 2, (i + 1) % 2
-        if i + 1 < e2e_steps:  # next step's upload, once the GEMVs of step i - 1 no longer read x_dev[nb]
-            with torch.cuda.stream(copy_stream):
-                if i >= 1:
-                    copy_stream.wait_event(used[nb])
-                x_dev[nb].copy_(x_host, non_blocking=True)
-                up_done[nb].record(copy_stream)
-        stream.wait_event(up_done[b])
-        if i >= 2:
-            stream.wait_event(read_done[b])  # y_dev[b] of step i - 2 has reached the host
-        c = i % copies
+
+    def issue_step(b, c):
         for j, (m, xv) in enumerate(zip(mats, x_views[b])):
             out = y_dev[b] if j == len(mats) - 1 else m["y"]
             mq.gemv_q4(m["wqs"][c], m["wss"][c], xv, out, m["k"], group=GROUP)
-        used[b].record(stream)
+
+    def e2e_run(issue):
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
         with torch.cuda.stream(copy_stream):
-            copy_stream.wait_event(used[b])
-            y_host[b].copy_(y_dev[b], non_blocking=True)
-            read_done[b].record(copy_stream)
-    stream.wait_stream(copy_stream)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / e2e_steps
+            copy_stream.wait_stream(stream)
+            x_dev[0].copy_(x_host, non_blocking=True)
+            up_done[0].record(copy_stream)
+        for i in range(e2e_steps):
+            b, nb = i % 2, (i + 1) % 2
+            if i + 1 < e2e_steps:  # next step's upload, once the GEMVs of step i - 1 no longer read x_dev[nb]
+                with torch.cuda.stream(copy_stream):
+                    if i >= 1:
+                        copy_stream.wait_event(used[nb])
+                    x_dev[nb].copy_(x_host, non_blocking=True)
+                    up_done[nb].record(copy_stream)
+            stream.wait_event(up_done[b])
+            if i >= 2:
+                stream.wait_event(read_done[b])  # y_dev[b] of step i - 2 has reached the host
+            issue(b, i % copies)
+            used[b].record(stream)
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(used[b])
+                y_host[b].copy_(y_dev[b], non_blocking=True)
+                read_done[b].record(copy_stream)
+        stream.wait_stream(copy_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1), world) / e2e_steps
+
+    e2e_eager_ms = e2e_run(issue_step)
+    step_graphs = [[graph_of(lambda b=b, c=c: issue_step(b, c)) for c in range(copies)] for b in range(2)]
+    e2e_ms = e2e_run(lambda b, c: step_graphs[b][c].replay())
+    del step_graphs
     e2e_value = job_bytes / (e2e_ms * 1e-3) / 1e9
+    e2e_eager_value = job_bytes / (e2e_eager_ms * 1e-3) / 1e9
 
     # ---- secondary: ternary GEMV, Qwen3-8B shapes, N-sharded the same way
     tern = {}
@@ -448,9 +461,12 @@ def run_mq(args):
                        "step": "the 5 GEMVs of a decode step, recorded once as a CUDA graph and replayed",
                        "l2": f"inputs larger than L2: {copies} rotating weight copies per rank"},
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "note": "mq.gemv_q4 python API call per matrix (no graph); every step the step's x vectors from "
+                    "note": "the step's five mq.gemv_q4 API calls recorded once per (activation buffer, weight "
+                            "copy) as a CUDA graph and replayed per step; every step the step's x vectors from "
                             "pinned host in one copy and the lm_head logits to pinned host, on a copy stream "
-                            "double-buffered against the GEMVs"},
+                            "double-buffered against the GEMVs",
+                    "eager_value": round(e2e_eager_value, 1),
+                    "eager_note": "the same loop with the five mq.gemv_q4 calls issued eagerly each step"},
             "roofline": {"bound": "hbm", "kernel": "gemv_q4_kernel<32,1,true> (lm_head shard)",
                          "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "frac_of_nominal_8tbs": round(achieved / 8000.0, 4),
