@@ -3,7 +3,7 @@ definition) and tests/golden/gguf_small.json, the file as the reference's own re
 (lfm2/gguf_read.py parse, imported from the reference checkout) sees it: version, metadata, tensor
 table (dims, type, offset, type name, bytes, absolute offset) and data start.
 
-  python tests/golden/make_gguf.py [--ref /root/reference]
+  python tests/golden/make_gguf.py [--ref <reference checkout>]
 
 The file covers every metadata type (numeric arrays below and above 64 entries, string arrays),
 a non-default alignment, and F32 / F16 / Q4_0 / BF16 / Q6_K tensors; the Q4_0 tensors hold seeded

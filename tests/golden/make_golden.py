@@ -1,6 +1,6 @@
 """Writes the golden fixtures under tests/golden/ from the reference itself, run in this container.
 
-  python tests/golden/make_golden.py [--ref /root/reference]
+  python tests/golden/make_golden.py [--ref <reference checkout>]
 
 Sources (nothing here is restated; every output comes from the reference's own code):
   * llama/run.py quantize4                    -> quantize4.npz        (int4 packer, G=64, max/7)
