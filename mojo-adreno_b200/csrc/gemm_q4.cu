@@ -562,11 +562,13 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
   p.tiles_m = two_per_sm ? 1 : (p.m + 255) / 256;
   p.bn = ((p.m + p.tiles_m - 1) / p.tiles_m + 15) / 16 * 16;
   p.tiles_n = (p.n + kBM - 1) / kBM;
-  // Split K (in quads of 64-k blocks) into as many parts as one wave of the SMs holds: the longest
-  // part sets the time (431 tokens x 3072 x 2048: 48 tiles x 3 parts of at most 12 blocks).
+  // Split K (in quads of 64-k blocks) into as many parts as one wave of the SMs holds (two CTAs per
+  // SM when they share it): the longest part sets the time (431 tokens x 3072 x 2048: 48 tiles x 3
+  // parts of at most 12 blocks).
   const int nkb = p.k / kBK, quads = nkb / 4;
   const int tiles = p.tiles_m * p.tiles_n;
-  const int splitk = std::max(1, std::min(quads, dev.sms / std::max(tiles, 1)));
+  const int slots = two_per_sm ? 2 * dev.sms : dev.sms;
+  const int splitk = std::max(1, std::min(quads, slots / std::max(tiles, 1)));
   p.kb_split = ((quads + splitk - 1) / splitk) * 4;
   p.splitk = (nkb + p.kb_split - 1) / p.kb_split;
   // Pipeline depth: as many stages as the SM's shared memory (or half of it) holds.
