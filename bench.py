@@ -646,9 +646,15 @@ def run_reference(args):
     from mq import synth
 
     torch.set_num_threads(os.cpu_count())
-    rows = 8192
     job_bytes = sum(q4_bytes(n, k, 1) for _, n, k in synth.LLAMA_LAYER)
-    smp = CpuSample(rows)
+    # Rows per step: 8192 (configs[0]'s matrix), fewer when that many steps would not finish in about
+    # 90 s, but at least 2048: smaller samples stay in the host caches and read faster per byte.
+    smp = CpuSample(8192)
+    smp.run()  # the first call pays for imports and page faults
+    per_row = smp.run() / 8192
+    rows = int(min(8192, max(2048, 90.0 / (args.steps + args.warmup) / per_row // 256 * 256)))
+    if rows != 8192:
+        smp = CpuSample(rows)
     for _ in range(args.warmup):
         smp.run()
     med = statistics.median(smp.run() for _ in range(args.steps))
