@@ -12,7 +12,8 @@ total work is fixed as N grows ("scaling": "strong"). value = algorithmic bytes 
 
 --impl reference times the reference's CPU path for the same workload on this host's cores: its
 dequantiser (Weights.int4 of qwen3moe/reference.py:53-65, restated in oracle/q4.py) followed by
-a torch fp32 matmul (qwen3moe/reference.py:135), on a bounded sample of the rows per step.
+a torch fp32 matmul (qwen3moe/reference.py:135), over the whole job every step, its row blocks
+spread over every host thread.
 """
 import argparse
 import json
@@ -177,6 +178,21 @@ def rotating_copies(shard_bytes):
     return max(2, -(-2 * L2_BYTES // shard_bytes))
 
 
+DTYPE = ("int4 weights (fp16 scale per 32) x activations staged as 15-bit fixed point per 32-k group (two int8 "
+         "limbs): exact integer products on the int8 tensor op, fp32 across groups")
+
+
+def workload_config(world):
+    """The workload both arms run (identical in the GPU and the reference line)."""
+    from mq import synth
+
+    return {"workload": "llama-3.2-1b decode layer + lm_head, Q4_0 G=32 GEMV, batch 1",
+            "matrices": {nm: [n, k] for nm, n, k in synth.LLAMA_LAYER}, "batch": 1,
+            "parallelism": f"column-parallel along output rows x{world} GPU(s), no communication; the reference "
+                           "arm splits the same rows over host threads",
+            "l2": "inputs larger than L2: rotating weight copies on the GPU (the reference arm streams host memory)"}
+
+
 def run_mq(args):
     import mq
     from mq import synth
@@ -337,7 +353,9 @@ def run_mq(args):
         gt = graph_of(lambda: [mq.project(tx, tws[i % tc], tss[i % tc], ty, hi - lo, k) for i in range(reps_in_graph)])
         tms = max_over_ranks(time_graphs([gt], 10, stream) / reps_in_graph, world)
         tbytes = n * k // 4 + n * (k // 128) * 2 + 2 * k + 4 * n
-        tern[name] = {"shape": [n, k], "ms": round(tms, 5), "GB/s": round(tbytes / (tms * 1e-3) / 1e9, 1)}
+        gbs = tbytes / (tms * 1e-3) / 1e9  # the whole matrix over the slowest rank's time
+        tern[name] = {"shape": [n, k], "ms": round(tms, 5), "GB/s_all_gpus": round(gbs, 1),
+                      "GB/s_per_gpu": round(gbs / world, 1), "frac_of_measured_hbm_per_gpu": round(gbs / world / peaks()[0], 4)}
         del tws, tss
 
     # ---- secondary: the fused decode epilogues (one launch each) against their unfused forms -------
@@ -393,9 +411,10 @@ def run_mq(args):
         gp = graph_of(lambda: [mq.p_gemm_q4(pw, ps, px, py, hi - lo, k, x.shape[0], group=GROUP) for _ in range(10)])
         pms = max_over_ranks(time_graphs([gp], 10, stream) / 10, world)
         flops = 2.0 * x.shape[0] * n * k
+        tf = flops / (pms * 1e-3) / 1e12  # the whole GEMM over the slowest rank's time
         prefill[name] = {"shape": [n, k], "tokens": x.shape[0], "ms": round(pms, 5),
-                         "TFLOP/s": round(flops / (pms * 1e-3) / 1e12, 1),
-                         "frac_of_measured_bf16_peak": round(flops / (pms * 1e-3) / 1e12 / tflops_peak, 4)}
+                         "TFLOP/s_all_gpus": round(tf, 1), "TFLOP/s_per_gpu": round(tf / world, 1),
+                         "frac_of_measured_bf16_peak_per_gpu": round(tf / world / tflops_peak, 4)}
         del gp
 
     # ---- secondary: ternary prefill GEMM (p_gemm_t2), Qwen3-8B projections, 512 rows, fp16 x -----------
@@ -411,8 +430,10 @@ def run_mq(args):
         gt_ = graph_of(lambda: [mq.p_gemm_t2(tx_, tw_d, ts_d, ty_, hi - lo, k, 512) for _ in range(10)])
         tms = max_over_ranks(time_graphs([gt_], 10, stream) / 10, world)
         flops = 2.0 * 512 * n * k
-        tprefill[name] = {"shape": [n, k], "rows": 512, "ms": round(tms, 5), "TFLOP/s": round(flops / (tms * 1e-3) / 1e12, 1),
-                          "frac_of_measured_bf16_peak": round(flops / (tms * 1e-3) / 1e12 / tflops_peak, 4)}
+        tf = flops / (tms * 1e-3) / 1e12
+        tprefill[name] = {"shape": [n, k], "rows": 512, "ms": round(tms, 5), "TFLOP/s_all_gpus": round(tf, 1),
+                          "TFLOP/s_per_gpu": round(tf / world, 1),
+                          "frac_of_measured_bf16_peak_per_gpu": round(tf / world / tflops_peak, 4)}
         del gt_
 
     # ---- secondary: the decode layer at batch 64 through the tensor-core path
@@ -428,7 +449,8 @@ def run_mq(args):
                                                 for m_, (xb, yb) in zip(mats, b64_bufs)]))
     b64_ms = max_over_ranks(time_graphs(b64_graphs, 50, stream), world)
     b64_bytes = sum(q4_bytes(n, k, 64) for _, n, k in synth.LLAMA_LAYER)
-    decode64 = {"ms_per_step": round(b64_ms, 5), "GB/s": round(b64_bytes / (b64_ms * 1e-3) / 1e9, 1),
+    b64_gbs = b64_bytes / (b64_ms * 1e-3) / 1e9
+    decode64 = {"ms_per_step": round(b64_ms, 5), "GB/s_all_gpus": round(b64_gbs, 1), "GB/s_per_gpu": round(b64_gbs / world, 1),
                 "x": "fp16 [64, k] per matrix", "path": "tcgen05 GEMM (batch > 4)"}
     del b64_graphs
 
@@ -447,19 +469,18 @@ def run_mq(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(budget_s=args.cpu_seconds)
+    config = workload_config(world)
 
     clocks = clk.summary()
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int4 weights (fp16 scales) x fp32 activations, fp32 accumulate",
+            "vs_baseline": None, "dtype": DTYPE,
             "data": "synthetic (seeded; BASELINE configs[1] distributions)",
-            "config": {"workload": "llama-3.2-1b decode layer + lm_head, Q4_0 G=32 GEMV, batch 1",
-                       "matrices": {nm: [n, k] for nm, n, k in synth.LLAMA_LAYER}, "batch": batch,
-                       "parallelism": f"column-parallel (rows) x{world}, no communication",
-                       "step": "the 5 GEMVs of a decode step, recorded once as a CUDA graph and replayed",
-                       "l2": f"inputs larger than L2: {copies} rotating weight copies per rank"},
+            "config": config,
+            "timing": {"step": "the 5 GEMVs of a decode step, recorded once as a CUDA graph and replayed",
+                       "weight_copies_per_rank": copies, "clock": "CUDA events, max over ranks"},
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "note": "the step's five mq.gemv_q4 API calls recorded once per (activation buffer, weight "
                             "copy) as a CUDA graph and replayed per step; every step the step's x vectors from "
@@ -581,49 +602,75 @@ def moe_bench_ep(mq, synth, dev, stream, world, rank, steps=30):
     return out
 
 
-class CpuSample:
-    """The reference's CPU path on a row sample of the workload: dequantise the int4 words as
-    Weights.int4 does (oracle/q4.py restates qwen3moe/reference.py:53-65, numpy), then a torch
-    fp32 matmul (qwen3moe/reference.py:135). The sample's inputs are drawn once."""
+class CpuJob:
+    """The reference's CPU path for the decode step: each matrix dequantised as Weights.int4 does
+    (oracle/q4.py restates qwen3moe/reference.py:53-65 in numpy) and multiplied by x with torch in
+    fp32 (qwen3moe/reference.py:135). Row blocks of every matrix are spread over `threads` host
+    threads (numpy and torch release the interpreter lock in their loops); `rows` limits every matrix
+    to its first rows (a sample), None runs the whole job."""
 
-    def __init__(self, rows):
+    BLOCK = 4096  # rows per task at k = 2048 (fewer for longer rows)
+
+    def __init__(self, threads, rows=None):
+        from concurrent.futures import ThreadPoolExecutor
+
         from mq import synth
 
-        rng = np.random.default_rng(0)
-        self.x = torch.from_numpy(rng.standard_normal((1, 2048)).astype(np.float32))
-        self.wq, self.ws = synth.q4_matrix(rng, rows, 2048, GROUP)
-        self.bytes = q4_bytes(rows, 2048, 1)
-        self.rows = rows
+        layer = synth.llama_layer(batch=1, seed=0, rows=rows)
+        self.mats = [(layer[nm][0], layer[nm][1], layer[nm][2]) for nm, _, _ in synth.LLAMA_LAYER]
+        self.xs = [torch.from_numpy(x) for x, _, _ in self.mats]
+        self.bytes = sum(q4_bytes(wq.shape[0], wq.shape[1] * 8, 1) for _, wq, _ in self.mats)
+        self.rows = sum(wq.shape[0] for _, wq, _ in self.mats)
+        self.threads = threads
+        self.pool = ThreadPoolExecutor(max_workers=threads)
 
-    def run(self, parts=None):
-        """Returns the seconds one dequantise + matmul of the sample takes (and, into `parts`, the
-        dequantise and the matmul apart)."""
+    def _block(self, i, r0, r1, parts):
         from oracle import q4
 
+        _, wq, ws = self.mats[i]
         t0 = time.perf_counter()
-        w = torch.from_numpy(q4.dequant(self.wq, self.ws, GROUP))
+        w = torch.from_numpy(q4.dequant(wq[r0:r1], ws[r0:r1], GROUP))
         t1 = time.perf_counter()
-        y = self.x @ w.T
+        y = self.xs[i] @ w.T
         t2 = time.perf_counter()
-        assert torch.isfinite(y).all()
-        if parts is not None:
-            parts.append((t1 - t0, t2 - t1))
-        return t2 - t0
+        parts.append((t1 - t0, t2 - t1))
+        return y
+
+    def run(self, parts=None):
+        """Seconds for one pass over the job (per-block dequantise and matmul thread-seconds into `parts`)."""
+        parts = [] if parts is None else parts
+        t0 = time.perf_counter()
+        futs = []
+        for i, (_, wq, _) in enumerate(self.mats):
+            block = self.BLOCK * 2048 // (wq.shape[1] * 8)  # about 8 M weights per task
+            futs += [self.pool.submit(self._block, i, r0, min(r0 + block, wq.shape[0]), parts)
+                     for r0 in range(0, wq.shape[0], block)]
+        ys = [f.result() for f in futs]
+        dt = time.perf_counter() - t0
+        assert all(bool(torch.isfinite(y).all()) for y in ys)
+        return dt
+
+
+def cpu_threads():
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
 
 
 def cpu_baseline(budget_s=10.0):
-    torch.set_num_threads(os.cpu_count())
-    smp = CpuSample(8192)
-    dt = smp.run()  # warm-up and sizing
-    reps = min(50, max(5, int(budget_s / max(dt, 1e-3))))
+    """The reference's CPU path on the GPU box's host cores, the whole job per pass."""
+    threads = cpu_threads()
+    torch.set_num_threads(1)  # the parallelism is over row blocks
+    job = CpuJob(threads)
+    dt = job.run()  # warm-up and sizing
+    reps = min(20, max(3, int(budget_s / max(dt, 1e-3))))
     parts = []
-    med = statistics.median(smp.run(parts) for _ in range(reps))
-    return {"value": round(smp.bytes / med / 1e9, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
-            "dequantise_ms": round(1e3 * statistics.median(p[0] for p in parts), 3),
-            "matmul_ms": round(1e3 * statistics.median(p[1] for p in parts), 3),
-            "total_ms": round(1e3 * med, 3),
-            "sample": f"{smp.rows}x2048 Q4_0 rows (G=32) of the workload: numpy dequantise (single-threaded, as "
-                      f"the reference's) + torch fp32 matmul ({torch.get_num_threads()} threads), median of {reps}",
+    times = [job.run(parts) for _ in range(reps)]
+    med = statistics.median(times)
+    return {"value": round(job.bytes / med / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "ms_per_step": round(1e3 * med, 3),
+            "dequantise_thread_s": round(sum(p[0] for p in parts) / reps, 3),
+            "matmul_thread_s": round(sum(p[1] for p in parts) / reps, 3),
+            "sample": f"the whole step ({job.rows} rows of the five matrices) per pass, median of {reps}: numpy "
+                      f"dequantise + torch fp32 matmul per block of about 8 M weights, blocks over {threads} threads",
             "cpu": platform_cpu()}
 
 
@@ -643,31 +690,33 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from mq import synth
-
-    torch.set_num_threads(os.cpu_count())
-    job_bytes = sum(q4_bytes(n, k, 1) for _, n, k in synth.LLAMA_LAYER)
-    # Rows per step: 8192 (configs[0]'s matrix), fewer when that many steps would not finish in about
-    # 90 s, but at least 2048: smaller samples stay in the host caches and read faster per byte.
-    smp = CpuSample(8192)
-    smp.run()  # the first call pays for imports and page faults
-    per_row = smp.run() / 8192
-    rows = int(min(8192, max(2048, 90.0 / (args.steps + args.warmup) / per_row // 256 * 256)))
-    if rows != 8192:
-        smp = CpuSample(rows)
+    threads = cpu_threads()
+    torch.set_num_threads(1)  # the parallelism is over row blocks
+    job = CpuJob(threads)
+    # Every step is the whole job while warmup + steps of it fit in about three minutes; past that each
+    # step runs the same leading rows of every matrix, and the line says so.
+    per_step = job.run()
+    rows = None
+    if per_step * (args.steps + args.warmup) > 180.0:
+        frac = 180.0 / (per_step * (args.steps + args.warmup))
+        rows = max(CpuJob.BLOCK, int(128256 * frac) // CpuJob.BLOCK * CpuJob.BLOCK)
+        job = CpuJob(threads, rows=rows)
     for _ in range(args.warmup):
-        smp.run()
-    med = statistics.median(smp.run() for _ in range(args.steps))
-    value = smp.bytes / med / 1e9
+        job.run()
+    times = [job.run() for _ in range(args.steps)]
+    med = statistics.median(times)
+    value = job.bytes / med / 1e9
+    sample = (f"the whole step per step ({job.rows} rows of the five matrices)" if rows is None else
+              f"the first {rows} rows of every matrix per step ({job.rows} rows)") + \
+        f": numpy dequantise + torch fp32 matmul per block of about 8 M weights, blocks over {threads} threads"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(job_bytes / (value * 1e9) * 1e3, 3),
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * med, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "int4 weights dequantised to fp32, fp32 matmul", "data": "synthetic (seeded)",
-        "config": {"workload": "llama-3.2-1b decode layer + lm_head, Q4_0 G=32 GEMV, batch 1",
-                   "sample_per_step": f"{rows}x2048 rows; ms_per_step extrapolates to the whole job"},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"{rows}x2048 Q4_0 rows per step (reference dequantiser restated + torch fp32 matmul)",
+        "dtype": "int4 weights dequantised to fp32, fp32 matmul", "data": "synthetic (seeded; BASELINE configs[1] distributions)",
+        "config": workload_config(world),
+        "timing": {"clock": "host perf_counter per step, median", "sample": sample},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample,
                          "cpu": platform_cpu()},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

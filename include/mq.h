@@ -85,7 +85,10 @@ MQ_API int mq_unpack_q4(const uint32_t *wq, const uint16_t *ws, int8_t *q, uint1
  * group in {32, 64, 128}; k % 32 == 0 and k % group == 0; add != 0 adds into y (gemv_add_q4).
  * 1 <= batch <= 64: batch <= 4 runs the streaming GEMV; batch > 4 runs the tensor-core GEMM
  * (mq_gemm_q4), which needs fp16 x here (fp32 x needs mq_gemm_q4's workspace) and k % 256 == 0.
- * wq and x 16-byte aligned (ws too for batch > 4), y 4-byte aligned.
+ * wq and x 16-byte aligned (ws too for batch > 4), y 4-byte aligned. The streaming GEMV stages x
+ * as 15-bit fixed point per 32-k group (two int8 limbs, step 1/65024 of the group's largest |x|) and
+ * multiplies exactly in integers; a NaN or an infinity in x makes the outputs of that token NaN,
+ * where the reference's fp32 sums are Inf or NaN.
  */
 MQ_API int mq_gemv_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y,
                int64_t n, int64_t k, int group, int batch, int add, void *stream);
@@ -108,7 +111,9 @@ MQ_API int mq_gate_up_q4(const uint32_t *wq, const uint16_t *ws, const void *x, 
  * n % 128 restrictions. x: [m][k] fp16 (MQ_F16) or fp32 (MQ_F32, converted to fp16 in `workspace`,
  * mq_gemm_q4_workspace_size() bytes); y: [m][n] fp32. group in {32, 64, 128}; k % 256 == 0.
  * The product uses fp16 x and fp16 q*scale with fp32 accumulation. wq, ws, x and workspace 16-byte
- * aligned, y 4-byte aligned. When K is split across CTAs (small n * m) y is zeroed first unless add.
+ * aligned, y 4-byte aligned. When K is split across CTAs (small n * m) y is zeroed first unless add,
+ * and the parts are added into y in an order that varies from run to run: y is then not bitwise
+ * reproducible (it differs in the last bits of fp32 between runs).
  */
 MQ_API size_t mq_gemm_q4_workspace_size(int64_t m, int64_t k, int x_dtype);
 MQ_API int mq_gemm_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y, int64_t n,
@@ -118,12 +123,12 @@ MQ_API int mq_gemm_q4(const uint32_t *wq, const uint16_t *ws, const void *x, int
  * mq_gemm_q4 for fp32 x without a caller workspace. This entry point has no counterpart in the
  * reference. Its fp16 copy of x lives in a fixed 4 MiB buffer inside libmq's own device memory
  * (m * k <= 2097152 activations; larger calls return MQ_EINVAL), so it allocates nothing: for callers
- * that cannot allocate device memory, such as a binding that passes only the reference's p_gemm_q4
- * arguments or a host whose own allocator owns the device. The first call on each device looks the
- * buffer's address up (cudaGetSymbolAddress) with that device current; make that first call before
- * any stream capture. Every call on a device shares the one buffer: calls that overlap in time (on
- * two streams or two host threads) race and must be serialised by the caller. Other arguments,
- * limits and numerics as mq_gemm_q4.
+ * that cannot allocate device memory, such as a binding that can pass only (wq, ws, x, y, n, k) and no
+ * scratch buffer, or a host whose own allocator owns the device. The first call in each CUDA context
+ * (normally one per device) looks the buffer's address up (cudaGetSymbolAddress) with that context
+ * current; make that first call before any stream capture. Every call in a context shares the one
+ * buffer: calls that overlap in time (on two streams or two host threads) race and must be
+ * serialised by the caller. Other arguments, limits and numerics as mq_gemm_q4.
  */
 MQ_API int mq_gemm_q4_noalloc(const uint32_t *wq, const uint16_t *ws, const float *x, float *y, int64_t n, int64_t k,
                               int64_t m, int group, int add, void *stream);
@@ -134,7 +139,10 @@ MQ_API int mq_gemm_q4_noalloc(const uint32_t *wq, const uint16_t *ws, const floa
  * (bonsai/kernels/kernels.mojo:283-325,437-448,451-489) as called by qwen3/model.mojo:128-135,170-181.
  * w: [k/16][n] u32, s: [k/128][n] f16, x: [batch][k] fp16 (the reference's fp16 pairs,
  * qwen3/kernels/qwen3k.mojo:17-20, are the same bytes), y: [batch][n] fp32.
- * k % 128 == 0; n % 4 == 0; w, s 16- and 8-byte aligned.
+ * k % 128 == 0; any n >= 1 (n % 4 == 0 streams w with TMA; other widths, such as the reference's
+ * second head half of 75893 outputs, with 4-byte copies); w and x 16-byte aligned, s 2-byte, y 4-byte.
+ * A NaN or an infinity in x makes every output of that token NaN (the reference's fp32 sums are then
+ * Inf or NaN: the same outputs are not finite).
  */
 MQ_API int mq_tgemv(const uint16_t *x, const uint32_t *w, const uint16_t *s, float *y, int64_t n, int64_t k,
              int batch, void *stream);

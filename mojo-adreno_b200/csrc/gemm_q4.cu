@@ -715,30 +715,50 @@ int gemm_q4_run(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dty
 }
 
 // mq_gemm_q4_noalloc keeps its fp16 copy of the fp32 activations in this module's own device memory,
-// for callers that have no device allocator to hand: a binding that passes exactly the reference's
-// p_gemm_q4 arguments (wq, ws, x, y, n, k: no scratch buffer), or a host whose memory manager owns
-// every device allocation. One copy per device, shared by every call on that device.
+// for callers that have no device allocator to hand: a binding that can pass only (wq, ws, x, y, n, k)
+// and no scratch buffer, or a host whose memory manager owns every device allocation. One copy per
+// CUDA context (normally one per device), shared by every call in that context.
 constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // m * k * 2 bytes at most
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of this device's copy of g_noalloc_scratch, looked up once per device (with that
-// device current) and cached.
+// Device address of the current context's copy of g_noalloc_scratch, looked up once per context
+// (a caller that makes its own, non-primary context current gets that context's copy) and cached.
 int noalloc_scratch(void **out) {
+  typedef CUresult (*CtxGetCurrentFn)(CUcontext *);
   static std::mutex mu;
+  static CtxGetCurrentFn ctx_fn = nullptr;
+  static CUcontext keys[64] = {};
   static void *cache[64] = {};
   int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  cudaError_t e = cudaGetDevice(&dev);  // also makes the device's primary context current if none is
   if (e != cudaSuccess) return fail(MQ_ECUDA, "mq_gemm_q4_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= 64) return fail(MQ_EUNSUPPORTED, "mq_gemm_q4_noalloc: device index %d out of range", dev);
   std::lock_guard<std::mutex> lock(mu);
-  if (!cache[dev]) {
+  if (!ctx_fn) {
+    void *fp = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fp, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fp)
+      return fail(MQ_ECUDA, "mq_gemm_q4_noalloc: cuCtxGetCurrent is not available from the driver");
+    ctx_fn = reinterpret_cast<CtxGetCurrentFn>(fp);
+  }
+  CUcontext ctx = nullptr;
+  if (ctx_fn(&ctx) != CUDA_SUCCESS || !ctx) {
+    e = cudaFree(nullptr);  // no context current yet: let the runtime make the primary one current
+    if (e != cudaSuccess || ctx_fn(&ctx) != CUDA_SUCCESS || !ctx)
+      return fail(MQ_ECUDA, "mq_gemm_q4_noalloc: no current CUDA context");
+  }
+  int slot = 0;
+  while (slot < 64 && keys[slot] && keys[slot] != ctx) ++slot;
+  if (slot == 64) return fail(MQ_EUNSUPPORTED, "mq_gemm_q4_noalloc: more than 64 CUDA contexts");
+  if (!keys[slot]) {
     void *p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p)
       return fail(MQ_ECUDA, "mq_gemm_q4_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    cache[dev] = p;
+    cache[slot] = p;
+    keys[slot] = ctx;
   }
-  *out = cache[dev];
+  *out = cache[slot];
   return MQ_OK;
 }
 

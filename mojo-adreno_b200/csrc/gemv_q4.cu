@@ -29,6 +29,10 @@
 //    phase on 8 different chunks.
 //  * Small matrices split K across the warps of a CTA (partials reduced in shared memory), so even
 //    a 2048-row matrix keeps every SM streaming.
+//  * Non-finite x. The fixed-point staging cannot carry Inf or NaN, so a 32-k group of x holding one
+//    gets a NaN scale and every output it touches becomes NaN. In the reference's fp32 arithmetic
+//    such an output is Inf or NaN (an infinite x times a weight is infinite, or NaN for weight 0), so
+//    the same outputs are not finite.
 #include <algorithm>
 
 #include "common.cuh"
@@ -249,13 +253,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int e = 0; e < 8; ++e) xv[e] = 0.f;
     }
     float m = 0.f;
+    int bad = 0;  // a non-finite x in the group: its scale becomes NaN
 #pragma unroll
-    for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(xv[e]));
+    for (int e = 0; e < 8; ++e) {
+      m = fmaxf(m, fabsf(xv[e]));
+      bad |= !isfinite(xv[e]);
+    }
 #pragma unroll
-    for (int o = 1; o < 4; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    for (int o = 1; o < 4; o <<= 1) {
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    }
     if (!live) continue;
-    const float inv = m > 0.f ? kLimbMax / m : 0.f;
-    if (j == 0) xs[(t * kc + c) * 4 + q] = m / kLimbMax * (1.f / 16.f);  // 1/16: weights enter as 16 * value
+    const float inv = m > 0.f && !bad ? kLimbMax / m : 0.f;
+    if (j == 0)  // 1/16: weights enter as 16 * value
+      xs[(t * kc + c) * 4 + q] = bad ? __int_as_float(0x7fc00000) : m / kLimbMax * (1.f / 16.f);
     int hi[8], lo[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {

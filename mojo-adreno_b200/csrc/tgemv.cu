@@ -27,8 +27,19 @@
 //    of candidate block r. Each warp reduces its 32 outputs to (best, index, non-finite) with
 //    shuffles and leaves them in shared memory; the warp that arrives last at the round's counter
 //    combines the 16 and writes the candidate. No warp waits for another.
+//  * Any width n. A TMA tensor map needs a row stride that is a multiple of 16 bytes, so n % 4 == 0
+//    streams the slots with TMA; any other n (the reference's second head half has 151669 - 75776 =
+//    75893 outputs, qwen3/model.mojo:176-181) fills the same swizzled slots with 4-byte cp.async
+//    copies issued by all 32 lanes of the warp (zero-filled past n), completing on the same slot
+//    barrier, so the consumer is unchanged. Outputs past n are never stored and never compete for
+//    the argmax, as the reference's per-output tail (kernels.mojo:477-487) leaves them out.
+//  * Non-finite x. The fixed-point staging cannot carry Inf or NaN, so a 128-k group of x holding one
+//    gets a NaN scale: every output it touches becomes NaN. In the reference's fp32 arithmetic such an
+//    output is Inf or NaN (x * w with x infinite is infinite or, for w = 0, NaN), so the outputs that
+//    are not finite are the same, and the head's non-finite flag fires where the reference's does.
 #include <algorithm>
 #include <climits>
+#include <cstring>
 
 #include "common.cuh"
 
@@ -60,12 +71,25 @@ struct Params {
   float *cand;      // head argmax candidates [batch][ncand][3], or null
   int ncand;        // ceil(n / 512)
   int cand_rounds;  // rounds of one CTA (shared-memory partials per round)
+  int plain;        // 1: the lanes fill the slots with cp.async (n % 4 != 0: no tensor map of w)
+  int y_vec;        // 1: a lane stores its 4 outputs as one float4 (n % 4 == 0, y 16-byte aligned)
+  const uint32_t *w;  // the words, read directly when plain
 };
 
 constexpr int kCandOutputs = 512;   // outputs of a candidate block = one round of 16 warps x 32
 constexpr int kMaxCandRounds = 8;   // rounds per CTA with candidates (n <= 8 * 512 * SMs)
 
 constexpr float kLimbMax = 32512.f;  // 127 * 256: |x| maps to at most this, so both limbs fit in int8
+
+// 4 bytes from global to shared memory, asynchronously; src_bytes = 0 writes zeros and reads nothing.
+__device__ __forceinline__ void cp_async4(void *dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes) : "memory");
+}
+// Arrives on `bar` once this thread's earlier cp.async copies have landed (the barrier's expected
+// count includes this arrival).
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 __device__ __forceinline__ uint32_t pack_bytes(int a, int b, int c, int d) {
   return (static_cast<uint32_t>(a) & 255u) | (static_cast<uint32_t>(b) & 255u) << 8 |
@@ -139,19 +163,33 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   auto issue = [&](uint32_t u) {
     int tile, sk;
-    if (lane != 0 || !items.get(u, tile, sk)) return;
+    if ((lane != 0 && !p.plain) || !items.get(u, tile, sk)) return;
     const int slot = u % S;
     uint64_t *bar = full + slot;
     uint8_t *dst = ring + slot * kSlotBytes;
+    if (p.plain) {  // lane l copies column tile * 32 + l of each word row into its swizzled place
+      const int col = tile * kCols + lane, row0 = sk * kWordRows, nrows = K / 16;
+      const bool in = col < N;
+      const uint32_t *src = p.w + (in ? col : 0);
+      uint8_t *d0 = dst + (lane & 3) * 4;
+#pragma unroll 8
+      for (int wr = 0; wr < kWordRows; ++wr) {
+        const bool live = in && row0 + wr < nrows;
+        cp_async4(d0 + wr * 128 + (((lane >> 2) ^ (wr & 7)) << 4), live ? src + static_cast<size_t>(row0 + wr) * N : p.w,
+                  live ? 4u : 0u);
+      }
+      cp_async_arrive(bar);
+      return;
+    }
     mbar_expect_tx(bar, bytes);
     tma_load_2d(dst, &wmap, bar, tile * kCols, sk * kWordRows);
     if (p.scales_tma) tma_load_2d(dst + kWordBytes, &smap, bar, tile * kCols, sk * kGroups);
   };
   griddep_launch_dependents();
   if (lane == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(full + s, 1);
+    for (int s = 0; s < S; ++s) mbar_init(full + s, p.plain ? 32 : 1);
     fence_mbar_init();
-    prefetch_tmap(&wmap);
+    if (!p.plain) prefetch_tmap(&wmap);
     if (p.scales_tma) prefetch_tmap(&smap);
   }
   __syncwarp();
@@ -195,11 +233,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int e = 0; e < 16; ++e) xv[e] = 0.f;
     }
     float m = 0.f;
+    int bad = 0;  // a non-finite x in the group: its scale becomes NaN
 #pragma unroll
-    for (int e = 0; e < 16; ++e) m = fmaxf(m, fabsf(xv[e]));
+    for (int e = 0; e < 16; ++e) {
+      m = fmaxf(m, fabsf(xv[e]));
+      bad |= !isfinite(xv[e]);
+    }
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float inv = m > 0.f ? kLimbMax / m : 0.f;
+    for (int o = 1; o < 8; o <<= 1) {
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+    const float inv = m > 0.f && !bad ? kLimbMax / m : 0.f;
     int hi[16], lo[16], shi = 0, slo = 0;
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
@@ -217,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!live) continue;
     const int gg = wr / 8;
     if (wr % 8 == 0) {
-      xs[t * kg + gg] = m / kLimbMax;
+      xs[t * kg + gg] = bad ? __int_as_float(0x7fc00000) : m / kLimbMax;
       lsum[(t * kg + gg) * 2] = shi;
       lsum[(t * kg + gg) * 2 + 1] = slo;
     }
@@ -312,8 +357,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int rows = kCols * p.rt;
     if (q < NB) {
       if (p.ks == 1) {  // the warp owns whole outputs: store directly, no barrier
-        if (tile < p.tiles && col < N && !aborted)
-          *reinterpret_cast<float4 *>(p.y + static_cast<size_t>(q) * N + col) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        if (tile < p.tiles && col < N && !aborted) {
+          float *out = p.y + static_cast<size_t>(q) * N + col;
+          if (p.y_vec) {
+            *reinterpret_cast<float4 *>(out) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+          } else {
+#pragma unroll
+            for (int o = 0; o < 4; ++o)
+              if (col + o < N) out[o] = acc[o];
+          }
+        }
       } else {
 #pragma unroll
         for (int o = 0; o < 4; ++o) red[(items.kw * rows + items.rtl * kCols + 4 * cgc + o) * NB + q] = acc[o];
@@ -322,9 +375,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.cand) {  // ks == 1: this round is candidate block r, this warp its outputs 32 * warp ..
       float bv = -INFINITY;
       int bi = INT_MAX, bad = 0;
-      if (q < NB && tile < p.tiles && col < N) {  // n % 4 == 0: all four outputs exist
+      if (q < NB && tile < p.tiles) {
 #pragma unroll
         for (int o = 0; o < 4; ++o) {
+          if (col + o >= N) break;  // only real outputs compete
           bad |= !isfinite(acc[o]);
           if (better(acc[o], col + o, bv, bi)) bv = acc[o], bi = col + o;
         }
@@ -403,9 +457,16 @@ int launch_sk(const uint32_t *w, Params p, cudaStream_t stream, const DeviceInfo
   MQ_REQUIRE(smem <= dev.smem_optin, MQ_EUNSUPPORTED, "mq_tgemv: k=%d batch=%d needs %zu B of shared memory (max %zu)", p.k,
              NB, smem, dev.smem_optin);
   CUtensorMap wmap, smap;
-  if (int rc = encode_tmap_2d(&wmap, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.n, p.k / 16, static_cast<uint64_t>(p.n) * 4,
-                              kCols, Sl::kWordRows, CU_TENSOR_MAP_SWIZZLE_128B, "mq_tgemv words"))
+  p.plain = p.n % 4 != 0;  // the row stride n * 4 bytes is not a multiple of 16: no tensor map
+  p.w = w;
+  if (p.plain) {
+    memset(&wmap, 0, sizeof(wmap));  // not read
+  } else if (int rc = encode_tmap_2d(&wmap, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.n, p.k / 16,
+                                     static_cast<uint64_t>(p.n) * 4, kCols, Sl::kWordRows, CU_TENSOR_MAP_SWIZZLE_128B,
+                                     "mq_tgemv words")) {
     return rc;
+  }
+  p.y_vec = p.n % 4 == 0 && aligned(p.y, 16);
   p.scales_tma = p.n % 8 == 0 && aligned(p.s, 16);
   if (p.scales_tma) {
     if (int rc = encode_tmap_2d(&smap, p.s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.n, p.k / 128,
@@ -440,10 +501,9 @@ int tgemv_run(const uint16_t *x, const uint32_t *w, const uint16_t *s, float *y,
   MQ_REQUIRE(n > 0 && k > 0 && n < (1LL << 31) && k <= (1 << 20), MQ_EINVAL, "mq_tgemv: bad shape n=%lld k=%lld",
              static_cast<long long>(n), static_cast<long long>(k));
   MQ_REQUIRE(k % 128 == 0, MQ_EINVAL, "mq_tgemv: k=%lld must be a multiple of 128", static_cast<long long>(k));
-  MQ_REQUIRE(n % 4 == 0, MQ_EINVAL, "mq_tgemv: n=%lld must be a multiple of 4", static_cast<long long>(n));
   MQ_REQUIRE(batch >= 1 && batch <= 4, MQ_EINVAL, "mq_tgemv: batch must be in 1..4 (got %d)", batch);
-  MQ_REQUIRE(mq::aligned(w, 16) && mq::aligned(s, 8) && mq::aligned(x, 16) && mq::aligned(y, 4) && mq::aligned(cand, 4),
-             MQ_EALIGN, "mq_tgemv: w and x must be 16-byte aligned, s 8-byte aligned");
+  MQ_REQUIRE(mq::aligned(w, 16) && mq::aligned(s, 2) && mq::aligned(x, 16) && mq::aligned(y, 4) && mq::aligned(cand, 4),
+             MQ_EALIGN, "mq_tgemv: w and x must be 16-byte aligned, s 2-byte and y 4-byte aligned");
   DeviceInfo dev;
   if (int rc = device_info(&dev)) return rc;
   Params p{};

@@ -15,14 +15,21 @@ def codes(w, n, k):
     return c.reshape(k, n).T.astype(np.int8)
 
 
-def tgemv(x16, w, s, n, k):
+def tgemv(x16, w, s, n, k, cols=4096):
     """Exact y[b, i] = sum_g s[g, i] sum_{k in g} (code - 1) x[b, k] (float64), the value
-    packed_linear + packed_reduce approximate (bonsai/kernels/kernels.mojo:283-325,437-448)."""
-    c = codes(w, n, k).astype(np.float64) - 1.0
-    sc = np.asarray(s, np.float16).astype(np.float64).reshape(k // 128, n)
+    packed_linear + packed_reduce approximate (bonsai/kernels/kernels.mojo:283-325,437-448).
+    Computed `cols` outputs at a time, so that full-size heads fit in host memory."""
+    w = np.asarray(w, np.uint32).reshape(k // 16, n)
+    sc = np.asarray(s, np.float16).reshape(k // 128, n)
     x = np.atleast_2d(np.asarray(x16, np.float16)).astype(np.float64)
-    wd = (c.reshape(n, k // 128, 128) * sc.T[:, :, None]).reshape(n, k)
-    return x @ wd.T
+    y = np.empty((x.shape[0], n), np.float64)
+    for c0 in range(0, n, cols):
+        c1 = min(n, c0 + cols)
+        c = codes(np.ascontiguousarray(w[:, c0:c1]), c1 - c0, k).astype(np.float64) - 1.0
+        scl = sc[:, c0:c1].astype(np.float64)
+        wd = (c.reshape(c1 - c0, k // 128, 128) * scl.T[:, :, None]).reshape(c1 - c0, k)
+        y[:, c0:c1] = x @ wd.T
+    return y
 
 
 CAND_BLOCK = 512  # logits of a candidate: 64 lanes x 8 (bonsai/kernels/kernels.mojo:491-517)

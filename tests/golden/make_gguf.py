@@ -77,8 +77,11 @@ def _plain(v):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("MQ_REFERENCE"),
+                    help="the reference tree (default: $MQ_REFERENCE)")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("give the reference tree with --ref or MQ_REFERENCE")
     path = os.path.join(HERE, "small.gguf")
     write(path)
     sys.path.insert(0, os.path.join(a.ref, "lfm2"))

@@ -61,8 +61,11 @@ def run(cmd):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("MQ_REFERENCE"),
+                    help="the reference tree (default: $MQ_REFERENCE)")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("give the reference tree with --ref or MQ_REFERENCE")
     ref = a.ref
     rng = np.random.default_rng(1234)
     os.environ.setdefault("PYTHONDONTWRITEBYTECODE", "1")

@@ -61,8 +61,10 @@ def test_tgemv_rejects_bad_arguments_before_launch():
     ok = P(1 << 20)
     rc, msg = _status("mq_tgemv", ok, ok, ok, ok, 64, 200, 1, None)
     assert rc == -1 and "128" in msg
-    rc, msg = _status("mq_tgemv", ok, ok, ok, ok, 66, 256, 1, None)
-    assert rc == -1 and "multiple of 4" in msg
+    rc, msg = _status("mq_tgemv", ok, ok, ok, ok, 0, 256, 1, None)
+    assert rc == -1 and "shape" in msg
+    rc, msg = _status("mq_tgemv", P((1 << 20) + 4), ok, ok, ok, 66, 256, 1, None)
+    assert rc == -2 and "aligned" in msg
     rc, msg = _status("mq_tgemv", ok, ok, ok, ok, 64, 256, 5, None)
     assert rc == -1 and "batch" in msg
 

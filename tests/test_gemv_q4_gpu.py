@@ -109,6 +109,36 @@ def test_gemv_wide_dynamic_range_in_a_group(cuda, spread):
     assert normwise(y, q4.gemv(wq, ws, x, 32)) <= TOL
 
 
+@pytest.mark.parametrize("dtype", [np.float32, np.float16])
+@pytest.mark.parametrize("n", [2048, 333])
+def test_gemv_non_finite_x(cuda, dtype, n):
+    """A NaN or an infinity in x makes the outputs non-finite exactly where the reference's fp32 sums
+    are (every row: an infinite x times a weight is infinite, or NaN for weight 0,
+    llama/kernels/gemv_q4.mojo:23-27); the fixed-point staging must not turn them into finite values.
+    A finite token of the same batch is unaffected, and the gate|up fusion propagates them too."""
+    rng = np.random.default_rng(41 + n)
+    k = 1024
+    x = rng.standard_normal((3, k)).astype(dtype)
+    x[0, 100] = np.nan
+    x[1, 1023] = np.inf
+    wq, ws = synth.q4_matrix(rng, n, k, 32)
+    ref = q4.gemv(wq, ws, x.astype(np.float64), 32)
+    assert not np.isfinite(ref[:2]).any()
+    y = run_gemv(cuda, wq, ws, x, 32)
+    np.testing.assert_array_equal(np.isfinite(y), np.isfinite(ref))
+    assert normwise(y[2:], ref[2:]) <= TIGHT_F32
+    y1 = run_gemv(cuda, wq, ws, x[1:2], 32, add_to=np.zeros((1, n), np.float32))
+    assert not np.isfinite(y1).any()
+    if n % 32 == 0:
+        f = n // 2
+        a = torch.full((3, f), 0.0, device=cuda)
+        mq.gate_up_q4(torch.from_numpy(wq.view(np.int32)).to(cuda), torch.from_numpy(ws).to(cuda),
+                      torch.from_numpy(x).to(cuda), a, k, f, group=32)
+        torch.cuda.synchronize()
+        a = a.cpu().numpy()
+        assert not np.isfinite(a[:2]).any() and np.isfinite(a[2]).all()
+
+
 def test_unpack_bit_exact(cuda):
     rng = np.random.default_rng(7)
     wq, ws = synth.q4_matrix(rng, 300, 1024, 64)

@@ -98,6 +98,20 @@ def test_moe_forward_small_pairs_fp16(cuda, tokens, topk):
     assert normwise(y, ref) <= TOL
 
 
+@pytest.mark.parametrize("group", [64, 128])
+@pytest.mark.parametrize("tokens,x16", [(404, False), (1, False), (2, True)])
+def test_moe_forward_groups(cuda, group, tokens, x16):
+    """The layer with G = 64 and G = 128 scales (qwen3moe exports its experts at G = 128,
+    qwen3moe/export.py:38-39,171-175) on each path: 404 tokens through the grouped tensor-core products,
+    one fp32 token through the decode GEMVs, two fp16 tokens (16 pairs) through the small-pair GEMVs."""
+    m = synth.moe_layer(seed=group + tokens, tokens=tokens, group=group)
+    ids, w = omoe.route(m["logits"], 8)
+    x = m["x"].astype(np.float16) if x16 else m["x"]
+    y = run_forward(cuda, x, ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 2048, 768, group)
+    ref = omoe.moe_layer(x.astype(np.float32), ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], group, 768)
+    assert normwise(y, ref) <= TOL
+
+
 @pytest.mark.parametrize("group,x_per_group", [(32, False), (32, True), (64, True), (128, False), (128, True)])
 def test_moe_gemv_matches_oracle(cuda, group, x_per_group):
     """The expert-indirect decode GEMV: rows of the selected experts only, shared or per-expert x."""

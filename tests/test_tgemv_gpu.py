@@ -159,3 +159,60 @@ def test_packed_head_all_negative_tail_stays_in_range(cuda):
     assert (y < 0).all()
     check_candidates(y, cand)
     assert 512 <= cand[0, 1, 1] < n and 0 <= idx[0] < n
+
+
+@pytest.mark.parametrize("n,k,batch", [(75893, 4096, 1), (1003, 1024, 3), (33, 256, 2), (6, 128, 1), (5, 512, 4),
+                                       (1, 128, 1)])
+def test_tgemv_ragged_width(cuda, n, k, batch):
+    """Any width n, as the reference's per-output tail handles it (bonsai/kernels/kernels.mojo:477-487):
+    n % 4 != 0 (a row stride no tensor map can describe) streams with cp.async; 75893 is the second
+    half of the Qwen3 head (qwen3/model.mojo:176-181, qwen3/convert.cpp:16,122-123) at full K."""
+    rng = np.random.default_rng(n + k + batch)
+    x = rng.standard_normal((batch, k)).astype(np.float16)
+    w, s = synth.ternary_matrix(rng, n, k)
+    y = run(cuda, x, w, s, n, k)
+    assert np.isfinite(y).all()
+    assert normwise(y, ternary.tgemv(x, w, s, n, k)) <= TIGHT
+    assert mq.device_status() == 0
+
+
+@pytest.mark.parametrize("n", [151936, 75776, 75893])
+def test_packed_head_full_size(cuda, n):
+    """The head at full size against the oracle: BASELINE configs[4]'s [151936, 4096] and the two halves
+    the reference's converter writes, head0 = 74 * 1024 rows and head1 = 151669 - 74 * 1024 = 75893 rows
+    (qwen3/convert.cpp:16,122-123), with candidates and the device greedy."""
+    rng = np.random.default_rng(n)
+    k = 4096
+    x = rng.standard_normal((1, k)).astype(np.float16)
+    w, s = synth.ternary_matrix(rng, n, k)
+    y, cand, idx = run_head(cuda, x, w, s, n, k)
+    ref = ternary.tgemv(x, w, s, n, k)
+    assert normwise(y, ref) <= TIGHT
+    check_candidates(y, cand)
+    np.testing.assert_array_equal(idx, ternary.greedy(cand))
+    np.testing.assert_array_equal(idx, y.argmax(axis=1))
+    top2 = np.sort(ref[0])[-2:]
+    if top2[1] - top2[0] > 4 * TIGHT * np.abs(ref[0]).max():
+        assert idx[0] == ref[0].argmax()
+
+
+@pytest.mark.parametrize("n", [4096, 1003])
+def test_tgemv_non_finite_x(cuda, n):
+    """A NaN or an infinity in x makes the outputs non-finite where the reference's fp32 sums are
+    (every output: x * w is infinite, or NaN for w = 0), and the greedy index -1 (bonsai/bonsai_vk.c:506-515
+    stops on non-finite logits); a finite token in the same batch is unaffected."""
+    rng = np.random.default_rng(31 + n)
+    k = 1024
+    x = rng.standard_normal((3, k)).astype(np.float16)
+    x[0, 517] = np.float16(np.nan)
+    x[1, 3] = np.float16(-np.inf)
+    w, s = synth.ternary_matrix(rng, n, k)
+    ref = ternary.tgemv(x, w, s, n, k)
+    assert not np.isfinite(ref[:2]).any()
+    y = run(cuda, x, w, s, n, k)
+    np.testing.assert_array_equal(np.isfinite(y), np.isfinite(ref))
+    assert normwise(y[2:], ref[2:]) <= TIGHT
+    yh, cand, idx = run_head(cuda, x, w, s, n, k)
+    np.testing.assert_array_equal(np.isfinite(yh), np.isfinite(ref))
+    assert (cand[:2, :, 2] == 1).all() and (cand[2, :, 2] == 0).all()
+    np.testing.assert_array_equal(idx, [-1, -1, ternary.greedy(cand[2:])[0]])
