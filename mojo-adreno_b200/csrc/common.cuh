@@ -60,9 +60,10 @@ int gemv_q4_grouped(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const
 }  // namespace gemv
 
 // The grouped expert GEMM (gemm_q4.cu): mode 1 gate|up + SiLU (fp16 out), mode 2 plain (fp32 out).
+// perm: xs rows (and mode 1's output rows) in the k order 0, 4, 1, 5, 2, 6, 3, 7 within each 8.
 int moe_gemm_run(int mode, const uint32_t *wq, const uint16_t *ws, const uint16_t *xs, int64_t pairs, int64_t k,
                  int experts, int64_t rows_per_expert, int group, const int32_t *tiles, const int32_t *ntiles,
-                 int max_tiles, int tile_m, void *out, cudaStream_t stream);
+                 int max_tiles, int tile_m, void *out, cudaStream_t stream, int perm);
 
 // The tcgen05 GEMM (gemm_q4.cu), shared by mq_gemm_q4 and the batched path of mq_gemv_q4.
 int gemm_q4_run(const uint32_t *wq, const uint16_t *ws, const void *x, int x_dtype, float *y, int64_t n, int64_t k,
@@ -306,6 +307,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// 32 consecutive 32-bit columns of TMEM lane (warp quarter * 32 + lane) from registers; warp-collective.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
 

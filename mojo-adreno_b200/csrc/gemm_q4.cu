@@ -10,17 +10,23 @@
 //  * The MMA sees W as the A operand (M = 128 weight rows per CTA) and the tokens as B (N = BN, a
 //    multiple of 16 up to 256), so the accumulator tile in TMEM is [128 weight rows][BN tokens]
 //    and the epilogue writes Y rows with consecutive threads on consecutive addresses.
-//  * Warp 0 streams each 64-k stage with TMA: the packed weights (128 rows x 32 bytes) and the X
-//    tile (BN rows x 128 bytes, 128-byte swizzle, zero-filled past M).
-//  * Warps 2-9 (two threads per weight row, 32 k each) dequantise the stage in registers -- byte permute,
+//  * Warp 0 streams each 128-k stage with ONE multi-lane TMA instruction: the packed weights
+//    (128 rows x 64 bytes) and the X tile as two 64-k sub-tiles (BN rows x 128 bytes each, 128-byte
+//    swizzle, zero-filled past M).
+//  * Warps 2-9 (two threads per weight row, 64 k each) dequantise the stage in registers -- byte permute,
 //    mask into an fp16 mantissa (1024 + u), one fp16x2 FMA to q = u - 8 (exact), one fp16x2
 //    multiply by the group scale (a single rounding) -- and store the fp16 A tile into TMEM with
 //    tcgen05.st (a TMEM ring of A slots next to the accumulator; each warp writes its own lane
-//    quarter). Shared memory then carries only the W/X ring. The one-matrix modes take two stages
-//    per pass, so one store wait covers both.
+//    quarter). Shared memory then carries only the W/X ring. For the MoE products the activations
+//    arrive in a permuted k order that needs no byte permute (dequant_word_perm).
 //  * Warp 1 owns the TMEM allocation and one of its threads issues tcgen05.mma kind::f16 with A read
-//    from TMEM (fp16 x fp16 -> fp32, M = 128, N = BN, K = 16, four per stage), committing each stage
+//    from TMEM (fp16 x fp16 -> fp32, M = 128, N = BN, K = 16, eight per stage), committing each stage
 //    back to the producer (and the A slot back to the dequant warps) and the final one to the epilogue.
+//  * Why 128 k per stage: the single issuing thread's per-stage work (a barrier wait, the MMAs, two
+//    commits) set the pace of every mode. Timed alone, neither the dequantisation, the TMEM stores,
+//    the MMAs themselves, the activation rows, the ring depth nor an L2 warm-up of the weights moved a
+//    64-k-stage kernel; halving the stages per k did (431 x 8192 x 2048: 19.5 -> 16.8 us; MoE
+//    gate|up at 404 tokens: 126 -> 107 us; batch-64 lm_head: 79 -> 62 us).
 //  * Warps 2-9 then move the accumulator out of TMEM (tcgen05.ld 32x32b, one weight row per
 //    thread, the two warps of a TMEM lane quarter taking alternate 32-column chunks), stage the fp32
 //    tile in the freed ring and write it with one TMA store (a reduce-add with `add` or split K).
@@ -38,12 +44,12 @@ namespace mq {
 namespace gemm {
 
 constexpr int kBM = 128;  // weight rows per CTA tile (the UMMA M)
-constexpr int kBK = 64;   // k per pipeline stage: one 128-byte fp16 row
+constexpr int kBK = 128;  // k per pipeline stage: two 128-byte fp16 rows of X (two swizzled sub-tiles)
 constexpr int kMaxStages = 8;  // W/X ring slots in shared memory
-constexpr int kACols = kBK / 2;  // TMEM columns of one dequantised A stage: 64 fp16 per row, as pairs
+constexpr int kACols = kBK / 2;  // TMEM columns of one dequantised A stage: 128 fp16 per row, as pairs
 constexpr int kDeqWarps = 8;   // two per scheduler: one dequant warp alone cannot hide its latencies
 constexpr int kThreads = 32 * (2 + kDeqWarps);  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 dequant + epilogue
-constexpr int kWTileBytes = kBM * 32;
+constexpr int kWTileBytes = kBM * kBK / 2;  // int4 W per stage: 128 rows x 64 bytes
 
 // MODE 0: dense Y = X W^T. MODE 1 (MoE gate|up): per expert e, rows e * 2fe + [0, fe) are gate and
 // + [fe, 2fe) up; a CTA takes 64 gate rows and the 64 matching up rows and writes
@@ -54,7 +60,7 @@ constexpr int kWTileBytes = kBM * 32;
 // (k / 16) * n + col holds codes k .. k + 15 of output col, weight (code - 1) * s[k / 128][col]):
 // p_gemm_t2 (bonsai/kernels/prefill.mojo:155-164).
 enum { kDense = 0, kGateUp = 1, kGrouped = 2, kTernary = 3 };
-constexpr int kTWTileBytes = 4 * kBM * 4;  // ternary W per stage: 4 word rows x 128 outputs
+constexpr int kTWTileBytes = kBK / 16 * kBM * 4;  // ternary W per stage: 8 word rows x 128 outputs
 
 struct Params {
   const __half *ws;
@@ -70,7 +76,7 @@ struct Params {
   int astages;   // dequantised A ring slots in TMEM (<= stages)
   int add;       // y += instead of y =
   int splitk;    // CTAs along K (red.add into y)
-  int kb_split;  // 64-k blocks per split (a multiple of 4)
+  int kb_split;  // 128-k blocks per split (a multiple of 2)
   int tiles_n, tiles_m;
   uint32_t tmem_cols;  // TMEM allocation: the fp32 accumulator, then the A ring
   uint32_t tmem_a;     // first TMEM column of the A ring
@@ -87,7 +93,7 @@ struct Layout {
 __host__ __device__ inline Layout layout(int bn, int stages) {
   Layout L;
   L.x = 0;
-  L.w = L.x + stages * bn * 128;
+  L.w = L.x + stages * bn * kBK * 2;
   L.bars = L.w + stages * kWTileBytes;
   L.tmem_slot = L.bars + (4 * kMaxStages + 1) * 8;
   L.total = L.tmem_slot + 16;
@@ -133,7 +139,41 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, __half2 s2) {
   return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
-template <int G, int MODE>
+// fp16 (q - 8) * s for the 8 nibbles of a word as 4 half2 (16 bytes) in the k order
+// 0, 4, 1, 5, 2, 6, 3, 7: nibbles j and j + 4 sit 16 bits apart, so one LOP3 masks both into fp16
+// mantissas and flips the stored two's complement to the offset value u = q + 8 (1024 + u, or
+// 1024 + 16u for the upper nibble of a byte), one fp16x2 FMA removes the offset exactly, one
+// multiply applies the scale (the only rounding, as in dequant_word). No byte permute: 5 integer
+// operations per word instead of 8. The activations must be stored in the same k order.
+__device__ __forceinline__ uint4 dequant_word_perm(uint32_t w, __half2 s2) {
+  constexpr uint32_t kOne = 0x3C003C00u;    // fp16x2 (1, 1)
+  constexpr uint32_t kOff0 = 0xE408E408u;   // fp16x2 (-1032, -1032)
+  constexpr uint32_t k16th = 0x2C002C00u;   // fp16x2 (1/16, 1/16)
+  constexpr uint32_t kOff1 = 0xD480D480u;   // fp16x2 (-72, -72)
+  const __half2 one = *reinterpret_cast<const __half2 *>(&kOne), off0 = *reinterpret_cast<const __half2 *>(&kOff0);
+  const __half2 sixteenth = *reinterpret_cast<const __half2 *>(&k16th), off1 = *reinterpret_cast<const __half2 *>(&kOff1);
+  const uint32_t t = w >> 8;
+  const uint32_t h0 = (w & 0x000F000Fu) ^ 0x64086408u;  // (1024 + u0, 1024 + u4)
+  const uint32_t h1 = (w & 0x00F000F0u) ^ 0x64806480u;  // (1024 + 16 u1, 1024 + 16 u5)
+  const uint32_t h2 = (t & 0x000F000Fu) ^ 0x64086408u;  // (1024 + u2, 1024 + u6)
+  const uint32_t h3 = (t & 0x00F000F0u) ^ 0x64806480u;  // (1024 + 16 u3, 1024 + 16 u7)
+  uint32_t out[4];
+  __half2 f;
+  f = __hmul2(__hfma2(*reinterpret_cast<const __half2 *>(&h0), one, off0), s2);
+  out[0] = *reinterpret_cast<uint32_t *>(&f);
+  f = __hmul2(__hfma2(*reinterpret_cast<const __half2 *>(&h1), sixteenth, off1), s2);
+  out[1] = *reinterpret_cast<uint32_t *>(&f);
+  f = __hmul2(__hfma2(*reinterpret_cast<const __half2 *>(&h2), one, off0), s2);
+  out[2] = *reinterpret_cast<uint32_t *>(&f);
+  f = __hmul2(__hfma2(*reinterpret_cast<const __half2 *>(&h3), sixteenth, off1), s2);
+  out[3] = *reinterpret_cast<uint32_t *>(&f);
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// Position of column j of a row stored in dequant_word_perm's k order (within each 8: 0, 4, 1, 5, 2, 6, 3, 7).
+__host__ __device__ __forceinline__ int perm_col(int j) { return (j & ~7) | ((j & 3) << 1) | ((j >> 2) & 1); }
+
+template <int G, int MODE, bool PERM = false>
 __global__ void __launch_bounds__(kThreads, 2)
     gemm_q4_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                    const __grid_constant__ CUtensorMap ymap, const Params p) {
@@ -171,8 +211,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   const int nkb_total = p.k / kBK;
   const int kb0 = split * p.kb_split, nk = min(p.kb_split, nkb_total - kb0);
-  // Stage i works on k-block kb0 + (i + rot) % nk; rot is a whole number of 4-block quads.
-  const int rot = 4 * (tn % max(1, nk / 4));
+  // Stage i works on k-block kb0 + (i + rot) % nk; rot is a whole number of 2-block pairs.
+  const int rot = 2 * (tn % max(1, nk / 2));
   auto kblock = [&](int i) { return kb0 + (i + rot) % nk; };
 
   if (threadIdx.x == 0) {
@@ -198,14 +238,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     // A TMA instruction holds its warp for ~0.2 us on B200 whatever it copies, so the copies of a
     // stage (W, or gate and up halves of W, and X) go out as ONE instruction executed by lanes 0..2,
     // each lane with its own map, destination and coordinates.
-    const int nload = MODE == kGateUp ? 3 : 2;
-    const CUtensorMap *lmap = lane == nload - 1 ? &xmap : &wmap;
+    const int nload = MODE == kGateUp ? 4 : 3;  // W lanes (1 or 2), then the two X sub-tile lanes
+    const int nwl = nload - 2;
+    const CUtensorMap *lmap = lane >= nwl ? &xmap : &wmap;
     if (lane == 0) {
       prefetch_tmap(&wmap);
       prefetch_tmap(&xmap);
     }
     __syncwarp();
-    const uint32_t bytes = (MODE == kTernary ? kTWTileBytes : kWTileBytes) + p.bn * 128;
+    const uint32_t bytes = (MODE == kTernary ? kTWTileBytes : kWTileBytes) + p.bn * kBK * 2;
     // The loops of all three roles keep their ring slot, phase and k block as running counters: a
     // single issuing thread retires only a few instructions per stage's worth of MMA time, so no
     // division or descriptor rebuild may sit in its path.
@@ -224,9 +265,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (lane < nload) {
         uint8_t *dst;
         int cx, cy;
-        if (lane == nload - 1) {  // X: bn token rows x 64 k
-          dst = smem + L.x + s * p.bn * 128;
-          cx = kb * kBK;
+        if (lane >= nwl) {  // X: bn token rows x 64 k, two sub-tiles per stage
+          dst = smem + L.x + s * p.bn * kBK * 2 + (lane - nwl) * p.bn * 128;
+          cx = kb * kBK + (lane - nwl) * 64;
           cy = m0;
         } else if (MODE == kTernary) {  // W: 4 word rows (64 k) x 128 outputs
           dst = smem + L.w + s * kWTileBytes;
@@ -257,7 +298,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       // field holds any shared-memory address of this CTA without carrying into bit 14).
       const uint64_t db0 = umma_desc_sw128(smem_u32(smem + L.x));
       const uint32_t da0 = tmem_d + p.tmem_a;  // A slot 0 in TMEM; a slot further is kACols columns on
-      const uint32_t x_step = (p.bn * 128) >> 4;
+      const uint32_t x_step = (p.bn * kBK * 2) >> 4;
+      const uint32_t xsub = (p.bn * 128) >> 4;  // the second 64-k sub-tile of a stage
       uint32_t da = da0;
       uint64_t db = db0;
       uint32_t ph = 0;
@@ -276,6 +318,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         umma_f16_ts(tmem_d, da + 8, db + 2, idesc, 1);
         umma_f16_ts(tmem_d, da + 16, db + 4, idesc, 1);
         umma_f16_ts(tmem_d, da + 24, db + 6, idesc, 1);
+        umma_f16_ts(tmem_d, da + 32, db + xsub, idesc, 1);
+        umma_f16_ts(tmem_d, da + 40, db + xsub + 2, idesc, 1);
+        umma_f16_ts(tmem_d, da + 48, db + xsub + 4, idesc, 1);
+        umma_f16_ts(tmem_d, da + 56, db + xsub + 6, idesc, 1);
         umma_commit(&empty[s]);
         if (split_rings) umma_commit(&aempty[as]);
         if (++s == S) {
@@ -297,29 +343,33 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else {
     // ---------------- dequant (two threads per weight row), then the epilogue ----------------
     const int quarter = warp & 3;          // the TMEM lanes this warp may read: 32 * quarter ..
-    const int half = (warp - 2) >> 2;      // which 32 k of each stage (and which column chunks) it owns
+    const int half = (warp - 2) >> 2;      // which 64 k of each stage (and which column chunks) it owns
     const int row = quarter * 32 + lane;
     // the weight row this thread dequantises (rows past N are zero-filled by TMA; their scale is unused)
     const int grow = MODE == kGateUp ? n0 + (row < 64 ? row : p.rows_per_expert / 2 + row - 64)
                                      : min(n0 + row, p.n - 1);
     const int spr = p.k / G;
-    // Scales: 4 stages (256 k) per vector load, prefetched one quad of stages ahead.
-    constexpr int kHalvesPerQuad = 4 * kBK / G;  // 8, 4 or 2
-    auto load_scales = [&](int quad, uint32_t (&dst)[4]) {
+    // Scales: 2 stages (256 k) per vector load, prefetched one pair of stages ahead. The stages run
+    // through k blocks kb0 + rot .. kb0 + nk - 1, then kb0 .. kb0 + rot - 1, a pair at a time.
+    constexpr int kHalvesPerPair = 2 * kBK / G;  // 8, 4 or 2
+    int qkb = kb0 + rot;  // first k block of the pair whose scales load_scales fetches next
+    auto load_scales = [&](int pair, uint32_t (&dst)[4]) {
       dst[0] = dst[1] = dst[2] = dst[3] = 0u;
-      if (4 * quad >= nk) return;
-      const int kb = kblock(4 * quad);
-      if (MODE == kTernary) {  // scales [k/128][n]: this row's two groups of the quad
+      if (2 * pair >= nk) return;
+      const int kb = qkb;
+      qkb += 2;
+      if (qkb == kb0 + nk) qkb = kb0;
+      if (MODE == kTernary) {  // scales [k/128][n]: this row's group of each stage of the pair
         const size_t g0 = static_cast<size_t>(kb * kBK / 128);
         const __half2 v = __halves2half2(p.ws[g0 * p.n + grow], p.ws[(g0 + 1) * p.n + grow]);
         dst[0] = *reinterpret_cast<const uint32_t *>(&v);
         return;
       }
       const __half *src = p.ws + static_cast<size_t>(grow) * spr + kb * kBK / G;
-      if (kHalvesPerQuad == 8) {
+      if (kHalvesPerPair == 8) {
         const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src));
         dst[0] = v.x, dst[1] = v.y, dst[2] = v.z, dst[3] = v.w;
-      } else if (kHalvesPerQuad == 4) {
+      } else if (kHalvesPerPair == 4) {
         const uint2 v = __ldg(reinterpret_cast<const uint2 *>(src));
         dst[0] = v.x, dst[1] = v.y;
       } else {
@@ -331,107 +381,76 @@ __global__ void __launch_bounds__(kThreads, 2)
     int ds = 0;        // W/X ring slot of the next stage
     uint32_t dph = 0;  // its phase parity
     int das = 0, dar = 0;  // A ring slot of the next stage and its round
-    constexpr bool kPairs = MODE == kDense || MODE == kTernary;
-    // This thread's 16 TMEM columns of A slot 0 (lane = its row; half h holds K 32h .. 32h + 31).
-    const uint32_t a_t0 = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + p.tmem_a + 16 * half;
-    for (int q4 = 0; q4 * 4 < nk; ++q4) {
-      load_scales(q4 + 1, nxt);
-      // One-matrix modes: two stages per pass, so both tiles' loads, conversions and TMEM stores
-      // overlap and one wait for the stores covers both (the grouped modes, whose stages wait on
-      // their copies instead, measured slower this way).
-      auto dq = [&](int u, int s, uint32_t (&r)[16]) {
-        __half2 s2;
+    // This thread's 32 TMEM columns of A slot 0 (lane = its row; half h holds K 64h .. 64h + 63).
+    const uint32_t a_t0 = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + p.tmem_a + 32 * half;
+    // This thread's 32 bytes of W in ring slot 0 (one-matrix and grouped int4 modes).
+    const uint8_t *w_t0 = smem + L.w + row * (kBK / 2) + half * 32;
+    for (int q2 = 0; q2 * 2 < nk; ++q2) {
+      load_scales(q2 + 1, nxt);
+      // The scale of word c (0..7) of this thread's 64 k in stage u of the pair, as a half2 pair.
+      auto scale_of = [&](int u, int c) {
+        uint32_t w;
+        bool hi;
         if (G == 32) {
-          const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[u]);
-          s2 = half ? __high2half2(pair) : __low2half2(pair);
+          w = half ? cur[2 * u + 1] : cur[2 * u];
+          hi = (c >> 2) & 1;
         } else if (G == 64) {
-          const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[u >> 1]);
-          s2 = (u & 1) ? __high2half2(pair) : __low2half2(pair);
+          w = cur[u];
+          hi = half;
         } else {
-          const __half2 pair = *reinterpret_cast<const __half2 *>(&cur[0]);
-          s2 = (u >> 1) ? __high2half2(pair) : __low2half2(pair);
+          w = cur[0];
+          hi = u;
         }
-        uint4 q[4];
-        if (MODE == kTernary) {
+        const __half2 pair = *reinterpret_cast<const __half2 *>(&w);
+        return hi ? __high2half2(pair) : __low2half2(pair);
+      };
+      auto dq = [&](int u, int s, uint32_t (&r)[32]) {
+        uint4 q[8];
+        if (MODE == kTernary) {  // word rows 4 half .. 4 half + 3 of the stage's 8
+          const __half2 s2 = scale_of(u, 0);
           const uint8_t *wt = smem + L.w + s * kWTileBytes + row * 4;
-          const uint32_t w0 = *reinterpret_cast<const uint32_t *>(wt + (2 * half) * kBM * 4);
-          const uint32_t w1 = *reinterpret_cast<const uint32_t *>(wt + (2 * half + 1) * kBM * 4);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) q[c] = dequant_t2(c < 2 ? w0 : w1, 16 * (c & 1), s2);
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t w = *reinterpret_cast<const uint32_t *>(wt + (4 * half + c) * kBM * 4);
+            q[2 * c] = dequant_t2(w, 0, s2);
+            q[2 * c + 1] = dequant_t2(w, 16, s2);
+          }
         } else {
-          const uint4 w = *reinterpret_cast<const uint4 *>(smem + L.w + s * kWTileBytes + row * 32 + half * 16);
-          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+          const uint4 w0 = *reinterpret_cast<const uint4 *>(w_t0 + s * kWTileBytes);
+          const uint4 w1 = *reinterpret_cast<const uint4 *>(w_t0 + s * kWTileBytes + 16);
+          const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-          for (int c = 0; c < 4; ++c) q[c] = dequant_word(wv[c], s2);
+          for (int c = 0; c < 8; ++c)
+            q[c] = PERM ? dequant_word_perm(wv[c], scale_of(u, c)) : dequant_word(wv[c], scale_of(u, c));
         }
 #pragma unroll
-        for (int c = 0; c < 4; ++c) r[4 * c] = q[c].x, r[4 * c + 1] = q[c].y, r[4 * c + 2] = q[c].z, r[4 * c + 3] = q[c].w;
+        for (int c = 0; c < 8; ++c) r[4 * c] = q[c].x, r[4 * c + 1] = q[c].y, r[4 * c + 2] = q[c].z, r[4 * c + 3] = q[c].w;
       };
       auto wait_stage = [&](int s, uint32_t ph, int as, int ar) {
-        if (!*abort_flag && !mbar_wait(&full[s], ph)) {
+        bool ok = !*abort_flag;
+        if (ok) ok = mbar_wait(&full[s], ph);
+        if (ok && split_rings && ar > 0) ok = mbar_wait(&aempty[as], (ar - 1) & 1);
+        ok = __all_sync(0xffffffffu, ok);
+        tc_fence_after();  // the TMEM stores below come after the MMA that last read the slot
+        if (!ok && lane == 0 && !*abort_flag) {
           raise_status(kStatusGemmDeqWait);
           *abort_flag = 1;
         }
-        if (split_rings && ar > 0 && !*abort_flag && !mbar_wait(&aempty[as], (ar - 1) & 1)) {
-          raise_status(kStatusGemmDeqWait);
-          *abort_flag = 1;
-        }
+        return ok;
       };
-      if constexpr (kPairs) {
 #pragma unroll
-        for (int u = 0; u < 4; u += 2) {
-          const int i = 4 * q4 + u;
-          if (i >= nk) break;
-          const bool two = i + 1 < nk;
-          const int s0 = ds, as0 = das, ar0 = dar;
-          const uint32_t ph0 = dph;
-          if (++ds == S) ds = 0, dph ^= 1;
-          if (++das == SA) das = 0, ++dar;
-          int s1 = 0, as1 = 0, ar1 = 0;
-          uint32_t ph1 = 0;
-          if (two) {
-            s1 = ds, as1 = das, ar1 = dar, ph1 = dph;
-            if (++ds == S) ds = 0, dph ^= 1;
-            if (++das == SA) das = 0, ++dar;
-          }
-          wait_stage(s0, ph0, as0, ar0);
-          if (two) wait_stage(s1, ph1, as1, ar1);
-          if (__all_sync(0xffffffffu, !*abort_flag)) {
-            uint32_t r0[16], r1[16];
-            dq(u, s0, r0);
-            if (two) dq(u + 1, s1, r1);
-            tmem_st16(a_t0 + as0 * kACols, r0);
-            if (two) tmem_st16(a_t0 + as1 * kACols, r1);
-            tmem_wait_st();
-          }
-          tc_fence_before();
-          mbar_arrive(&deq[as0]);
-          if (two) mbar_arrive(&deq[as1]);
+      for (int u = 0; u < 2; ++u) {
+        if (2 * q2 + u >= nk) break;
+        if (wait_stage(ds, dph, das, dar)) {  // tcgen05.st is warp-collective: the whole warp or none
+          uint32_t r[32];
+          dq(u, ds, r);
+          tmem_st32(a_t0 + das * kACols, r);
+          tmem_wait_st();
         }
-      } else {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int i = 4 * q4 + u;
-          if (i >= nk) break;
-          const int s = ds, as = das;
-          wait_stage(s, dph, as, dar);
-          if (__all_sync(0xffffffffu, !*abort_flag)) {  // tcgen05.st is warp-collective
-            uint32_t r[16];
-            dq(u, s, r);
-            tmem_st16(a_t0 + as * kACols, r);
-            tmem_wait_st();
-          }
-          tc_fence_before();  // orders the TMEM stores before the arrive that the MMA thread acquires
-          mbar_arrive(&deq[as]);
-          if (++ds == S) {
-            ds = 0;
-            dph ^= 1;
-          }
-          if (++das == SA) {
-            das = 0;
-            ++dar;
-          }
-        }
+        tc_fence_before();  // orders the TMEM stores before the arrive that the MMA thread acquires
+        mbar_arrive(&deq[das]);
+        if (++ds == S) ds = 0, dph ^= 1;
+        if (++das == SA) das = 0, ++dar;
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
@@ -521,7 +540,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int j = 0; j < 32; ++j) {
             if (c0 + j < mcount) {
               const float g = v[j], u = up[row * p.bn + ((c0 + j) ^ (row & 15))];
-              p.y16[static_cast<size_t>(m0 + c0 + j) * p.n_out + col] = __float2half_rn(g / (1.f + expf(-g)) * u);
+              p.y16[static_cast<size_t>(m0 + c0 + j) * p.n_out + (PERM ? perm_col(col) : col)] =
+                  __float2half_rn(g / (1.f + expf(-g)) * u);
             }
           }
         }
@@ -562,14 +582,14 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
   p.tiles_m = two_per_sm ? 1 : (p.m + 255) / 256;
   p.bn = ((p.m + p.tiles_m - 1) / p.tiles_m + 15) / 16 * 16;
   p.tiles_n = (p.n + kBM - 1) / kBM;
-  // Split K (in quads of 64-k blocks) into as many parts as one wave of the SMs holds (two CTAs per
+  // Split K (in pairs of 128-k blocks) into as many parts as one wave of the SMs holds (two CTAs per
   // SM when they share it): the longest part sets the time (431 tokens x 3072 x 2048: 48 tiles x 3
   // parts of at most 12 blocks).
-  const int nkb = p.k / kBK, quads = nkb / 4;
+  const int nkb = p.k / kBK, pairs = nkb / 2;
   const int tiles = p.tiles_m * p.tiles_n;
   const int slots = two_per_sm ? 2 * dev.sms : dev.sms;
-  const int splitk = std::max(1, std::min(quads, slots / std::max(tiles, 1)));
-  p.kb_split = ((quads + splitk - 1) / splitk) * 4;
+  const int splitk = std::max(1, std::min(pairs, slots / std::max(tiles, 1)));
+  p.kb_split = ((pairs + splitk - 1) / splitk) * 2;
   p.splitk = (nkb + p.kb_split - 1) / p.kb_split;
   // Pipeline depth: as many stages as the SM's shared memory (or half of it) holds.
   const size_t budget = two_per_sm ? dev.smem_optin / 2 - 1024 : dev.smem_optin;
@@ -592,7 +612,7 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
                                      "mq_gemm_q4 weights")) {
     return rc;
   }
-  if (int rc = encode_tmap_2d(&xmap, x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k, p.m, static_cast<uint64_t>(p.k) * 2, kBK,
+  if (int rc = encode_tmap_2d(&xmap, x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k, p.m, static_cast<uint64_t>(p.k) * 2, 64,
                               p.bn, CU_TENSOR_MAP_SWIZZLE_128B, "mq_gemm_q4 activations"))
     return rc;
   if (p.splitk > 1 && !p.add) {
@@ -614,7 +634,7 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
   return launch_overlapped(kern, dim3(tiles * p.splitk), dim3(kThreads), smem, stream, "mq_gemm_q4", wmap, xmap, ymap, p);
 }
 
-template <int G, int MODE>
+template <int G, int MODE, bool PERM>
 int launch_grouped(const uint32_t *wq, const __half *ws, const __half *xs, int64_t pairs, int64_t k, int experts,
                    int rows_per_expert, const int32_t *tiles, const int32_t *ntiles, int max_tiles, int bn, void *out,
                    cudaStream_t stream, const DeviceInfo &dev) {
@@ -648,10 +668,10 @@ int launch_grouped(const uint32_t *wq, const __half *ws, const __half *xs, int64
   if (int rc = encode_tmap_2d(&wmap, wq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, p.k / 8, p.n, static_cast<uint64_t>(p.k) / 2,
                               kBK / 8, MODE == kGateUp ? kBM / 2 : kBM, CU_TENSOR_MAP_SWIZZLE_NONE, "mq_moe_gemm_q4 weights"))
     return rc;
-  if (int rc = encode_tmap_2d(&xmap, xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k, p.m, static_cast<uint64_t>(p.k) * 2, kBK,
+  if (int rc = encode_tmap_2d(&xmap, xs, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.k, p.m, static_cast<uint64_t>(p.k) * 2, 64,
                               p.bn, CU_TENSOR_MAP_SWIZZLE_128B, "mq_moe_gemm_q4 activations"))
     return rc;
-  auto kern = gemm_q4_kernel<G, MODE>;
+  auto kern = gemm_q4_kernel<G, MODE, PERM>;
   static size_t configured[64] = {};
   if (int rc = ensure_smem(kern, smem, configured, "mq_moe_gemm_q4")) return rc;
   p.y_tma = 0;
@@ -662,23 +682,31 @@ int launch_grouped(const uint32_t *wq, const __half *ws, const __half *xs, int64
 }  // namespace gemm
 
 // Grouped expert product (MoE): mode 1 = gate|up with SiLU (fp16 out), mode 2 = plain (fp32 out).
+// perm: xs rows (and mode 1's output rows) are stored in dequant_word_perm's k order.
 int moe_gemm_run(int mode, const uint32_t *wq, const uint16_t *ws, const uint16_t *xs, int64_t pairs, int64_t k,
                  int experts, int64_t rows_per_expert, int group, const int32_t *tiles, const int32_t *ntiles,
-                 int max_tiles, int tile_m, void *out, cudaStream_t stream) {
+                 int max_tiles, int tile_m, void *out, cudaStream_t stream, int perm) {
   DeviceInfo dev;
   if (int rc = device_info(&dev)) return rc;
   const __half *w16 = reinterpret_cast<const __half *>(ws);
   const __half *x16 = reinterpret_cast<const __half *>(xs);
   const int rpe = static_cast<int>(rows_per_expert);
-#define MQ_GROUPED(G)                                                                                                  \
-  return mode == 1 ? gemm::launch_grouped<G, gemm::kGateUp>(wq, w16, x16, pairs, k, experts, rpe, tiles, ntiles,       \
-                                                           max_tiles, tile_m, out, stream, dev)                       \
-                   : gemm::launch_grouped<G, gemm::kGrouped>(wq, w16, x16, pairs, k, experts, rpe, tiles, ntiles,      \
-                                                            max_tiles, tile_m, out, stream, dev)
+#define MQ_GROUPED(G, P)                                                                                               \
+  return mode == 1 ? gemm::launch_grouped<G, gemm::kGateUp, P>(wq, w16, x16, pairs, k, experts, rpe, tiles, ntiles,    \
+                                                              max_tiles, tile_m, out, stream, dev)                    \
+                   : gemm::launch_grouped<G, gemm::kGrouped, P>(wq, w16, x16, pairs, k, experts, rpe, tiles, ntiles,   \
+                                                               max_tiles, tile_m, out, stream, dev)
+  if (perm) {
+    switch (group) {
+      case 32: MQ_GROUPED(32, true);
+      case 64: MQ_GROUPED(64, true);
+      default: MQ_GROUPED(128, true);
+    }
+  }
   switch (group) {
-    case 32: MQ_GROUPED(32);
-    case 64: MQ_GROUPED(64);
-    default: MQ_GROUPED(128);
+    case 32: MQ_GROUPED(32, false);
+    case 64: MQ_GROUPED(64, false);
+    default: MQ_GROUPED(128, false);
   }
 #undef MQ_GROUPED
 }
@@ -881,5 +909,5 @@ extern "C" int mq_moe_gemm_q4(int mode, const uint32_t *wq, const uint16_t *ws, 
   MQ_REQUIRE(mq::aligned(wq, 16) && mq::aligned(ws, 16) && mq::aligned(xs, 16), MQ_EALIGN,
              "mq_moe_gemm_q4: wq, ws and xs must be 16-byte aligned");
   return mq::moe_gemm_run(mode, wq, ws, xs, pairs, k, experts, rows_per_expert, group, tiles, ntiles, max_tiles, tile_m,
-                          out, static_cast<cudaStream_t>(stream));
+                          out, static_cast<cudaStream_t>(stream), 0);
 }

@@ -213,8 +213,15 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
 
 // ---- gather: expert-sorted fp16 copies of the tokens' rows ---------------------------------------
 // xg[s] = fp16(x[order[s] / topk]) (p_gather of lfm2moe/kernels/mk.mojo:164-176); order null: s / topk.
+// perm: each 8 consecutive columns are stored in the k order 0, 4, 1, 5, 2, 6, 3, 7, the order in which
+// the grouped products dequantise a weight word (gemm_q4.cu, dequant_word_perm).
+__device__ __forceinline__ uint4 perm8(uint4 v) {  // halves 0..7 -> 0, 4, 1, 5, 2, 6, 3, 7
+  return make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x5410),
+                    __byte_perm(v.y, v.w, 0x7632));
+}
+
 __global__ void gather_kernel(const void *__restrict__ x, int x_f16, const int32_t *__restrict__ order, int pairs,
-                              int topk, int d, __half *__restrict__ xg) {
+                              int topk, int d, __half *__restrict__ xg, int perm = 0) {
   const int vec = d / 8;  // 8 values per thread step
   for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < static_cast<int64_t>(pairs) * vec;
        it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -233,6 +240,7 @@ __global__ void gather_kernel(const void *__restrict__ x, int x_f16, const int32
       const float4 a = src[0], b = src[1];
       out = make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y), pack_half2(b.z, b.w));
     }
+    if (perm) out = perm8(out);
     *reinterpret_cast<uint4 *>(xg + static_cast<size_t>(s) * d + c) = out;
   }
 }
@@ -539,12 +547,19 @@ extern "C" int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, co
   if (int rc = mq_moe_group(ids, tokens, topk, experts, mq::moe::kTileM, w.counts, w.offsets, w.order, w.slot_of, w.tiles,
                             w.ntiles, s))
     return rc;
-  if (int rc = mq_moe_gather(x, x_dtype, w.order, P, topk, d, reinterpret_cast<uint16_t *>(w.xg), s)) return rc;
+  // The activations and the SwiGLU outputs travel in the products' dequantisation k order (perm).
+  {
+    mq::DeviceInfo dev;
+    if (int rc = mq::device_info(&dev)) return rc;
+    mq::moe::gather_kernel<<<mq::moe::grid_for(P * (d / 8), 256, dev), 256, 0, s>>>(
+        x, x_dtype == MQ_F16, w.order, static_cast<int>(P), topk, static_cast<int>(d), w.xg, 1);
+    if (int rc = mq::check_launch("mq_moe_forward gather")) return rc;
+  }
   if (int rc = mq::moe_gemm_run(1, gu_wq, gu_ws, reinterpret_cast<const uint16_t *>(w.xg), P, d, experts, 2 * fe, group,
-                                w.tiles, w.ntiles, w.max_tiles, mq::moe::kTileM, w.a, s))
+                                w.tiles, w.ntiles, w.max_tiles, mq::moe::kTileM, w.a, s, 1))
     return rc;
   if (int rc = mq::moe_gemm_run(2, dn_wq, dn_ws, reinterpret_cast<const uint16_t *>(w.a), P, fe, experts, d, group, w.tiles,
-                                w.ntiles, w.max_tiles, mq::moe::kTileM, w.z, s))
+                                w.ntiles, w.max_tiles, mq::moe::kTileM, w.z, s, 1))
     return rc;
   return mq_moe_combine(w.z, w.slot_of, weights, tokens, topk, d, add, y, s);
 }
