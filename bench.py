@@ -557,11 +557,15 @@ def moe_bench(mq, synth, dev, stream, world, rank):
     return out
 
 
-def moe_bench_ep(mq, synth, dev, stream, world, rank, steps=30):
+def moe_bench_ep(mq, synth, dev, stream, world, rank, steps=50):
     """Tokens/s of the expert-parallel MoE layer (BASELINE configs[3] at N GPUs): rank r owns experts
-    [r * 128 / N, (r + 1) * 128 / N) and routes its share of the tokens; dispatch and combine are NCCL
-    all-to-alls in the fixed-capacity form (mq.ExpertParallelMoE with max_tokens: static split sizes,
-    no host read). Timed with CUDA events over `steps` layers, max over ranks."""
+    [r * 128 / N, (r + 1) * 128 / N) and routes its share of the tokens; rows travel to their experts'
+    owners and back through NVLink peer memory (mq.ExpertParallelMoE's peer exchange: kernels only, no
+    NCCL, no host read), the whole layer recorded once as a CUDA graph and replayed. Timed with CUDA
+    events, max over ranks; every rank checks its tokens' outputs against the fp64 oracle layer, and
+    the line reports the largest normwise error over the ranks (asserted <= 1e-3)."""
+    from oracle import moe as omoe
+
     d, fe, experts, topk = 2048, 768, 128, 8
     out = {}
     for tokens in (404, 1):
@@ -583,21 +587,81 @@ def moe_bench_ep(mq, synth, dev, stream, world, rank, steps=30):
             tids = torch.empty(0, topk, dtype=torch.int32, device=dev)
             tw = torch.empty(0, topk, device=dev)
         y = torch.empty(hi_t - lo_t, d, device=dev)
+        # per-phase device times: the layer's steps captured in one CUDA graph with timing events between
+        # them (external events, so that they are recorded on every replay)
+        L0 = layers[0]
+        B = L0.peer
+        ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(5)]
+
+        def phased():
+            st = mq.kernels._stream()
+            ev[0].record()
+            if hi_t > lo_t:
+                _, order, slot_of, local = L0.ops.plan(tids, hi_t - lo_t, topk, experts, world, L0.capacity)
+            else:
+                order = local = slot_of = L0.empty_plan
+            ev[1].record()
+            mq.lib.call("mq_ep_dispatch", tx.data_ptr(), 0, order.data_ptr(), local.data_ptr(), hi_t - lo_t, topk, d,
+                        world, rank, L0.capacity, B.peer_rows.data_ptr(), B.peer_ids.data_ptr(), B.peer_flags.data_ptr(),
+                        B.ptr["epoch"], B.ptr["done"], st)
+            ev[2].record()
+            g0 = L0.w
+            mq.lib.call("mq_ep_expert_step", B.ptr["rows"], B.ptr["ids"], g0[0].data_ptr(), g0[1].data_ptr(),
+                        g0[2].data_ptr(), g0[3].data_ptr(), world * L0.capacity, L0.local_experts, d, fe, 32, world, rank,
+                        L0.capacity, B.peer_ret.data_ptr(), B.ptr["flags"], B.peer_flags.data_ptr(), B.ptr["epoch"],
+                        B.ptr["done"] + 4, L0.workspace.data_ptr(), L0.workspace.numel(), st)
+            ev[3].record()
+            if hi_t > lo_t:
+                mq.lib.call("mq_ep_combine", B.ret.data_ptr(), slot_of.data_ptr(), tw.data_ptr(), hi_t - lo_t, topk, d,
+                            0, y.data_ptr(), B.ptr["flags"], world, B.ptr["epoch"], st)
+            else:
+                mq.lib.call("mq_ep_wait", B.ptr["flags"], 1, world, B.ptr["epoch"], st)
+            ev[4].record()
+
+        gph = graph_of(phased)
+        barrier(world)
+        acc = [0.0] * 4
+        for _ in range(10):
+            gph.replay()
+            torch.cuda.synchronize()
+            for i in range(4):
+                acc[i] += ev[i].elapsed_time(ev[i + 1]) / 10
+        names = ("plan", "dispatch", "wait_rows_experts_and_return", "wait_returns_and_combine")
+        phases = {nm: round(a * 1e3, 2) for nm, a in zip(names, acc)}
+        del gph
+        # the layer as a CUDA graph, one per weight copy, replayed back to back
+        graphs = [graph_of(lambda L=L: L(tx, tids, tw, y)) for L in layers]
         for i in range(3):
-            layers[i % copies](tx, tids, tw, y)
+            graphs[i % copies].replay()
         torch.cuda.synchronize()
         barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for i in range(steps):
-            layers[i % copies](tx, tids, tw, y)
+            graphs[i % copies].replay()
         e1.record(stream)
         torch.cuda.synchronize()
         ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+        status = int(max_over_ranks(float(mq.device_status()), world))
+        err = 0.0
+        if hi_t > lo_t:
+            ids_np = tids.cpu().numpy()
+            ref = omoe.moe_layer(m["x"][lo_t:hi_t], ids_np, tw.cpu().numpy(), m["gu_wq"], m["gu_ws"], m["dn_wq"],
+                                 m["dn_ws"], 32, fe)
+            err = float(np.abs(y.cpu().numpy() - ref).max() / np.abs(ref).max())
+        err = max_over_ranks(err, world)
+        assert err <= 1e-3 and status == 0, f"expert-parallel layer: normwise error {err}, device status {status}"
         out[f"tokens_{tokens}"] = {"ms": round(ms, 5), "tokens/s": round(tokens / (ms * 1e-3), 1),
+                                   "phases_us": phases, "parity_normwise_max_over_ranks": err,
                                    "parallelism": f"expert-parallel x{world} ({experts // world} experts per GPU), "
-                                                  "NCCL all-to-all dispatch and combine, fixed capacity "
-                                                  f"{max_tokens * topk} rows per rank pair"}
+                                                  "peer-memory dispatch and return over NVLink (no NCCL on the data "
+                                                  f"path), capacity {max_tokens * topk} rows per rank pair, "
+                                                  "the layer replayed as a CUDA graph"}
+        del graphs
+        torch.cuda.synchronize()
+        barrier(world)
+        for L in layers:
+            L.close()
         del layers, gws
     return out
 

@@ -267,6 +267,56 @@ MQ_API int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, const 
                           int experts, int topk, int64_t d, int64_t fe, int group, int add, void *workspace,
                           size_t workspace_bytes, void *stream);
 
+/* ---- expert parallelism over NVLink peer memory ------------------------------------------------------
+ * No counterpart in the reference, which runs every expert on one device (qwen3moe/model.mojo:256-267).
+ * One process per GPU; rank r owns the experts [r E / world, (r + 1) E / world). Each rank exports one
+ * device buffer (mq_ipc_handle) and maps its peers' (mq_ipc_open); the exchange then runs as kernels
+ * on the stream, with no host read, so a whole layer can be captured in a CUDA graph:
+ *   mq_ep_plan (capacity cap) -> mq_ep_dispatch -> mq_ep_expert_step -> mq_ep_combine
+ * (mq_ep_expert_step waits for the rows, mq_ep_combine for the returned outputs; mq_ep_wait is the
+ * same wait on its own).
+ * Buffers of rank r (each rank's own, mapped by the others; pointer tables are device arrays of world
+ * pointers, entry r = the local buffer): rows fp16 [world * cap][d] (received rows), ids int32
+ * [world * cap], ret fp32 [world * cap][d] (returned outputs, row d * cap + i for send slot i to owner
+ * d), flags int32 [2][world], epoch int32 and two arrival counters int32, all zero-initialised. Every
+ * wait is bounded: a rank that does not answer within 2 s is reported through mq_device_status
+ * (10: dispatch, 11: return) and the layer goes on without it. */
+
+/* Exports the device allocation holding ptr: a 64-byte handle and ptr's offset within it. */
+MQ_API int mq_ipc_handle(const void *ptr, void *handle, int64_t *offset);
+/* Maps a peer's exported allocation into the current device (peer access enabled): *ptr = its base + offset. */
+MQ_API int mq_ipc_open(const void *handle, int64_t offset, void **ptr);
+/* Unmaps what mq_ipc_open mapped (the same ptr and offset). */
+MQ_API int mq_ipc_close(void *ptr, int64_t offset);
+/* Starts a layer: epoch += 1 (every rank runs the same layers, so the epochs agree), and writes this rank's pairs into their owners' receive buffers: send slot d * cap + i (the fixed-capacity
+ * plan of mq_ep_plan: order, local_ids) becomes row rank * cap + i of owner d's rows, with id
+ * local_ids[slot] (-1 for an empty slot); then raises flag [0][rank] on every owner to the epoch.
+ * x: [tokens][d] fp32 or fp16 (may be NULL when tokens == 0); done: this rank's dispatch counter. */
+MQ_API int mq_ep_dispatch(const void *x, int x_dtype, const int32_t *order, const int32_t *local_ids, int64_t tokens,
+                          int topk, int64_t d, int world, int rank, int cap, uint16_t *const *peer_rows,
+                          int32_t *const *peer_ids, int *const *peer_flags, int *epoch, int *done, void *stream);
+/* Waits (one CTA, bounded) until flags[which][s] >= epoch for every rank s. */
+MQ_API int mq_ep_wait(const int *flags, int which, int world, const int *epoch, void *stream);
+/* Sends expert outputs back: row slot = s * cap + i with ids[slot] >= 0 goes from z (its row slot_of[slot],
+ * or slot when slot_of is NULL) to sender s's ret row rank * cap + i; then raises flag [1][rank] on
+ * every sender. done: this rank's return counter. */
+MQ_API int mq_ep_return(const float *z, const int32_t *slot_of, const int32_t *ids, int64_t d, int world, int rank,
+                        int cap, float *const *peer_ret, int *const *peer_flags, const int *epoch, int *done,
+                        void *stream);
+/* Waits for every rank's rows (flags [0]), then this rank's experts on its received rows (rows, ids; nrows = world * cap, ids -1
+ * skipped), then mq_ep_return. Expert weights are this rank's slices (experts = its expert count) in
+ * mq_moe_forward's layout. Workspace: mq_ep_workspace_size(nrows, experts, d, fe) bytes, 256-byte aligned. */
+MQ_API size_t mq_ep_workspace_size(int64_t rows, int experts, int64_t d, int64_t fe);
+MQ_API int mq_ep_expert_step(const uint16_t *rows, const int32_t *ids, const uint32_t *gu_wq, const uint16_t *gu_ws,
+                             const uint32_t *dn_wq, const uint16_t *dn_ws, int64_t nrows, int experts, int64_t d,
+                             int64_t fe, int group, int world, int rank, int cap, float *const *peer_ret,
+                             const int *flags, int *const *peer_flags, const int *epoch, int *done, void *workspace,
+                             size_t workspace_bytes, void *stream);
+/* Waits for every owner's returned outputs (flags [1]), then y[t] (+)= sum_k weights[t][k] * ret[slot_of[t * topk + k]]
+ * (mq_moe_combine over the plan's slot_of). */
+MQ_API int mq_ep_combine(const float *ret, const int32_t *slot_of, const float *weights, int64_t tokens, int topk,
+                         int64_t d, int add, float *y, const int *flags, int world, const int *epoch, void *stream);
+
 /* ---- weight files -------------------------------------------------------------------------------- */
 
 /* Reads nbytes at byte `offset` of the file at `path` into device memory at dst, through two pinned

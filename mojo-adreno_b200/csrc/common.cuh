@@ -119,6 +119,8 @@ enum : int {
   kStatusGemvDrainWait = 7,
   kStatusMoeBadExpertId = 8,  // an expert id >= experts: the pair was left out (negative ids mean "none")
   kStatusEpOverflow = 9,      // more pairs for one rank than the plan's capacity: the excess was left out
+  kStatusEpDispatchWait = 10,  // an expert-parallel rank's rows did not arrive in time (the layer went on without them)
+  kStatusEpReturnWait = 11,    // an owner's expert outputs did not come back in time
 };
 
 // Waits until the kernels this grid depends on (earlier work on its stream) have completed and
@@ -128,6 +130,24 @@ __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wa
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void raise_status(int code) { atomicCAS(&g_status, 0, code); }
+
+
+// ---- device: waiting for expert-parallel peers ------------------------------------------------
+
+// A wait for the flags of an expert-parallel exchange (ep.cu): flags[which * world + s] >= *epoch for
+// every rank s. Kernels that start a step of the exchange take one (flags null: no wait) and wait in
+// every CTA before touching the data the flags announce.
+struct FlagWait {
+  const int *flags = nullptr;
+  int which = 0, world = 0;
+  const int *epoch = nullptr;
+};
+
+__device__ __forceinline__ int ld_acquire_sys(const int *p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 // ---- device: PTX wrappers ---------------------------------------------------------------------
 
@@ -142,6 +162,26 @@ __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+// Threads 0 .. world - 1 of the CTA wait (bounded: 2 s, then status 10 or 11 and go on) for their
+// rank's flag, then the CTA synchronises; the acquire loads make the peers' writes visible.
+__device__ __forceinline__ void wait_flags(const FlagWait &w) {
+  if (!w.flags) return;
+  const int e = *w.epoch;
+  for (int s = threadIdx.x; s < w.world; s += blockDim.x) {
+    const int *f = w.flags + w.which * w.world + s;
+    if (ld_acquire_sys(f) >= e) continue;
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire_sys(f) < e) {
+      if (globaltimer() - t0 > 2000000000ull) {
+        raise_status(w.which == 0 ? kStatusEpDispatchWait : kStatusEpReturnWait);
+        break;
+      }
+      __nanosleep(200);
+    }
+  }
+  __syncthreads();
 }
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {

@@ -78,7 +78,8 @@ __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + 
 
 // First weight row of output tile `tile` (the rows themselves, or an expert's rows through ids).
 // An expert id past the weight matrix is reported and read as expert 0; a negative id ("no expert",
-// the padding of a fixed-capacity exchange) reads expert 0 silently.
+// the padding of a fixed-capacity exchange) loads nothing (issue skips the tile) and its outputs are
+// left unspecified.
 __device__ __forceinline__ int weight_row0(const Params &p, int tile) {
   const int tr = p.gu ? kRows / 2 : kRows;  // weight rows (of one kind) per output tile
   if (!p.ids) return tile * tr;
@@ -168,6 +169,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int slot = u % S;
     uint64_t *bar = full + slot;
     uint8_t *dst = ring + slot * p.slot_bytes;
+    if (p.ids && __ldg(p.ids + tile / p.tpg) < 0) {  // an empty slot ("no expert"): nothing to read; its outputs are unused
+      mbar_arrive(bar);
+      return;
+    }
     const int wrow = weight_row0(p, tile);
     mbar_expect_tx(bar, bytes);
     if (p.gu) {  // [2 planes][16 rows]: the gate rows into slot rows 0..15, the up rows into 16..31

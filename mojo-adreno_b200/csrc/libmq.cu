@@ -10,3 +10,4 @@
 #include "moe.cu"
 #include "pack.cu"
 #include "io.cu"
+#include "ep.cu"

@@ -85,7 +85,8 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
                                                               int32_t *__restrict__ offsets, int32_t *__restrict__ order,
                                                               int32_t *__restrict__ slot_of, int32_t *__restrict__ tiles,
                                                               int32_t *__restrict__ ntiles, int32_t *__restrict__ local,
-                                                              int cap) {
+                                                              int cap, FlagWait wait = FlagWait()) {
+  wait_flags(wait);  // an expert-parallel owner: the senders' rows and ids have arrived
   extern __shared__ int32_t sh[];
   int32_t *warp_cnt = sh;                    // [32 warps][experts]: pairs of the warp's range, then their start
   int32_t *start = warp_cnt + 32 * experts;  // [experts + 1]: bucket totals, then offsets
@@ -220,10 +221,14 @@ __device__ __forceinline__ uint4 perm8(uint4 v) {  // halves 0..7 -> 0, 4, 1, 5,
                     __byte_perm(v.y, v.w, 0x7632));
 }
 
+// valid (may be null): only the first *valid positions are copied (the pairs the grouping kept).
 __global__ void gather_kernel(const void *__restrict__ x, int x_f16, const int32_t *__restrict__ order, int pairs,
-                              int topk, int d, __half *__restrict__ xg, int perm = 0) {
+                              int topk, int d, __half *__restrict__ xg, int perm = 0, const int32_t *valid = nullptr,
+                              FlagWait wait = FlagWait()) {
+  wait_flags(wait);  // an expert-parallel owner: the senders' rows and ids have arrived
   const int vec = d / 8;  // 8 values per thread step
-  for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < static_cast<int64_t>(pairs) * vec;
+  const int64_t n = static_cast<int64_t>(valid ? min(*valid, pairs) : pairs) * vec;
+  for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < n;
        it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int s = static_cast<int>(it / vec), c = static_cast<int>(it % vec) * 8;
     const int o = order ? order[s] : s;  // no order: the pairs in their own order
@@ -257,7 +262,9 @@ __global__ void silu_mul_kernel(const float *__restrict__ h, float *__restrict__
 // ---- combine: y[t][c] (+)= sum_k w[t][k] * z[slot_of[t * topk + k]][c] (p_moe_sum, p_combine) -----
 // The k terms are added in order k = 0 .. topk - 1, then added to y: deterministic.
 __global__ void combine_kernel(const float *__restrict__ z, const int32_t *__restrict__ slot_of,
-                               const float *__restrict__ w, int tokens, int topk, int d, int add, float *__restrict__ y) {
+                               const float *__restrict__ w, int tokens, int topk, int d, int add, float *__restrict__ y,
+                               FlagWait wait = FlagWait()) {
+  wait_flags(wait);  // an expert-parallel sender: every owner's outputs have come back
   const int vec = d / 4;
   for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < static_cast<int64_t>(tokens) * vec;
        it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -497,6 +504,60 @@ extern "C" size_t mq_moe_workspace_size(int64_t tokens, int experts, int topk, i
   return mq::moe::carve(nullptr, tokens, experts, topk, d, fe).bytes;
 }
 
+namespace mq {
+namespace moe {
+
+// The experts of the layer on P = tokens * topk pairs (ids -1: no expert, skipped): z_out receives the
+// expert outputs (fp32 rows of d) and slot_of_out the row of pair p in them (null: row p). Up to
+// small_pairs pairs run on the streaming GEMVs (each pair's own x), more on grouping + gather + the
+// two grouped tensor-core products (the activations in their dequantisation k order).
+int experts(const void *x, int x_dtype, const int32_t *ids, const uint32_t *gu_wq, const uint16_t *gu_ws,
+            const uint32_t *dn_wq, const uint16_t *dn_ws, int64_t tokens, int experts_n, int topk, int64_t d, int64_t fe,
+            int group, const Work &w, cudaStream_t s, int64_t small_pairs, const float **z_out,
+            const int32_t **slot_of_out, FlagWait wait = FlagWait()) {
+  const int64_t P = tokens * topk;
+  DeviceInfo dev;
+  if (int rc = device_info(&dev)) return rc;
+  if (P <= small_pairs) {
+    float *a = reinterpret_cast<float *>(w.a), *z = w.z;
+    gather_kernel<<<grid_for(P * (d / 8), 256, dev), 256, 0, s>>>(x, x_dtype == MQ_F16, nullptr, static_cast<int>(P),
+                                                                  topk, static_cast<int>(d), w.xg, 0, nullptr, wait);
+    if (int rc = check_launch("mq_moe_forward gather")) return rc;
+    if (int rc = gemv::gemv_q4_grouped(gu_wq, gu_ws, experts_n * 2 * fe, w.xg, a, ids, static_cast<int>(P),
+                                       static_cast<int>(2 * fe), static_cast<int>(fe), d, group, 1, s, 1, 1))
+      return rc;
+    if (int rc = gemv::gemv_q4_grouped(dn_wq, dn_ws, experts_n * d, a, z, ids, static_cast<int>(P), static_cast<int>(d),
+                                       static_cast<int>(d), fe, group, 1, s, 0, 0))
+      return rc;
+    *z_out = z;
+    *slot_of_out = nullptr;
+    return MQ_OK;
+  }
+  {
+    const size_t smem = (32 * experts_n + 2 * (experts_n + 1)) * sizeof(int32_t);
+    group_kernel<<<1, kGroupThreads, smem, s>>>(ids, 1, static_cast<int>(P), experts_n, kTileM, w.counts, w.offsets,
+                                                 w.order, w.slot_of, w.tiles, w.ntiles, nullptr, 0, wait);
+    if (int rc = check_launch("mq_moe_forward group")) return rc;
+  }
+  // The activations and the SwiGLU outputs travel in the products' dequantisation k order (perm); only
+  // the pairs the grouping kept are gathered (offsets[experts] of them).
+  gather_kernel<<<grid_for(P * (d / 8), 256, dev), 256, 0, s>>>(x, x_dtype == MQ_F16, w.order, static_cast<int>(P), topk,
+                                                                static_cast<int>(d), w.xg, 1, w.offsets + experts_n);
+  if (int rc = check_launch("mq_moe_forward gather")) return rc;
+  if (int rc = moe_gemm_run(1, gu_wq, gu_ws, reinterpret_cast<const uint16_t *>(w.xg), P, d, experts_n, 2 * fe, group,
+                            w.tiles, w.ntiles, w.max_tiles, kTileM, w.a, s, 1))
+    return rc;
+  if (int rc = moe_gemm_run(2, dn_wq, dn_ws, reinterpret_cast<const uint16_t *>(w.a), P, fe, experts_n, d, group, w.tiles,
+                            w.ntiles, w.max_tiles, kTileM, w.z, s, 1))
+    return rc;
+  *z_out = w.z;
+  *slot_of_out = w.slot_of;
+  return MQ_OK;
+}
+
+}  // namespace moe
+}  // namespace mq
+
 extern "C" int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, const float *weights, const uint32_t *gu_wq,
                               const uint16_t *gu_ws, const uint32_t *dn_wq, const uint16_t *dn_ws, float *y, int64_t tokens,
                               int experts, int topk, int64_t d, int64_t fe, int group, int add, void *workspace,
@@ -526,40 +587,65 @@ extern "C" int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, co
       return rc;
     return mq_moe_combine(z, nullptr, weights, 1, topk, d, add, y, s);
   }
-  if (P <= mq::moe::kSmallPairs) {
-    // A few pairs (a small decode batch; an expert-parallel rank's share of one token): the same
-    // streaming GEMVs with each pair's own x, fp16 as the grouped GEMMs take it, instead of grouping
-    // tokens for tensor-core tiles they would barely fill.
-    float *a = reinterpret_cast<float *>(w.a), *z = w.z;
-    mq::DeviceInfo dev;
-    if (int rc = mq::device_info(&dev)) return rc;
-    mq::moe::gather_kernel<<<mq::moe::grid_for(P * (d / 8), 256, dev), 256, 0, s>>>(
-        x, x_dtype == MQ_F16, nullptr, static_cast<int>(P), topk, static_cast<int>(d), w.xg);
-    if (int rc = mq::check_launch("mq_moe_forward gather")) return rc;
-    if (int rc = mq::gemv::gemv_q4_grouped(gu_wq, gu_ws, experts * 2 * fe, w.xg, a, ids, static_cast<int>(P),
-                                           static_cast<int>(2 * fe), static_cast<int>(fe), d, group, 1, s, 1, 1))
-      return rc;
-    if (int rc = mq::gemv::gemv_q4_grouped(dn_wq, dn_ws, experts * d, a, z, ids, static_cast<int>(P), static_cast<int>(d),
-                                           static_cast<int>(d), fe, group, 1, s, 0, 0))
-      return rc;
-    return mq_moe_combine(z, nullptr, weights, tokens, topk, d, add, y, s);
-  }
-  if (int rc = mq_moe_group(ids, tokens, topk, experts, mq::moe::kTileM, w.counts, w.offsets, w.order, w.slot_of, w.tiles,
-                            w.ntiles, s))
+  // Up to kSmallPairs pairs (a small decode batch, an expert-parallel rank's share of one token) run
+  // on the streaming GEMVs with each pair's own fp16 x instead of tensor-core tiles they would barely fill.
+  const float *z = nullptr;
+  const int32_t *slot_of = nullptr;
+  if (int rc = mq::moe::experts(x, x_dtype, ids, gu_wq, gu_ws, dn_wq, dn_ws, tokens, experts, topk, d, fe, group, w, s,
+                                mq::moe::kSmallPairs, &z, &slot_of))
     return rc;
-  // The activations and the SwiGLU outputs travel in the products' dequantisation k order (perm).
-  {
-    mq::DeviceInfo dev;
-    if (int rc = mq::device_info(&dev)) return rc;
-    mq::moe::gather_kernel<<<mq::moe::grid_for(P * (d / 8), 256, dev), 256, 0, s>>>(
-        x, x_dtype == MQ_F16, w.order, static_cast<int>(P), topk, static_cast<int>(d), w.xg, 1);
-    if (int rc = mq::check_launch("mq_moe_forward gather")) return rc;
-  }
-  if (int rc = mq::moe_gemm_run(1, gu_wq, gu_ws, reinterpret_cast<const uint16_t *>(w.xg), P, d, experts, 2 * fe, group,
-                                w.tiles, w.ntiles, w.max_tiles, mq::moe::kTileM, w.a, s, 1))
+  return mq_moe_combine(z, slot_of, weights, tokens, topk, d, add, y, s);
+}
+
+extern "C" size_t mq_ep_workspace_size(int64_t rows, int experts, int64_t d, int64_t fe) {
+  return mq_moe_workspace_size(rows, experts, 1, d, fe);
+}
+
+extern "C" int mq_ep_expert_step(const uint16_t *rows, const int32_t *ids, const uint32_t *gu_wq, const uint16_t *gu_ws,
+                                 const uint32_t *dn_wq, const uint16_t *dn_ws, int64_t nrows, int experts, int64_t d,
+                                 int64_t fe, int group, int world, int rank, int cap, float *const *peer_ret,
+                                 const int *flags, int *const *peer_flags, const int *epoch, int *done, void *workspace,
+                                 size_t workspace_bytes, void *stream) {
+  MQ_REQUIRE(rows && ids && gu_wq && gu_ws && dn_wq && dn_ws && peer_ret && flags && peer_flags && epoch && done,
+             MQ_EINVAL, "mq_ep_expert_step: null pointer");
+  MQ_REQUIRE(nrows == static_cast<int64_t>(world) * cap && nrows > 0, MQ_EINVAL,
+             "mq_ep_expert_step: nrows must be world * cap");
+  MQ_REQUIRE(experts >= 1 && experts <= 256 && d % 256 == 0 && fe % 256 == 0, MQ_EINVAL,
+             "mq_ep_expert_step: bad experts, d or fe");
+  const mq::moe::Work need = mq::moe::carve(nullptr, nrows, experts, 1, d, fe);
+  MQ_REQUIRE(workspace && workspace_bytes >= need.bytes && mq::aligned(workspace, 256), MQ_EINVAL,
+             "mq_ep_expert_step: needs a 256-byte aligned workspace of %zu bytes", need.bytes);
+  const mq::moe::Work w = mq::moe::carve(static_cast<uint8_t *>(workspace), nrows, experts, 1, d, fe);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The received rows hold at most a few real pairs when the layer carries a few tokens (decode):
+  // the GEMVs skip the empty slots (id -1) without reading weights, so they serve up to 64 slots.
+  const float *z = nullptr;
+  const int32_t *slot_of = nullptr;
+  mq::FlagWait wait;  // the senders' rows: the first kernel waits for them
+  wait.flags = flags;
+  wait.which = 0;
+  wait.world = world;
+  wait.epoch = epoch;
+  if (int rc = mq::moe::experts(rows, MQ_F16, ids, gu_wq, gu_ws, dn_wq, dn_ws, nrows, experts, 1, d, fe, group, w, s,
+                                64, &z, &slot_of, wait))
     return rc;
-  if (int rc = mq::moe_gemm_run(2, dn_wq, dn_ws, reinterpret_cast<const uint16_t *>(w.a), P, fe, experts, d, group, w.tiles,
-                                w.ntiles, w.max_tiles, mq::moe::kTileM, w.z, s, 1))
-    return rc;
-  return mq_moe_combine(w.z, w.slot_of, weights, tokens, topk, d, add, y, s);
+  return mq_ep_return(z, slot_of, ids, d, world, rank, cap, peer_ret, peer_flags, epoch, done, s);
+}
+
+extern "C" int mq_ep_combine(const float *ret, const int32_t *slot_of, const float *weights, int64_t tokens, int topk,
+                             int64_t d, int add, float *y, const int *flags, int world, const int *epoch, void *stream) {
+  MQ_REQUIRE(ret && slot_of && weights && y && flags && epoch, MQ_EINVAL, "mq_ep_combine: null pointer");
+  MQ_REQUIRE(tokens > 0 && topk >= 1 && d > 0 && d % 4 == 0 && world >= 1 && world <= 256, MQ_EINVAL,
+             "mq_ep_combine: bad shape (d must be a multiple of 4)");
+  MQ_REQUIRE(mq::aligned(ret, 16) && mq::aligned(y, 16), MQ_EALIGN, "mq_ep_combine: ret and y must be 16-byte aligned");
+  mq::DeviceInfo dev;
+  if (int rc = mq::device_info(&dev)) return rc;
+  mq::FlagWait wait;  // every owner's outputs: each CTA waits for them
+  wait.flags = flags;
+  wait.which = 1;
+  wait.world = world;
+  wait.epoch = epoch;
+  mq::moe::combine_kernel<<<mq::moe::grid_for(tokens * (d / 4), 256, dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      ret, slot_of, weights, static_cast<int>(tokens), topk, static_cast<int>(d), add != 0, y, wait);
+  return mq::check_launch("mq_ep_combine");
 }

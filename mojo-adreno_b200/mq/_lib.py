@@ -39,6 +39,17 @@ SIGNATURES = {
     "mq_quantize_q4": (c_int, [c_vp, c_int, c_i64, c_i64, c_int, c_int, c_vp, c_vp, c_vp]),
     "mq_q4_0_to_words": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp]),
     "mq_pack_ternary": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp]),
+    "mq_ipc_handle": (c_int, [c_vp, c_vp, ctypes.POINTER(c_i64)]),
+    "mq_ipc_open": (c_int, [c_vp, c_i64, ctypes.POINTER(c_vp)]),
+    "mq_ipc_close": (c_int, [c_vp, c_i64]),
+    "mq_ep_dispatch": (c_int, [c_vp, c_int, c_vp, c_vp, c_i64, c_int, c_i64, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp,
+                               c_vp, c_vp]),
+    "mq_ep_wait": (c_int, [c_vp, c_int, c_int, c_vp, c_vp]),
+    "mq_ep_return": (c_int, [c_vp, c_vp, c_vp, c_i64, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "mq_ep_workspace_size": (c_size, [c_i64, c_int, c_i64, c_i64]),
+    "mq_ep_expert_step": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_int, c_i64, c_i64, c_int, c_int, c_int,
+                                  c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_size, c_vp]),
+    "mq_ep_combine": (c_int, [c_vp, c_vp, c_vp, c_i64, c_int, c_i64, c_int, c_vp, c_vp, c_int, c_vp, c_vp]),
     "mq_read_file_to_device": (c_int, [c_vp, c_i64, c_char_p, c_i64, c_vp]),
     "mq_pack_half": (c_int, [c_vp, c_vp, c_i64, c_vp]),
 }

@@ -15,7 +15,15 @@ is then:
      does (moek.mojo:479-488).
 
 Every rank takes the same collective steps in the same order, also when it sends or receives no
-rows. Two exchange forms:
+rows. Three exchange forms:
+
+- peer (the default when max_tokens is given): no NCCL on the data path. Each rank exports one
+  device buffer through CUDA IPC and maps the others' (NVLink peer memory); a layer is then a chain
+  of kernels on the stream -- mq_ep_plan, mq_ep_dispatch (the pairs' rows written straight into
+  their owners' receive buffers, at fixed per-sender slots), mq_ep_expert_step (waits for the rows,
+  runs the owner's experts, writes the outputs straight back into the senders' return buffers),
+  mq_ep_combine (waits for them, sums per token) -- with epoch flags and bounded waits, no host
+  read, so a whole layer can be captured in a CUDA graph. Only real pairs cross NVLink.
 
 - compact (default): only the pairs travel; the split sizes are exchanged first and read on the host
   (one small device-to-host copy per layer), which the variable-size all-to-all needs.
@@ -24,6 +32,8 @@ rows. Two exchange forms:
   the layer needs no host read and stays asynchronous on the stream; the price is the empty slots'
   bytes on NVLink (the experts skip them).
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -86,6 +96,55 @@ class DeviceOps:
         return y
 
 
+class PeerBuffers:
+    """One rank's exchange buffers for the peer form, and device tables of every rank's buffers.
+
+    One allocation holds rows fp16 [world * cap, d] (received rows), ids int32 [world * cap], ret fp32
+    [world * cap, d] (returned outputs), flags int32 [2, world], the epoch and two arrival counters, all
+    zeroed. It is exported with mq_ipc_handle; the other ranks' allocations are mapped with mq_ipc_open
+    (one mapping per peer). Table entry r of peer_* is rank r's buffer as this device addresses it."""
+
+    def __init__(self, world, rank, cap, d, device, pg=None):
+        slots = world * cap
+        parts = [("rows", slots * d * 2), ("ids", slots * 4), ("ret", slots * d * 4), ("flags", 2 * world * 4),
+                 ("epoch", 4), ("done", 8)]
+        self.off, at = {}, 0
+        for name, n in parts:
+            self.off[name] = at
+            at += (n + 255) // 256 * 256
+        self.buf = torch.zeros(at, dtype=torch.uint8, device=device)
+        torch.cuda.synchronize(device)  # zeroed before any peer can write into it
+        base = self.buf.data_ptr()
+        self.opened = []
+        bases = [base] * world
+        if world > 1:
+            handle, offset = (ctypes.c_char * 64)(), ctypes.c_int64()
+            lib.call("mq_ipc_handle", base, ctypes.cast(handle, ctypes.c_void_p), ctypes.byref(offset))
+            metas = [None] * world
+            dist.all_gather_object(metas, (bytes(handle), offset.value), group=pg)
+            for s_, (hb, ob) in enumerate(metas):
+                if s_ == rank:
+                    continue
+                ptr = ctypes.c_void_p()
+                hbuf = ctypes.create_string_buffer(hb, 64)
+                lib.call("mq_ipc_open", ctypes.cast(hbuf, ctypes.c_void_p), ob, ctypes.byref(ptr))
+                bases[s_] = ptr.value
+                self.opened.append((ptr.value, ob))
+            dist.barrier(group=pg)  # every rank mapped every buffer before any layer runs
+
+        def table(name):
+            return torch.tensor([b + self.off[name] for b in bases], dtype=torch.int64, device=device)
+
+        self.peer_rows, self.peer_ids, self.peer_ret, self.peer_flags = (table(n) for n in ("rows", "ids", "ret", "flags"))
+        self.ptr = {name: base + o for name, o in self.off.items()}
+        self.ret = self.buf[self.off["ret"]:self.off["ret"] + slots * d * 4].view(torch.float32).view(slots, d)
+
+    def close(self):
+        for ptr, off in self.opened:
+            lib.call("mq_ipc_close", ptr, off)
+        self.opened = []
+
+
 class ExpertParallelMoE:
     """One rank's share of an expert-parallel MoE layer.
 
@@ -96,7 +155,7 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, gu_wq, gu_ws, dn_wq, dn_ws, d, fe, experts, topk=8, group=32, pg=None, ops=None,
-                 max_tokens=None):
+                 max_tokens=None, exchange=None):
         self.pg = pg
         self.world = dist.get_world_size(pg) if dist.is_initialized() else 1
         self.rank = dist.get_rank(pg) if dist.is_initialized() else 0
@@ -111,6 +170,18 @@ class ExpertParallelMoE:
             _need(dn_wq, "dn_wq", _WORDS, local * d * fe // 8)
             _need(dn_ws, "dn_ws", (torch.float16,), local * d * fe // group)
         self.w = (gu_wq, gu_ws, dn_wq, dn_ws)
+        # peer: device peer-memory exchange (needs the fixed capacity and the device path); nccl: all-to-alls
+        self.exchange = exchange or ("peer" if self.capacity and ops is None else "nccl")
+        if self.exchange == "peer":
+            if not self.capacity or ops is not None:
+                raise MQError(-1, "the peer exchange needs max_tokens and the device ops")
+            dev = gu_wq.device
+            self.local_experts = local
+            self.peer = PeerBuffers(self.world, self.rank, self.capacity, d, dev, pg)
+            rows = self.world * self.capacity
+            nbytes = lib.mq_ep_workspace_size(rows, local, d, fe)
+            self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            self.empty_plan = torch.full((rows,), -1, dtype=torch.int32, device=dev)
 
     def _a2a(self, out, inp, out_splits, in_splits):
         if self.world == 1:
@@ -124,6 +195,8 @@ class ExpertParallelMoE:
         tokens = x.shape[0]
         if ids.numel() != tokens * topk or weights.numel() != tokens * topk:
             raise MQError(-1, f"ids / weights must hold tokens * topk = {tokens * topk} entries")
+        if self.exchange == "peer":
+            return self._forward_peer(x, ids, weights, y, add)
         if self.capacity:
             return self._forward_fixed(x, ids, weights, y, add)
         # 1. plan, and the rows to send, in send order (a rank without tokens still joins every exchange)
@@ -179,5 +252,36 @@ class ExpertParallelMoE:
         if tokens == 0:
             return y
         return self.ops.combine(ret, slot_of, weights, tokens, topk, d, add, y)
+
+    def _forward_peer(self, x, ids, weights, y, add):
+        """The peer-memory exchange: every step a kernel on the current stream, no host read."""
+        d, topk, world, rank, cap, B = self.d, self.topk, self.world, self.rank, self.capacity, self.peer
+        tokens = x.shape[0]
+        if tokens * topk > cap:
+            raise MQError(-1, f"{tokens} tokens exceed max_tokens = {cap // topk}")
+        st = _stream()
+        if tokens > 0:
+            _, order, slot_of, local = self.ops.plan(ids, tokens, topk, self.experts, world, cap)
+        else:
+            order = local = self.empty_plan
+        lib.call("mq_ep_dispatch", _p(x) if tokens else None, MQ_F16 if x.dtype == torch.float16 else MQ_F32, _p(order),
+                 _p(local), tokens, topk, d, world, rank, cap, _p(B.peer_rows), _p(B.peer_ids), _p(B.peer_flags),
+                 B.ptr["epoch"], B.ptr["done"], st)
+        gu_wq, gu_ws, dn_wq, dn_ws = self.w
+        lib.call("mq_ep_expert_step", B.ptr["rows"], B.ptr["ids"], _p(gu_wq), _p(gu_ws), _p(dn_wq), _p(dn_ws),
+                 world * cap, self.local_experts, d, self.fe, self.group, world, rank, cap, _p(B.peer_ret),
+                 B.ptr["flags"], _p(B.peer_flags), B.ptr["epoch"], B.ptr["done"] + 4, _p(self.workspace),
+                 self.workspace.numel(), st)
+        if tokens == 0:  # still waits for the returns: every rank takes the same steps
+            lib.call("mq_ep_wait", B.ptr["flags"], 1, world, B.ptr["epoch"], st)
+            return y
+        lib.call("mq_ep_combine", _p(B.ret), _p(slot_of), _p(weights), tokens, topk, d, int(bool(add)), _p(y),
+                 B.ptr["flags"], world, B.ptr["epoch"], st)
+        return y
+
+    def close(self):
+        """Unmaps the peers' buffers (call on every rank after the last layer, before the process group ends)."""
+        if self.exchange == "peer":
+            self.peer.close()
 
     __call__ = forward

@@ -1,6 +1,8 @@
 """One rank of the 2-GPU expert-parallel MoE check (launched by tests/test_ep_gpu.py through
-torch.distributed.run): Qwen3-30B-A3B layer shapes, each rank with its own tokens and its 64 experts,
-NCCL all-to-all; the rank's output is compared with the fp64 oracle layer on the full expert set."""
+torch.distributed.run): Qwen3-30B-A3B layer shapes, each rank with its own tokens and its 64 experts;
+with EP_MAX_TOKENS the peer-memory exchange (rows written into the owners' buffers over NVLink),
+without it the compact NCCL all-to-all. The rank's output is compared with the fp64 oracle layer on
+the full expert set, over two layers in a row, eagerly and replayed from a CUDA graph (peer form)."""
 import datetime
 import os
 import sys
@@ -38,12 +40,26 @@ def main():
                                    t(m["dn_wq"][lo * d:hi * d]), t(m["dn_ws"][lo * d:hi * d]), d, fe, experts, topk=topk,
                                    group=group, max_tokens=int(os.environ.get("EP_MAX_TOKENS") or 0) or None)
         ys = []
+        tx, tids, tw = t(x), t(ids), t(w)
         for _ in range(2):  # two layers in a row through the same buffers
             y = torch.full((counts[rank], d), float("nan"), device=dev)
-            moe(t(x), t(ids), t(w), y)
+            moe(tx, tids, tw, y)
             ys.append(y)
+        if moe.exchange == "peer":  # the same layer captured once and replayed twice
+            yg = torch.full((counts[rank], d), float("nan"), device=dev)
+            g = torch.cuda.CUDAGraph()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g):
+                moe(tx, tids, tw, yg)
+            for _ in range(2):
+                g.replay()
+            torch.cuda.synchronize()
+            ys.append(yg.clone())
+            del g
         torch.cuda.synchronize()
         assert mq.device_status() == 0
+        dist.barrier()
+        moe.close()
         if counts[rank]:
             ref = omoe.moe_layer(x, ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], group, fe)
             for y in ys:
