@@ -54,9 +54,10 @@ int launch_overlapped(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
 namespace gemv {
 // The expert-indirect GEMV of the MoE decode (gemv_q4.cu); gate_up fuses the SwiGLU of gate|up rows;
 // x is fp32, or fp16 with x_f16.
+// gate (may be null): a device count; when *gate > gate_max the launch does nothing.
 int gemv_q4_grouped(const uint32_t *wq, const uint16_t *ws, int64_t wrows, const void *x, float *y,
                     const int32_t *ids, int ngroups, int group_rows, int rows_per_group, int64_t k, int group, int xpg,
-                    cudaStream_t stream, int gate_up, int x_f16);
+                    cudaStream_t stream, int gate_up, int x_f16, const int32_t *gate = nullptr, int gate_max = 0);
 }  // namespace gemv
 
 // The grouped expert GEMM (gemm_q4.cu): mode 1 gate|up + SiLU (fp16 out), mode 2 plain (fp32 out).

@@ -34,11 +34,15 @@ __device__ __forceinline__ void st_release_sys(int *p, int v) {
 // The CTA that arrives last at `done` (after every CTA fenced its stores at system scope) raises
 // flag slot `which * world + rank` on every peer to the epoch, re-arms `done` for the next layer and,
 // when `epoch` is given, stores the new epoch (every CTA read the old one before its arrival).
+// The CTA barrier orders the CTA's writes before its thread 0, whose GPU-scope fence and arrival
+// pass them on to the last CTA to arrive (the grid-barrier pattern: fences are cumulative); that
+// CTA's one system-scope fence and store-release then publish every CTA's writes to the peers. A
+// system-scope fence in every thread serialised thousands of them (15 us for a handful of rows).
 __device__ void signal_peers(int *const *peer_flags, int which, int world, int rank, int e, int *done,
                              int *epoch = nullptr) {
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence();
     if (atomicAdd(done, 1) == static_cast<int>(gridDim.x) - 1) {
       *done = 0;
       if (epoch) *epoch = e;

@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
                                                               int32_t *__restrict__ offsets, int32_t *__restrict__ order,
                                                               int32_t *__restrict__ slot_of, int32_t *__restrict__ tiles,
                                                               int32_t *__restrict__ ntiles, int32_t *__restrict__ local,
-                                                              int cap, FlagWait wait = FlagWait()) {
+                                                              int cap, FlagWait wait = FlagWait(), int small_limit = 0) {
   wait_flags(wait);  // an expert-parallel owner: the senders' rows and ids have arrived
   extern __shared__ int32_t sh[];
   int32_t *warp_cnt = sh;                    // [32 warps][experts]: pairs of the warp's range, then their start
@@ -158,7 +158,8 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
       start[experts] = run;
       offsets[experts] = run;
       tstart[experts] = trun;
-      if (ntiles) *ntiles = trun;
+      // small_limit: at most that many kept pairs run on the per-pair GEMVs, so no tile is handed out
+      if (ntiles) *ntiles = small_limit > 0 && run <= small_limit ? 0 : trun;
     }
   }
   __syncthreads();
@@ -247,6 +248,24 @@ __global__ void gather_kernel(const void *__restrict__ x, int x_f16, const int32
     }
     if (perm) out = perm8(out);
     *reinterpret_cast<uint4 *>(xg + static_cast<size_t>(s) * d + c) = out;
+  }
+}
+
+// ---- the per-pair path of an expert-parallel owner: the first pairs of the grouped order, compacted --
+// For s < n_out: xs[s] = rows[order[s]] (fp16, natural k order) and cid[s] = ids[order[s]] when s < *valid,
+// cid[s] = -1 after. Does nothing when *valid > n_out (the grouped products have the work).
+__global__ void small_gather_kernel(const __half *__restrict__ rows, const int32_t *__restrict__ order,
+                                    const int32_t *__restrict__ ids, const int32_t *__restrict__ valid, int n_out, int d,
+                                    __half *__restrict__ xs, int32_t *__restrict__ cid) {
+  const int nv = *valid;
+  if (nv > n_out) return;
+  const int vec = d / 8;
+  for (int it = blockIdx.x * blockDim.x + threadIdx.x; it < n_out * vec; it += gridDim.x * blockDim.x) {
+    const int s = it / vec, c = (it % vec) * 8;
+    if (c == 0) cid[s] = s < nv ? ids[order[s]] : -1;
+    if (s < nv)
+      *reinterpret_cast<uint4 *>(xs + static_cast<size_t>(s) * d + c) =
+          *reinterpret_cast<const uint4 *>(rows + static_cast<size_t>(order[s]) * d + c);
   }
 }
 
@@ -476,7 +495,8 @@ inline size_t align_up(size_t v) { return (v + 255) / 256 * 256; }
 inline Work carve(uint8_t *base, int64_t tokens, int experts, int topk, int64_t d, int64_t fe) {
   Work w{};
   const int64_t P = tokens * topk;
-  w.max_tiles = static_cast<int>(experts + (P + kTileM - 1) / kTileM);
+  // tiles = sum over the touched experts of ceil(count / kTileM) <= touched + P / kTileM, touched <= min(experts, P)
+  w.max_tiles = static_cast<int>(std::min<int64_t>(experts, P) + (P + kTileM - 1) / kTileM);
   size_t off = 0;
   auto take = [&](size_t bytes) {
     uint8_t *p = base ? base + off : nullptr;
@@ -597,8 +617,20 @@ extern "C" int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, co
   return mq_moe_combine(z, slot_of, weights, tokens, topk, d, add, y, s);
 }
 
+namespace mq {
+namespace moe {
+constexpr int kEpSmall = 16;  // an owner with at most this many pairs runs them on per-pair GEMVs
+// The per-pair path's buffers after the layer's workspace: compacted rows [kEpSmall][d] fp16, their
+// expert ids [kEpSmall], SwiGLU outputs [kEpSmall][fe] fp32.
+inline size_t ep_small_bytes(int64_t d, int64_t fe) {
+  return align_up(kEpSmall * d * 2) + align_up(kEpSmall * 4) + align_up(kEpSmall * fe * 4);
+}
+}  // namespace moe
+}  // namespace mq
+
 extern "C" size_t mq_ep_workspace_size(int64_t rows, int experts, int64_t d, int64_t fe) {
-  return mq_moe_workspace_size(rows, experts, 1, d, fe);
+  if (rows <= 0 || experts <= 0 || d <= 0 || fe <= 0) return 0;
+  return mq_moe_workspace_size(rows, experts, 1, d, fe) + mq::moe::ep_small_bytes(d, fe);
 }
 
 extern "C" int mq_ep_expert_step(const uint16_t *rows, const int32_t *ids, const uint32_t *gu_wq, const uint16_t *gu_ws,
@@ -613,22 +645,65 @@ extern "C" int mq_ep_expert_step(const uint16_t *rows, const int32_t *ids, const
   MQ_REQUIRE(experts >= 1 && experts <= 256 && d % 256 == 0 && fe % 256 == 0, MQ_EINVAL,
              "mq_ep_expert_step: bad experts, d or fe");
   const mq::moe::Work need = mq::moe::carve(nullptr, nrows, experts, 1, d, fe);
-  MQ_REQUIRE(workspace && workspace_bytes >= need.bytes && mq::aligned(workspace, 256), MQ_EINVAL,
-             "mq_ep_expert_step: needs a 256-byte aligned workspace of %zu bytes", need.bytes);
+  const size_t total = need.bytes + mq::moe::ep_small_bytes(d, fe);
+  MQ_REQUIRE(workspace && workspace_bytes >= total && mq::aligned(workspace, 256), MQ_EINVAL,
+             "mq_ep_expert_step: needs a 256-byte aligned workspace of %zu bytes", total);
   const mq::moe::Work w = mq::moe::carve(static_cast<uint8_t *>(workspace), nrows, experts, 1, d, fe);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The received rows hold at most a few real pairs when the layer carries a few tokens (decode):
-  // the GEMVs skip the empty slots (id -1) without reading weights, so they serve up to 64 slots.
-  const float *z = nullptr;
-  const int32_t *slot_of = nullptr;
-  mq::FlagWait wait;  // the senders' rows: the first kernel waits for them
+  // Both paths of the layer are on the stream, chosen on the device by the number of pairs that
+  // arrived (the host cannot know it): the grouping hands out no tiles when at most kEpSmall pairs
+  // came (the grouped products then exit at once), and the per-pair GEMVs exit when more came. A few
+  // pairs (decode) thus cost per-pair GEMVs over only the real rows; many cost the tensor-core tiles.
+  using mq::moe::kEpSmall;
+  const int64_t P = nrows;
+  mq::FlagWait wait;  // the senders' rows: the grouping (the first kernel) waits for them
   wait.flags = flags;
   wait.which = 0;
   wait.world = world;
   wait.epoch = epoch;
-  if (int rc = mq::moe::experts(rows, MQ_F16, ids, gu_wq, gu_ws, dn_wq, dn_ws, nrows, experts, 1, d, fe, group, w, s,
-                                64, &z, &slot_of, wait))
+  const int32_t *valid = w.offsets + experts;
+  mq::DeviceInfo dev;
+  if (int rc = mq::device_info(&dev)) return rc;
+  {
+    const size_t smem = (32 * experts + 2 * (experts + 1)) * sizeof(int32_t);
+    mq::moe::group_kernel<<<1, mq::moe::kGroupThreads, smem, s>>>(ids, 1, static_cast<int>(P), experts,
+                                                                  mq::moe::kTileM, w.counts, w.offsets, w.order,
+                                                                  w.slot_of, w.tiles, w.ntiles, nullptr, 0, wait,
+                                                                  kEpSmall);
+    if (int rc = mq::check_launch("mq_ep_expert_step group")) return rc;
+  }
+  // per-pair path: its buffers after the layer's workspace
+  uint8_t *small = static_cast<uint8_t *>(workspace) + need.bytes;
+  __half *xs = reinterpret_cast<__half *>(small);
+  int32_t *cid = reinterpret_cast<int32_t *>(small + mq::moe::align_up(kEpSmall * d * 2));
+  float *a32 = reinterpret_cast<float *>(small + mq::moe::align_up(kEpSmall * d * 2) + mq::moe::align_up(kEpSmall * 4));
+  mq::moe::small_gather_kernel<<<mq::moe::grid_for(std::min<int64_t>(kEpSmall, P) * (d / 8), 256, dev), 256, 0, s>>>(
+      reinterpret_cast<const __half *>(rows), w.order, ids, valid, static_cast<int>(std::min<int64_t>(kEpSmall, P)),
+      static_cast<int>(d), xs, cid);
+  if (int rc = mq::check_launch("mq_ep_expert_step small gather")) return rc;
+  const int nsmall = static_cast<int>(std::min<int64_t>(kEpSmall, P));
+  if (int rc = mq::gemv::gemv_q4_grouped(gu_wq, gu_ws, experts * 2 * fe, xs, a32, cid, nsmall, static_cast<int>(2 * fe),
+                                         static_cast<int>(fe), d, group, 1, s, 1, 1, valid, nsmall))
     return rc;
+  if (int rc = mq::gemv::gemv_q4_grouped(dn_wq, dn_ws, experts * d, a32, w.z, cid, nsmall, static_cast<int>(d),
+                                         static_cast<int>(d), fe, group, 1, s, 0, 0, valid, nsmall))
+    return rc;
+  if (P <= kEpSmall) {  // never more than kEpSmall pairs: the grouped path has nothing to do
+    return mq_ep_return(w.z, w.slot_of, ids, d, world, rank, cap, peer_ret, peer_flags, epoch, done, s);
+  }
+  // grouped path (no tiles when the per-pair path ran): activations in the products' k order
+  mq::moe::gather_kernel<<<mq::moe::grid_for(P * (d / 8), 256, dev), 256, 0, s>>>(
+      rows, 1, w.order, static_cast<int>(P), 1, static_cast<int>(d), w.xg, 1, valid);
+  if (int rc = mq::check_launch("mq_ep_expert_step gather")) return rc;
+  if (int rc = mq::moe_gemm_run(1, gu_wq, gu_ws, reinterpret_cast<const uint16_t *>(w.xg), P, d, experts, 2 * fe, group,
+                                w.tiles, w.ntiles, w.max_tiles, mq::moe::kTileM, w.a, s, 1))
+    return rc;
+  if (int rc = mq::moe_gemm_run(2, dn_wq, dn_ws, reinterpret_cast<const uint16_t *>(w.a), P, fe, experts, d, group,
+                                w.tiles, w.ntiles, w.max_tiles, mq::moe::kTileM, w.z, s, 1))
+    return rc;
+  // both paths leave the outputs at the pairs' grouped positions (slot_of)
+  const float *z = w.z;
+  const int32_t *slot_of = w.slot_of;
   return mq_ep_return(z, slot_of, ids, d, world, rank, cap, peer_ret, peer_flags, epoch, done, s);
 }
 

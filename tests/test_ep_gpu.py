@@ -83,6 +83,26 @@ def test_ep_single_rank_device_path(cuda, max_tokens):
     assert normwise(y.cpu().numpy(), ref) <= 1e-3
 
 
+@pytest.mark.parametrize("tokens", [1, 2, 3])
+def test_ep_peer_small_and_grouped_owner_paths(cuda, tokens):
+    """The peer form's owner step picks its path on the device: at most 16 received pairs run on the
+    per-pair GEMVs over the compacted rows (1 and 2 tokens), more on the grouped products (3 tokens =
+    24 pairs); both against the fp64 oracle, twice in a row."""
+    m = synth.moe_layer(seed=10 + tokens, tokens=tokens)
+    ids, w = omoe.route(m["logits"], 8)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a.view(np.int32) if a.dtype == np.uint32 else a)).to(cuda)
+    moe = mq.ExpertParallelMoE(t(m["gu_wq"]), t(m["gu_ws"]), t(m["dn_wq"]), t(m["dn_ws"]), 2048, 768, 128,
+                               max_tokens=tokens)
+    assert moe.exchange == "peer"
+    ref = omoe.moe_layer(m["x"], ids, w, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 32, 768)
+    for _ in range(2):
+        y = torch.full((tokens, 2048), float("nan"), device=cuda)
+        moe(t(m["x"]), t(ids), t(w), y)
+        torch.cuda.synchronize()
+        assert mq.device_status() == 0
+        assert normwise(y.cpu().numpy(), ref) <= 1e-3
+
+
 def _port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
