@@ -193,10 +193,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.scales_tma) prefetch_tmap(&smap);
   }
   __syncwarp();
-  // The first S weight tiles of each warp go out before the dependency wait: the only kernels that let
-  // this one start before they finish (this library's GEMV and GEMM kernels) write their outputs, never
-  // weights, and any other kernel finishes before this one starts, so the weights are final.
-  for (int s = 0; s < S; ++s) issue(s);
+  // In a launch of one round per CTA (latency-bound) the first S weight tiles of each warp go out
+  // before the dependency wait: the only kernels that let this one start before they finish (this
+  // library's GEMV and GEMM kernels) write their outputs, never weights, and any other kernel finishes
+  // before this one starts, so the weights are final (12288 x 4096: 7.6 -> 7.0 us). Multi-round
+  // launches (the head) keep the loads after the staging, which measured faster there.
+  const bool pre = p.nrounds <= static_cast<int>(gridDim.x);
+  if (pre)
+    for (int s = 0; s < S; ++s) issue(s);
   griddep_wait();  // everything above only read weights
 
   uint2 *bfrag = reinterpret_cast<uint2 *>(smem + L.bfrag);  // [K/32 steps][2 NB][4]
@@ -212,6 +216,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // codes h * 2 + 4i and h * 2 + 1 + 4i) lane q' of column 2t + l holds limb l of x at those codes of
   // word row 4b + q'.
   const int nrow = K / 16;
+  // Without the early loads: warps with no staging item issue their first loads now (they would only
+  // wait at the staging barrier); the others after it, so that lane 0's TMA holds do not delay the
+  // barrier. When every warp stages (long K), all issue now: the loads then cover the longer staging.
+  const bool early = 32 * warp >= NB * nrow || NB * nrow >= kThreads;
+  if (!pre && early)
+    for (int s = 0; s < S; ++s) issue(s);
   for (int base = 0; base < NB * nrow; base += kThreads) {
     const int it = base + threadIdx.x;
     const bool live = it < NB * nrow;
@@ -276,6 +286,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
 
+  if (!pre && !early)
+    for (int s = 0; s < S; ++s) issue(s);
 
   const int g = lane >> 2, q = lane & 3;
   const bool act = g < 2 * NB;                // columns (token g / 2, limb g % 2) in use
