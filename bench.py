@@ -524,7 +524,9 @@ def device_route(mq, logits, dev, topk=8):
 
 def moe_bench(mq, synth, dev, stream, world, rank):
     """Tokens/s of the MoE layer (routing given, computed once on the device) with every expert on
-    this GPU."""
+    this GPU. Each CUDA graph holds several layers in a row, as a model's graph does, so the time per
+    layer carries no host launch cost; the layers cycle through enough copies of the expert weights
+    that the experts a layer touches are never found in L2."""
     out = {}
     for tokens in (404, 1):
         m = synth.moe_layer(seed=0, tokens=tokens)
@@ -533,27 +535,30 @@ def moe_bench(mq, synth, dev, stream, world, rank):
         ids = tids.cpu().numpy()
         gw = [torch.from_numpy(m[k].view(np.int32) if m[k].dtype == np.uint32 else m[k]).to(dev)
               for k in ("gu_wq", "gu_ws", "dn_wq", "dn_ws")]
-        wbytes = sum(a.numel() * a.element_size() for a in gw)
-        copies = rotating_copies(wbytes)
+        used = np.unique(ids)
+        active_bytes = len(used) * (1536 * 2048 + 2048 * 768) * 9 // 16  # int4 + fp16 scales per G=32
+        copies = rotating_copies(active_bytes)
         gws = [gw] + [[a.clone() for a in gw] for _ in range(copies - 1)]
         y = torch.zeros(tokens, 2048, device=dev)
         ws = torch.empty(mq.lib.mq_moe_workspace_size(tokens, 128, 8, 2048, 768), dtype=torch.uint8, device=dev)
-        graphs = [graph_of(lambda c=c: mq.moe_forward(tx, tids, tw, *gws[c], y, 2048, 768, group=32, workspace=ws))
-                  for c in range(copies)]
-        ms = max_over_ranks(time_graphs(graphs, 50, stream), world)
-        used = np.unique(ids)
-        active_bytes = len(used) * (1536 * 2048 + 2048 * 768) * 9 // 16  # int4 + fp16 scales per G=32
+        layers = max(copies, 8)
+        g = graph_of(lambda: [mq.moe_forward(tx, tids, tw, *gws[i % copies], y, 2048, 768, group=32, workspace=ws)
+                              for i in range(layers)])
+        ms = max_over_ranks(time_graphs([g], 10, stream) / layers, world)
         # the router (fp32 [128, 2048] GEMV) and routing on the device, timed on their own
         rw = torch.from_numpy((np.random.default_rng(5).standard_normal((128, 2048)) * 0.02).astype(np.float32)).to(dev)
         rl = torch.empty(tokens, 128, device=dev)
         rids = torch.empty(tokens, 8, dtype=torch.int32, device=dev)
         rwts = torch.empty(tokens, 8, device=dev)
-        router_ms = max_over_ranks(time_graphs([graph_of(lambda: mq.router(rw, tx, rids, rwts, 8, rl))], 50, stream), world)
+        reps = 20
+        gr = graph_of(lambda: [mq.router(rw, tx, rids, rwts, 8, rl) for _ in range(reps)])
+        router_ms = max_over_ranks(time_graphs([gr], 10, stream) / reps, world)
         out[f"tokens_{tokens}"] = {"ms": round(ms, 5), "tokens/s": round(tokens / (ms * 1e-3), 1),
                                    "router_and_route_ms": round(router_ms, 5),
                                    "experts_touched": int(len(used)),
-                                   "expert_weight_GB/s": round(active_bytes / (ms * 1e-3) / 1e9, 1)}
-        del graphs, gws
+                                   "expert_weight_GB/s": round(active_bytes / (ms * 1e-3) / 1e9, 1),
+                                   "timing": f"{layers} layers per CUDA graph over {copies} weight copies"}
+        del g, gr, gws
     return out
 
 
@@ -576,10 +581,17 @@ def moe_bench_ep(mq, synth, dev, stream, world, rank, steps=50):
                  m["dn_ws"][lo * d:hi * d])
         gw = [torch.from_numpy(np.ascontiguousarray(a.view(np.int32) if a.dtype == np.uint32 else a)).to(dev)
               for a in parts]
-        copies = rotating_copies(sum(a.numel() * a.element_size() for a in gw))
+        # Enough weight copies that the experts a layer touches on any rank are never found in L2 (the
+        # same count on every rank: the global routing is known to all of them).
+        used = np.unique(device_route(mq, m["logits"], dev, topk)[0].cpu().numpy())
+        per_expert = (2 * fe * d + d * fe) * 9 // 16  # int4 + fp16 scales per G=32
+        copies = max(rotating_copies(max(1, int(np.sum((used >= r * experts // world) & (used < (r + 1) * experts // world))))
+                                     * per_expert) for r in range(world))
         gws = [gw] + [[a.clone() for a in gw] for _ in range(copies - 1)]
         max_tokens = max(hi_ - lo_ for lo_, hi_ in (shard(tokens, world, r) for r in range(world)))
-        layers = [mq.ExpertParallelMoE(*g, d, fe, experts, topk=topk, group=32, max_tokens=max_tokens) for g in gws]
+        layers = [mq.ExpertParallelMoE(*gws[0], d, fe, experts, topk=topk, group=32, max_tokens=max_tokens)]
+        layers += [mq.ExpertParallelMoE(*g, d, fe, experts, topk=topk, group=32, max_tokens=max_tokens, share=layers[0])
+                   for g in gws[1:]]
         tx = torch.from_numpy(np.ascontiguousarray(m["x"][lo_t:hi_t])).to(dev)
         if hi_t > lo_t:
             tids, tw = device_route(mq, np.ascontiguousarray(m["logits"][lo_t:hi_t]), dev)
@@ -629,19 +641,22 @@ def moe_bench_ep(mq, synth, dev, stream, world, rank, steps=50):
         names = ("plan", "dispatch", "wait_rows_experts_and_return", "wait_returns_and_combine")
         phases = {nm: round(a * 1e3, 2) for nm, a in zip(names, acc)}
         del gph
-        # the layer as a CUDA graph, one per weight copy, replayed back to back
-        graphs = [graph_of(lambda L=L: L(tx, tids, tw, y)) for L in layers]
-        for i in range(3):
-            graphs[i % copies].replay()
+        # several layers in a row as one CUDA graph (as a model's graph holds them), cycling through the
+        # weight copies, replayed back to back
+        nl = max(copies, 8)
+        graph = graph_of(lambda: [layers[i % copies](tx, tids, tw, y) for i in range(nl)])
+        for i in range(2):
+            graph.replay()
         torch.cuda.synchronize()
         barrier(world)
+        reps = max(2, steps // nl)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for i in range(steps):
-            graphs[i % copies].replay()
+        for i in range(reps):
+            graph.replay()
         e1.record(stream)
         torch.cuda.synchronize()
-        ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+        ms = max_over_ranks(e0.elapsed_time(e1) / (reps * nl), world)
         status = int(max_over_ranks(float(mq.device_status()), world))
         err = 0.0
         if hi_t > lo_t:
@@ -655,9 +670,10 @@ def moe_bench_ep(mq, synth, dev, stream, world, rank, steps=50):
                                    "phases_us": phases, "parity_normwise_max_over_ranks": err,
                                    "parallelism": f"expert-parallel x{world} ({experts // world} experts per GPU), "
                                                   "peer-memory dispatch and return over NVLink (no NCCL on the data "
-                                                  f"path), capacity {max_tokens * topk} rows per rank pair, "
-                                                  "the layer replayed as a CUDA graph"}
-        del graphs
+                                                  f"path), capacity {max_tokens * topk} rows per rank pair",
+                                   "timing": f"{nl} layers per CUDA graph over {copies} weight copies, max over ranks; "
+                                             "phases from one layer's graph with events between its steps"}
+        del graph
         torch.cuda.synchronize()
         barrier(world)
         for L in layers:

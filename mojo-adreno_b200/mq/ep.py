@@ -152,10 +152,13 @@ class ExpertParallelMoE:
     [E_local * 2fe, d/8], down [E_local * d, fe/8], fp16 scales per `group`. `experts` is the
     layer's total. forward(x, ids, weights, y) takes this rank's tokens: x [T, d] fp32 or fp16, ids
     int32 and weights fp32 [T, topk] from the router, and writes (or adds into) y fp32 [T, d].
+    share: another layer of the same shape (peer exchange) whose peer buffers and workspace this
+    layer uses too -- the layers of a model run one after another on the stream, so one set of
+    buffers serves them all; only the layer that made the buffers unmaps them (close).
     """
 
     def __init__(self, gu_wq, gu_ws, dn_wq, dn_ws, d, fe, experts, topk=8, group=32, pg=None, ops=None,
-                 max_tokens=None, exchange=None):
+                 max_tokens=None, exchange=None, share=None):
         self.pg = pg
         self.world = dist.get_world_size(pg) if dist.is_initialized() else 1
         self.rank = dist.get_rank(pg) if dist.is_initialized() else 0
@@ -177,11 +180,19 @@ class ExpertParallelMoE:
                 raise MQError(-1, "the peer exchange needs max_tokens and the device ops")
             dev = gu_wq.device
             self.local_experts = local
-            self.peer = PeerBuffers(self.world, self.rank, self.capacity, d, dev, pg)
             rows = self.world * self.capacity
-            nbytes = lib.mq_ep_workspace_size(rows, local, d, fe)
-            self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-            self.empty_plan = torch.full((rows,), -1, dtype=torch.int32, device=dev)
+            if share is not None:
+                if (share.exchange != "peer" or share.capacity != self.capacity or share.d != d or share.fe != fe
+                        or share.local_experts != local or share.world != self.world):
+                    raise MQError(-1, "share: the other layer must be a peer-exchange layer of the same shape")
+                self.peer, self.workspace, self.empty_plan = share.peer, share.workspace, share.empty_plan
+                self.owns_peer = False
+            else:
+                self.peer = PeerBuffers(self.world, self.rank, self.capacity, d, dev, pg)
+                nbytes = lib.mq_ep_workspace_size(rows, local, d, fe)
+                self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+                self.empty_plan = torch.full((rows,), -1, dtype=torch.int32, device=dev)
+                self.owns_peer = True
 
     def _a2a(self, out, inp, out_splits, in_splits):
         if self.world == 1:
@@ -281,7 +292,7 @@ class ExpertParallelMoE:
 
     def close(self):
         """Unmaps the peers' buffers (call on every rank after the last layer, before the process group ends)."""
-        if self.exchange == "peer":
+        if self.exchange == "peer" and self.owns_peer:
             self.peer.close()
 
     __call__ = forward
