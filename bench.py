@@ -553,12 +553,21 @@ def moe_bench(mq, synth, dev, stream, world, rank):
         reps = 20
         gr = graph_of(lambda: [mq.router(rw, tx, rids, rwts, 8, rl) for _ in range(reps)])
         router_ms = max_over_ranks(time_graphs([gr], 10, stream) / reps, world)
+        # the fused chain: router GEMV + top-k + softmax in one cluster kernel, then the grouping
+        gf = graph_of(lambda: [mq.route_group(rw, tx, rids, rwts, 8, group=tokens * 8 > 16) for _ in range(reps)])
+        fused_ms = max_over_ranks(time_graphs([gf], 10, stream) / reps, world)
+        # the whole layer with its router (mq_moe_layer): routing, grouping and experts
+        gl = graph_of(lambda: [mq.moe_layer(tx, rw, *gws[i % copies], y, 2048, 768, group=32, ids=rids, weights=rwts,
+                                            workspace=ws) for i in range(layers)])
+        layer_ms = max_over_ranks(time_graphs([gl], 10, stream) / layers, world)
         out[f"tokens_{tokens}"] = {"ms": round(ms, 5), "tokens/s": round(tokens / (ms * 1e-3), 1),
                                    "router_and_route_ms": round(router_ms, 5),
+                                   "router_route_and_grouping_fused_ms": round(fused_ms, 5),
+                                   "layer_with_router_ms": round(layer_ms, 5),
                                    "experts_touched": int(len(used)),
                                    "expert_weight_GB/s": round(active_bytes / (ms * 1e-3) / 1e9, 1),
                                    "timing": f"{layers} layers per CUDA graph over {copies} weight copies"}
-        del g, gr, gws
+        del g, gr, gf, gl, gws
     return out
 
 

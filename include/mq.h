@@ -204,6 +204,20 @@ MQ_API int mq_moe_group(const int32_t *ids, int64_t tokens, int topk, int expert
                         int32_t *offsets, int32_t *order, int32_t *slot_of, int32_t *tiles, int32_t *ntiles,
                         void *stream);
 
+/* The router chain fused: mq_moe_router, mq_moe_route and (counts != NULL) mq_moe_group in two
+ * launches. A cluster of 8 CTAs computes the router logits of 16 tokens (each CTA an eighth of the
+ * experts), keeps them in shared memory and routes each token from the cluster's distributed shared
+ * memory; the grouping follows as a programmatic dependent launch. ids and weights are those of
+ * mq_moe_route on the logits this chain computes, and the grouping that of mq_moe_group on those
+ * ids. logits (may be NULL): receives the router logits [tokens][experts]. Replaces gemv_f32 + route
+ * + p_expert_lists / p_expert_items (qwen3moe/kernels/moek.mojo:143-197, 432-442, 548-557).
+ * experts <= 256, topk <= 32, d % 4 == 0; w and x 16-byte aligned. counts == NULL skips the grouping
+ * (the other grouping outputs are then ignored). */
+MQ_API int mq_moe_route_group(const float *w, const float *x, float *logits, int32_t *ids, float *weights,
+                              int64_t tokens, int experts, int topk, int64_t d, int tile, int32_t *counts,
+                              int32_t *offsets, int32_t *order, int32_t *slot_of, int32_t *tiles, int32_t *ntiles,
+                              void *stream);
+
 /* Expert-parallel dispatch plan: experts are split into `world` equal contiguous ranges, range r owned
  * by rank r. The tokens * topk pairs are grouped stably by owning rank: counts[r], offsets[r]
  * (offsets[world] = pairs), order[offsets[r] + i] = the i-th pair sent to rank r, slot_of[pair] = its
@@ -266,6 +280,16 @@ MQ_API int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, const 
                           const uint16_t *gu_ws, const uint32_t *dn_wq, const uint16_t *dn_ws, float *y, int64_t tokens,
                           int experts, int topk, int64_t d, int64_t fe, int group, int add, void *workspace,
                           size_t workspace_bytes, void *stream);
+
+/* The MoE layer with its router on the device, as the model runs it (qwen3moe/model.mojo:208-274:
+ * gemv_f32 router, route, the experts): the fused router chain (mq_moe_route_group) writes ids,
+ * weights (and logits, when not NULL) and the grouping into the workspace, then the layer runs as
+ * mq_moe_forward does on those ids. x fp32 [tokens][d]; router_w fp32 [experts][d]; the workspace
+ * is mq_moe_workspace_size(tokens, experts, topk, d, fe) bytes, 256-byte aligned. */
+MQ_API int mq_moe_layer(const float *x, const float *router_w, const uint32_t *gu_wq, const uint16_t *gu_ws,
+                        const uint32_t *dn_wq, const uint16_t *dn_ws, float *y, int32_t *ids, float *weights,
+                        float *logits, int64_t tokens, int experts, int topk, int64_t d, int64_t fe, int group, int add,
+                        void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---- expert parallelism over NVLink peer memory ------------------------------------------------------
  * No counterpart in the reference, which runs every expert on one device (qwen3moe/model.mojo:256-267).

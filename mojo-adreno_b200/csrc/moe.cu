@@ -16,18 +16,11 @@ namespace moe {
 // ---- routing: one warp per token -----------------------------------------------------------
 // Top-k experts by logit (the lowest index among equals), then softmax over the k chosen logits
 // (max-subtracted, fp32), as route / p_route compute it. E <= 256 (each lane holds E / 32 logits).
-template <int PER>  // logits per lane
-__global__ void route_kernel(const float *__restrict__ logits, int32_t *__restrict__ ids, float *__restrict__ weights,
-                             int tokens, int experts, int topk) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
-  if (warp >= tokens) return;
-  const float *lg = logits + static_cast<size_t>(warp) * experts;
-  float v[PER];
-#pragma unroll
-  for (int i = 0; i < PER; ++i) {
-    const int e = i * 32 + lane;
-    v[i] = e < experts ? lg[e] : -INFINITY;
-  }
+// One token's routing by one warp: v[i] is the logit of expert i * 32 + lane (-inf past experts).
+// route_kernel and the fused router chain (route_group_kernel) both use it, so the two route alike.
+template <int PER>
+__device__ __forceinline__ void route_row(float (&v)[PER], int lane, int experts, int topk, int32_t *__restrict__ ids_row,
+                                          float *__restrict__ weights_row) {
   float top[32];
   int32_t idx[32];
   for (int k = 0; k < topk; ++k) {
@@ -60,10 +53,25 @@ __global__ void route_kernel(const float *__restrict__ logits, int32_t *__restri
     float total = 0.f;
     for (int k = 0; k < topk; ++k) total += expf(top[k] - top[0]);
     for (int k = 0; k < topk; ++k) {
-      ids[static_cast<size_t>(warp) * topk + k] = idx[k];
-      weights[static_cast<size_t>(warp) * topk + k] = expf(top[k] - top[0]) / total;
+      ids_row[k] = idx[k];
+      weights_row[k] = expf(top[k] - top[0]) / total;
     }
   }
+}
+
+template <int PER>  // logits per lane
+__global__ void route_kernel(const float *__restrict__ logits, int32_t *__restrict__ ids, float *__restrict__ weights,
+                             int tokens, int experts, int topk) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  if (warp >= tokens) return;
+  const float *lg = logits + static_cast<size_t>(warp) * experts;
+  float v[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = i * 32 + lane;
+    v[i] = e < experts ? lg[e] : -INFINITY;
+  }
+  route_row<PER>(v, lane, experts, topk, ids + static_cast<size_t>(warp) * topk, weights + static_cast<size_t>(warp) * topk);
 }
 
 // ---- grouping: a stable counting sort of the (token, slot) pairs by expert, one CTA ---------
@@ -86,6 +94,7 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
                                                               int32_t *__restrict__ slot_of, int32_t *__restrict__ tiles,
                                                               int32_t *__restrict__ ntiles, int32_t *__restrict__ local,
                                                               int cap, FlagWait wait = FlagWait(), int small_limit = 0) {
+  griddep_wait();    // launched behind the fused router (programmatic dependent launch): its ids are written
   wait_flags(wait);  // an expert-parallel owner: the senders' rows and ids have arrived
   extern __shared__ int32_t sh[];
   int32_t *warp_cnt = sh;                    // [32 warps][experts]: pairs of the warp's range, then their start
@@ -226,6 +235,7 @@ __device__ __forceinline__ uint4 perm8(uint4 v) {  // halves 0..7 -> 0, 4, 1, 5,
 __global__ void gather_kernel(const void *__restrict__ x, int x_f16, const int32_t *__restrict__ order, int pairs,
                               int topk, int d, __half *__restrict__ xg, int perm = 0, const int32_t *valid = nullptr,
                               FlagWait wait = FlagWait()) {
+  griddep_wait();    // launched behind the fused router (programmatic dependent launch): its ids are written
   wait_flags(wait);  // an expert-parallel owner: the senders' rows and ids have arrived
   const int vec = d / 8;  // 8 values per thread step
   const int64_t n = static_cast<int64_t>(valid ? min(*valid, pairs) : pairs) * vec;
@@ -374,6 +384,119 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const float *__r
     }
 }
 
+// ---- the fused router chain: router GEMV + top-k + softmax in one cluster kernel -------------
+// A cluster of 8 CTAs takes kRgTokens tokens; CTA r computes the logits of experts
+// [r * epc, (r + 1) * epc) (epc = ceil(E / 8) <= 32) for them, keeps them in its shared memory,
+// and after a cluster barrier each token is routed by one warp that reads its E logits from the
+// eight CTAs' shared memory (distributed shared memory), so the logits never round-trip through
+// global memory (they are written out only when asked for). The grouping (group_kernel) follows as
+// a programmatic dependent launch. The router follows gemv_f32 / p_gemv_f32 (moek.mojo:143-153,
+// 284-295), the routing route / p_route (moek.mojo:156-197, 385-425).
+constexpr int kRgCluster = 8, kRgThreads = 256, kRgTokens = 16, kRgChunk = 512;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster: shared-memory writes before it are visible to the
+// cluster's reads after it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// A float at the same shared-memory offset as `p` in CTA `rank` of this cluster.
+__device__ __forceinline__ float ld_cluster_f32(const float *p, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(p)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+template <int EPW, int PER>  // experts per warp (epc <= 8 * EPW), logits per lane in routing (E <= 32 * PER)
+__global__ void __cluster_dims__(kRgCluster, 1, 1) __launch_bounds__(kRgThreads)
+    route_group_kernel(const float *__restrict__ w, const float *__restrict__ x, float *__restrict__ logits,
+                       int32_t *__restrict__ ids, float *__restrict__ weights, int tokens, int experts, int topk, int d) {
+  constexpr int kPass = EPW < 2 ? EPW : 2;  // experts a warp accumulates at once (more passes re-read x)
+  __shared__ __align__(16) float xs[kRgTokens][kRgChunk];
+  __shared__ float lg[kRgTokens][32];  // this CTA's experts' logits
+  const uint32_t rank = cluster_ctarank();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int t0 = static_cast<int>(blockIdx.x / kRgCluster) * kRgTokens;
+  const int epc = (experts + kRgCluster - 1) / kRgCluster, e_lo = static_cast<int>(rank) * epc;
+  griddep_launch_dependents();
+  griddep_wait();  // x may come from the previous kernel on the stream
+#pragma unroll 1
+  for (int pass = 0; pass < EPW / kPass; ++pass) {
+    float acc[kPass][kRgTokens];
+#pragma unroll
+    for (int j = 0; j < kPass; ++j)
+#pragma unroll
+      for (int t = 0; t < kRgTokens; ++t) acc[j][t] = 0.f;
+    for (int k0 = 0; k0 < d; k0 += kRgChunk) {
+      const int kn = min(kRgChunk, d - k0);
+      __syncthreads();
+      for (int i = threadIdx.x; i < kRgTokens * kRgChunk / 4; i += kRgThreads) {
+        const int t = i / (kRgChunk / 4), k = (i % (kRgChunk / 4)) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t0 + t < tokens && k < kn) v = *reinterpret_cast<const float4 *>(x + static_cast<size_t>(t0 + t) * d + k0 + k);
+        *reinterpret_cast<float4 *>(&xs[t][k]) = v;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < kPass; ++j) {
+        const int le = warp + 8 * (pass * kPass + j), e = e_lo + le;
+        const bool live = le < epc && e < experts;
+        const float *wr = w + static_cast<size_t>(live ? e : 0) * d + k0;
+        float4 wv[kRgChunk / 128];
+#pragma unroll
+        for (int q = 0; q < kRgChunk / 128; ++q) {
+          const int k = lane * 4 + 128 * q;
+          wv[q] = live && k < kn ? __ldg(reinterpret_cast<const float4 *>(wr + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int q = 0; q < kRgChunk / 128; ++q) {
+          const int k = lane * 4 + 128 * q;
+#pragma unroll
+          for (int t = 0; t < kRgTokens; ++t) {
+            const float4 xv = *reinterpret_cast<const float4 *>(&xs[t][k]);
+            acc[j][t] = fmaf(wv[q].x, xv.x, fmaf(wv[q].y, xv.y, fmaf(wv[q].z, xv.z, fmaf(wv[q].w, xv.w, acc[j][t]))));
+          }
+        }
+      }
+    }
+    // Each warp sums its lanes in a fixed order; the logits stay in shared memory.
+#pragma unroll
+    for (int j = 0; j < kPass; ++j) {
+      const int le = warp + 8 * (pass * kPass + j), e = e_lo + le;
+#pragma unroll
+      for (int t = 0; t < kRgTokens; ++t) {
+        float v = acc[j][t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0 && le < epc && e < experts) {
+          lg[t][le] = v;
+          if (logits && t0 + t < tokens) logits[static_cast<size_t>(t0 + t) * experts + e] = v;
+        }
+      }
+    }
+  }
+  cluster_sync();
+  // Routing: token t0 + tt by warp tt / 8 of CTA tt % 8, its logits gathered from the eight CTAs.
+  const int tt = static_cast<int>(rank) + kRgCluster * warp;
+  if (tt < kRgTokens && t0 + tt < tokens) {
+    float v[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = i * 32 + lane;
+      v[i] = e < experts ? ld_cluster_f32(&lg[tt][e % epc], static_cast<uint32_t>(e / epc)) : -INFINITY;
+    }
+    route_row<PER>(v, lane, experts, topk, ids + static_cast<size_t>(t0 + tt) * topk,
+                   weights + static_cast<size_t>(t0 + tt) * topk);
+  }
+  cluster_sync();  // no CTA leaves while another may still read its logits
+}
+
 }  // namespace moe
 }  // namespace mq
 
@@ -411,6 +534,54 @@ extern "C" int mq_moe_route(const float *logits, int32_t *ids, float *weights, i
   else
     mq::moe::route_kernel<8><<<grid, threads, 0, s>>>(logits, ids, weights, static_cast<int>(tokens), experts, topk);
   return mq::check_launch("mq_moe_route");
+}
+
+namespace mq {
+namespace moe {
+// The fused router chain on `stream`: route_group_kernel, then (counts != null) group_kernel as a
+// programmatic dependent launch. Shapes are checked by the callers.
+int route_group(const float *w, const float *x, float *logits, int32_t *ids, float *weights, int64_t tokens,
+                int experts, int topk, int64_t d, int tile, int32_t *counts, int32_t *offsets, int32_t *order,
+                int32_t *slot_of, int32_t *tiles, int32_t *ntiles, cudaStream_t s) {
+  const unsigned grid = static_cast<unsigned>((tokens + kRgTokens - 1) / kRgTokens) * kRgCluster;
+  const int epc = (experts + kRgCluster - 1) / kRgCluster;
+  const int ti = static_cast<int>(tokens), ei = experts, di = static_cast<int>(d);
+  int rc;
+  if (epc <= 8)
+    rc = launch_overlapped(route_group_kernel<1, 4>, dim3(grid), dim3(kRgThreads), 0, s, "mq_moe_route_group", w, x,
+                           logits, ids, weights, ti, ei, topk, di);
+  else if (epc <= 16 && experts <= 128)
+    rc = launch_overlapped(route_group_kernel<2, 4>, dim3(grid), dim3(kRgThreads), 0, s, "mq_moe_route_group", w, x,
+                           logits, ids, weights, ti, ei, topk, di);
+  else
+    rc = launch_overlapped(route_group_kernel<4, 8>, dim3(grid), dim3(kRgThreads), 0, s, "mq_moe_route_group", w, x,
+                           logits, ids, weights, ti, ei, topk, di);
+  if (rc || !counts) return rc;
+  const size_t smem = (32 * experts + 2 * (experts + 1)) * sizeof(int32_t);
+  const int32_t *cids = ids;
+  int32_t *no_local = nullptr;
+  return launch_overlapped(group_kernel, dim3(1), dim3(kGroupThreads), smem, s, "mq_moe_route_group (grouping)", cids, 1,
+                           static_cast<int>(tokens * topk), experts, tile, counts, offsets, order, slot_of, tiles, ntiles,
+                           no_local, 0, FlagWait(), 0);
+}
+}  // namespace moe
+}  // namespace mq
+
+extern "C" int mq_moe_route_group(const float *w, const float *x, float *logits, int32_t *ids, float *weights,
+                                  int64_t tokens, int experts, int topk, int64_t d, int tile, int32_t *counts,
+                                  int32_t *offsets, int32_t *order, int32_t *slot_of, int32_t *tiles, int32_t *ntiles,
+                                  void *stream) {
+  MQ_REQUIRE(w && x && ids && weights, MQ_EINVAL, "mq_moe_route_group: null pointer");
+  MQ_REQUIRE(!counts || (offsets && order && slot_of && tiles && ntiles), MQ_EINVAL,
+             "mq_moe_route_group: the grouping outputs are all given or counts is null");
+  MQ_REQUIRE(tokens > 0 && tokens < (1 << 24) && tokens * topk < (1 << 30), MQ_EINVAL, "mq_moe_route_group: bad token count");
+  MQ_REQUIRE(experts >= 1 && experts <= 256, MQ_EINVAL, "mq_moe_route_group: experts must be in 1..256 (got %d)", experts);
+  MQ_REQUIRE(topk >= 1 && topk <= 32 && topk <= experts, MQ_EINVAL, "mq_moe_route_group: topk must be in 1..min(32, experts)");
+  MQ_REQUIRE(d > 0 && d % 4 == 0 && d < (1 << 24), MQ_EINVAL, "mq_moe_route_group: d must be a positive multiple of 4");
+  MQ_REQUIRE(tile >= 1, MQ_EINVAL, "mq_moe_route_group: tile must be >= 1");
+  MQ_REQUIRE(mq::aligned(w, 16) && mq::aligned(x, 16), MQ_EALIGN, "mq_moe_route_group: w and x must be 16-byte aligned");
+  return mq::moe::route_group(w, x, logits, ids, weights, tokens, experts, topk, d, tile, counts, offsets, order,
+                              slot_of, tiles, ntiles, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int mq_moe_group(const int32_t *ids, int64_t tokens, int topk, int experts, int tile, int32_t *counts,
@@ -534,7 +705,7 @@ namespace moe {
 int experts(const void *x, int x_dtype, const int32_t *ids, const uint32_t *gu_wq, const uint16_t *gu_ws,
             const uint32_t *dn_wq, const uint16_t *dn_ws, int64_t tokens, int experts_n, int topk, int64_t d, int64_t fe,
             int group, const Work &w, cudaStream_t s, int64_t small_pairs, const float **z_out,
-            const int32_t **slot_of_out, FlagWait wait = FlagWait()) {
+            const int32_t **slot_of_out, FlagWait wait = FlagWait(), bool grouped = false) {
   const int64_t P = tokens * topk;
   DeviceInfo dev;
   if (int rc = device_info(&dev)) return rc;
@@ -553,7 +724,7 @@ int experts(const void *x, int x_dtype, const int32_t *ids, const uint32_t *gu_w
     *slot_of_out = nullptr;
     return MQ_OK;
   }
-  {
+  if (!grouped) {  // grouped: the fused router chain already wrote the grouping into w
     const size_t smem = (32 * experts_n + 2 * (experts_n + 1)) * sizeof(int32_t);
     group_kernel<<<1, kGroupThreads, smem, s>>>(ids, 1, static_cast<int>(P), experts_n, kTileM, w.counts, w.offsets,
                                                  w.order, w.slot_of, w.tiles, w.ntiles, nullptr, 0, wait);
@@ -613,6 +784,45 @@ extern "C" int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, co
   const int32_t *slot_of = nullptr;
   if (int rc = mq::moe::experts(x, x_dtype, ids, gu_wq, gu_ws, dn_wq, dn_ws, tokens, experts, topk, d, fe, group, w, s,
                                 mq::moe::kSmallPairs, &z, &slot_of))
+    return rc;
+  return mq_moe_combine(z, slot_of, weights, tokens, topk, d, add, y, s);
+}
+
+extern "C" int mq_moe_layer(const float *x, const float *router_w, const uint32_t *gu_wq, const uint16_t *gu_ws,
+                            const uint32_t *dn_wq, const uint16_t *dn_ws, float *y, int32_t *ids, float *weights,
+                            float *logits, int64_t tokens, int experts, int topk, int64_t d, int64_t fe, int group, int add,
+                            void *workspace, size_t workspace_bytes, void *stream) {
+  MQ_REQUIRE(x && router_w && gu_wq && gu_ws && dn_wq && dn_ws && y && ids && weights, MQ_EINVAL, "mq_moe_layer: null pointer");
+  MQ_REQUIRE(tokens > 0 && tokens < (1 << 24) && experts >= 1 && experts <= 256 && topk >= 1 && topk <= 32 && topk <= experts,
+             MQ_EINVAL, "mq_moe_layer: bad tokens / experts / topk");
+  MQ_REQUIRE(d % 256 == 0 && fe % 256 == 0 && d < (1 << 24), MQ_EINVAL, "mq_moe_layer: d and fe must be multiples of 256");
+  MQ_REQUIRE(mq::aligned(x, 16) && mq::aligned(router_w, 16), MQ_EALIGN, "mq_moe_layer: x and router_w must be 16-byte aligned");
+  const mq::moe::Work need = mq::moe::carve(nullptr, tokens, experts, topk, d, fe);
+  MQ_REQUIRE(workspace && workspace_bytes >= need.bytes, MQ_EINVAL, "mq_moe_layer: needs a workspace of %zu bytes (got %zu)",
+             need.bytes, workspace_bytes);
+  MQ_REQUIRE(mq::aligned(workspace, 256), MQ_EALIGN, "mq_moe_layer: workspace must be 256-byte aligned");
+  const mq::moe::Work w = mq::moe::carve(static_cast<uint8_t *>(workspace), tokens, experts, topk, d, fe);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t P = tokens * topk;
+  // The grouping is needed only by the grouped tensor-core products (more than kSmallPairs pairs).
+  const bool grouped = tokens > 1 && P > mq::moe::kSmallPairs;
+  if (int rc = mq::moe::route_group(router_w, x, logits, ids, weights, tokens, experts, topk, d, mq::moe::kTileM,
+                                    grouped ? w.counts : nullptr, w.offsets, w.order, w.slot_of, w.tiles, w.ntiles, s))
+    return rc;
+  if (tokens == 1) {  // decode: the streaming GEMVs over the selected experts' rows (as mq_moe_forward)
+    float *a = reinterpret_cast<float *>(w.a), *z = w.z;
+    if (int rc = mq::gemv::gemv_q4_grouped(gu_wq, gu_ws, experts * 2 * fe, x, a, ids, topk, static_cast<int>(2 * fe),
+                                           static_cast<int>(fe), d, group, 0, s, 1, 0))
+      return rc;
+    if (int rc = mq::gemv::gemv_q4_grouped(dn_wq, dn_ws, experts * d, a, z, ids, topk, static_cast<int>(d),
+                                           static_cast<int>(d), fe, group, 1, s, 0, 0))
+      return rc;
+    return mq_moe_combine(z, nullptr, weights, 1, topk, d, add, y, s);
+  }
+  const float *z = nullptr;
+  const int32_t *slot_of = nullptr;
+  if (int rc = mq::moe::experts(x, MQ_F32, ids, gu_wq, gu_ws, dn_wq, dn_ws, tokens, experts, topk, d, fe, group, w, s,
+                                mq::moe::kSmallPairs, &z, &slot_of, mq::FlagWait(), grouped))
     return rc;
   return mq_moe_combine(z, slot_of, weights, tokens, topk, d, add, y, s);
 }

@@ -26,6 +26,10 @@ SIGNATURES = {
     "mq_moe_router": (c_int, [c_vp, c_vp, c_vp, c_i64, c_int, c_i64, c_vp]),
     "mq_moe_route": (c_int, [c_vp, c_vp, c_vp, c_i64, c_int, c_int, c_vp]),
     "mq_moe_group": (c_int, [c_vp, c_i64, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "mq_moe_route_group": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_int, c_int, c_i64, c_int, c_vp, c_vp, c_vp,
+                                   c_vp, c_vp, c_vp, c_vp]),
+    "mq_moe_layer": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_int, c_int, c_i64,
+                             c_i64, c_int, c_int, c_vp, c_size, c_vp]),
     "mq_ep_plan": (c_int, [c_vp, c_i64, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "mq_moe_gather": (c_int, [c_vp, c_int, c_vp, c_i64, c_int, c_i64, c_vp, c_vp]),
     "mq_moe_gemm_q4": (c_int, [c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_int, c_i64, c_int, c_vp, c_vp, c_int, c_int,

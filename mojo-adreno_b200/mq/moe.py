@@ -9,7 +9,8 @@ import torch
 from ._lib import MQError, lib
 from .kernels import MQ_F16, MQ_F32, _need, _p, _stream, _WORDS
 
-__all__ = ["gemv_f32", "p_gemv_f32", "router", "p_route", "route", "p_expert_lists", "moe_gemv_q4", "moe_gate_up", "moe_down", "moe_forward", "TILE_M"]
+__all__ = ["gemv_f32", "p_gemv_f32", "router", "p_route", "route", "p_expert_lists", "route_group", "moe_gemv_q4",
+           "moe_gate_up", "moe_down", "moe_forward", "moe_layer", "TILE_M"]
 
 TILE_M = 64  # tokens per expert work tile of the grouped products
 
@@ -77,6 +78,41 @@ def p_expert_lists(ids, experts, tile=TILE_M):
     lib.call("mq_moe_group", _p(ids), tokens, topk, experts, tile, _p(counts), _p(offsets), _p(order), _p(slot_of),
              _p(tiles), _p(ntiles), _stream())
     return counts, offsets, order, slot_of, tiles, ntiles
+
+
+def route_group(w, x, ids, weights, topk=8, logits=None, tile=TILE_M, group=True):
+    """The router chain fused on the device: router logits (fp32 W [experts, d] . x [tokens, d]),
+    the top-k experts and softmax weights of each token, and (group=True) the stable grouping of the
+    pairs by expert -- gemv_f32 + route + p_expert_lists / p_expert_items (moek.mojo:143-197,
+    432-442, 548-557) in two launches, the logits kept on chip (written to `logits` when given).
+    Returns (ids, weights) and, with group, p_expert_lists' (counts, offsets, order, slot_of, tiles,
+    ntiles)."""
+    _need(x, "x", (torch.float32,))
+    d = x.shape[-1]
+    tokens = x.numel() // d
+    _need(w, "w", (torch.float32,))
+    experts = w.numel() // d
+    _need(ids, "ids", (torch.int32,), tokens * topk)
+    _need(weights, "weights", (torch.float32,), tokens * topk)
+    if logits is not None:
+        _need(logits, "logits", (torch.float32,), tokens * experts)
+    if not group:
+        lib.call("mq_moe_route_group", _p(w), _p(x), _p(logits) if logits is not None else None, _p(ids), _p(weights),
+                 tokens, experts, topk, d, tile, None, None, None, None, None, None, _stream())
+        return ids, weights
+    pairs = tokens * topk
+    dev = x.device
+    max_tiles = experts + (pairs + tile - 1) // tile
+    counts = torch.empty(experts, dtype=torch.int32, device=dev)
+    offsets = torch.empty(experts + 1, dtype=torch.int32, device=dev)
+    order = torch.empty(pairs, dtype=torch.int32, device=dev)
+    slot_of = torch.empty(pairs, dtype=torch.int32, device=dev)
+    tiles = torch.empty(max_tiles * 3, dtype=torch.int32, device=dev)
+    ntiles = torch.empty(1, dtype=torch.int32, device=dev)
+    lib.call("mq_moe_route_group", _p(w), _p(x), _p(logits) if logits is not None else None, _p(ids), _p(weights),
+             tokens, experts, topk, d, tile, _p(counts), _p(offsets), _p(order), _p(slot_of), _p(tiles), _p(ntiles),
+             _stream())
+    return (ids, weights), (counts, offsets, order, slot_of, tiles, ntiles)
 
 
 def moe_gemv_q4(wq, ws, ids, x, y, k, group_rows, rows_per_group=None, group=32, x_per_group=False):
@@ -147,3 +183,36 @@ def moe_forward(x, ids, weights, gu_wq, gu_ws, dn_wq, dn_ws, y, d, fe, group=32,
              _p(gu_ws), _p(dn_wq), _p(dn_ws), _p(y), tokens, experts, topk, d, fe, group, int(bool(add)),
              _p(workspace), nbytes, _stream())
     return y
+
+
+def moe_layer(x, router_w, gu_wq, gu_ws, dn_wq, dn_ws, y, d, fe, group=32, topk=8, ids=None, weights=None, logits=None,
+              add=False, workspace=None):
+    """y (+)= the MoE layer with its router on the device, as the model runs it (qwen3moe/model.mojo:
+    208-274): the fused router chain (route_group) picks each token's experts and weights, then the
+    experts run as in moe_forward. x fp32 [tokens, d]; router_w fp32 [experts, d]; ids int32 and
+    weights fp32 [tokens, topk] receive the routing (made when None), logits fp32 [tokens, experts]
+    the router logits when given. Returns (y, ids, weights)."""
+    _need(x, "x", (torch.float32,))
+    tokens = x.numel() // d
+    _need(router_w, "router_w", (torch.float32,))
+    experts = router_w.numel() // d
+    _need(gu_wq, "gu_wq", _WORDS, experts * 2 * fe * d // 8)
+    _need(gu_ws, "gu_ws", (torch.float16,), experts * 2 * fe * d // group)
+    _need(dn_wq, "dn_wq", _WORDS, experts * d * fe // 8)
+    _need(dn_ws, "dn_ws", (torch.float16,), experts * d * fe // group)
+    _need(y, "y", (torch.float32,), tokens * d)
+    ids = torch.empty(tokens, topk, dtype=torch.int32, device=x.device) if ids is None else ids
+    weights = torch.empty(tokens, topk, dtype=torch.float32, device=x.device) if weights is None else weights
+    _need(ids, "ids", (torch.int32,), tokens * topk)
+    _need(weights, "weights", (torch.float32,), tokens * topk)
+    if logits is not None:
+        _need(logits, "logits", (torch.float32,), tokens * experts)
+    nbytes = lib.mq_moe_workspace_size(tokens, experts, topk, d, fe)
+    if workspace is None:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    if workspace.numel() < nbytes:
+        raise MQError(-1, f"workspace: {workspace.numel()} bytes < {nbytes}")
+    lib.call("mq_moe_layer", _p(x), _p(router_w), _p(gu_wq), _p(gu_ws), _p(dn_wq), _p(dn_ws), _p(y), _p(ids),
+             _p(weights), _p(logits) if logits is not None else None, tokens, experts, topk, d, fe, group,
+             int(bool(add)), _p(workspace), nbytes, _stream())
+    return y, ids, weights

@@ -182,3 +182,72 @@ def test_router_logits_and_routing(cuda, tokens, experts, d):
     rid, rw = omoe.route(got, 8)
     np.testing.assert_array_equal(ids.cpu().numpy(), rid)
     np.testing.assert_allclose(wts.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("tokens,experts,d", [(404, 128, 2048), (1, 128, 2048), (7, 60, 768), (33, 128, 4100),
+                                              (17, 256, 512), (5, 20, 64)])
+def test_route_group_fused_chain(cuda, tokens, experts, d):
+    """The fused router chain (one cluster kernel: router GEMV + top-k + softmax from distributed shared
+    memory, then the grouping): logits against float64, routing bit-exact against the oracle on the
+    chain's own logits, grouping bit-exact against the oracle's expert lists of those ids."""
+    rng = np.random.default_rng(3 * tokens + experts + d)
+    w = (rng.standard_normal((experts, d)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((tokens, d)).astype(np.float32)
+    topk = min(8, experts)
+    logits = torch.empty(tokens, experts, device=cuda)
+    ids = torch.empty(tokens, topk, dtype=torch.int32, device=cuda)
+    wts = torch.empty(tokens, topk, device=cuda)
+    (_, _), (counts, offsets, order, slot_of, tiles, ntiles) = mq.route_group(t(w, cuda), t(x, cuda), ids, wts, topk=topk,
+                                                                             logits=logits)
+    torch.cuda.synchronize()
+    assert mq.device_status() == 0
+    got = logits.cpu().numpy()
+    assert normwise(got, x.astype(np.float64) @ w.astype(np.float64).T) <= 1e-5
+    rid, rw = omoe.route(got, topk)
+    np.testing.assert_array_equal(ids.cpu().numpy(), rid)
+    np.testing.assert_allclose(wts.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+    ro, rorder = omoe.expert_lists(rid, experts)
+    np.testing.assert_array_equal(offsets.cpu().numpy(), ro)
+    np.testing.assert_array_equal(counts.cpu().numpy(), np.diff(ro))
+    np.testing.assert_array_equal(order.cpu().numpy(), rorder)
+    np.testing.assert_array_equal(slot_of.cpu().numpy()[rorder], np.arange(tokens * topk))
+    assert int(ntiles.item()) == int(np.sum((np.diff(ro) + 63) // 64))
+    # without the grouping: the same routing
+    ids2 = torch.empty_like(ids)
+    wts2 = torch.empty_like(wts)
+    mq.route_group(t(w, cuda), t(x, cuda), ids2, wts2, topk=topk, group=False)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(ids2.cpu().numpy(), rid)
+    np.testing.assert_array_equal(wts2.cpu().numpy(), wts.cpu().numpy())
+
+
+@pytest.mark.parametrize("tokens", [404, 1, 2, 3])
+def test_moe_layer_with_router(cuda, tokens):
+    """The whole layer with its router on the device (mq_moe_layer), in a CUDA graph replayed twice:
+    the routing equals the oracle's on the chain's logits, the output the fp64 layer on that routing.
+    1 token runs the decode GEMVs, 2 tokens (16 pairs) the small-pair GEMVs, 3 and 404 the grouped
+    tensor-core products on the chain's grouping."""
+    m = synth.moe_layer(seed=11, tokens=tokens)
+    rw = (np.random.default_rng(5).standard_normal((128, 2048)) * 0.02).astype(np.float32)
+    tx, trw = t(m["x"], cuda), t(rw, cuda)
+    gw = [t(m[k], cuda) for k in ("gu_wq", "gu_ws", "dn_wq", "dn_ws")]
+    y = torch.full((tokens, 2048), float("nan"), device=cuda)
+    ids = torch.empty(tokens, 8, dtype=torch.int32, device=cuda)
+    wts = torch.empty(tokens, 8, device=cuda)
+    logits = torch.empty(tokens, 128, device=cuda)
+    ws = torch.empty(mq.lib.mq_moe_workspace_size(tokens, 128, 8, 2048, 768), dtype=torch.uint8, device=cuda)
+    mq.moe_layer(tx, trw, *gw, y, 2048, 768, group=32, ids=ids, weights=wts, logits=logits, workspace=ws)
+    torch.cuda.synchronize()
+    y.fill_(float("nan"))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        mq.moe_layer(tx, trw, *gw, y, 2048, 768, group=32, ids=ids, weights=wts, logits=logits, workspace=ws)
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    assert mq.device_status() == 0
+    rid, rwts = omoe.route(logits.cpu().numpy(), 8)
+    np.testing.assert_array_equal(ids.cpu().numpy(), rid)
+    np.testing.assert_allclose(wts.cpu().numpy(), rwts, rtol=2e-6, atol=1e-7)
+    ref = omoe.moe_layer(m["x"], rid, rwts, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 32, 768)
+    assert normwise(y.cpu().numpy(), ref) <= TOL
