@@ -554,20 +554,24 @@ def moe_bench(mq, synth, dev, stream, world, rank):
         gr = graph_of(lambda: [mq.router(rw, tx, rids, rwts, 8, rl) for _ in range(reps)])
         router_ms = max_over_ranks(time_graphs([gr], 10, stream) / reps, world)
         # the fused chain: router GEMV + top-k + softmax in one cluster kernel, then the grouping
-        gf = graph_of(lambda: [mq.route_group(rw, tx, rids, rwts, 8, group=tokens * 8 > 16) for _ in range(reps)])
+        gf = graph_of(lambda: [mq.route_group(rw, tx, rids, rwts, 8, logits=rl, group=tokens * 8 > 16)
+                               for _ in range(reps)])
         fused_ms = max_over_ranks(time_graphs([gf], 10, stream) / reps, world)
+        gfr = graph_of(lambda: [mq.route_group(rw, tx, rids, rwts, 8, logits=rl, group=False) for _ in range(reps)])
+        fused_route_ms = max_over_ranks(time_graphs([gfr], 10, stream) / reps, world)
         # the whole layer with its router (mq_moe_layer): routing, grouping and experts
         gl = graph_of(lambda: [mq.moe_layer(tx, rw, *gws[i % copies], y, 2048, 768, group=32, ids=rids, weights=rwts,
                                             workspace=ws) for i in range(layers)])
         layer_ms = max_over_ranks(time_graphs([gl], 10, stream) / layers, world)
         out[f"tokens_{tokens}"] = {"ms": round(ms, 5), "tokens/s": round(tokens / (ms * 1e-3), 1),
                                    "router_and_route_ms": round(router_ms, 5),
+                                   "router_and_route_fused_ms": round(fused_route_ms, 5),
                                    "router_route_and_grouping_fused_ms": round(fused_ms, 5),
                                    "layer_with_router_ms": round(layer_ms, 5),
                                    "experts_touched": int(len(used)),
                                    "expert_weight_GB/s": round(active_bytes / (ms * 1e-3) / 1e9, 1),
                                    "timing": f"{layers} layers per CUDA graph over {copies} weight copies"}
-        del g, gr, gf, gl, gws
+        del g, gr, gf, gfr, gl, gws
     return out
 
 
@@ -817,7 +821,8 @@ def profile_case(name, launches):
     Cases: gemv_lm_head (configs[1] head, batch 1), tgemv_head (configs[4] head), gemm_gate_up
     (configs[2] 8192x2048, 431 tokens), gemm_decode64_head (configs[1] head, batch 64), moe_prefill
     and moe_decode (configs[3], 404 tokens and 1 token), gemm_t2_gate_up / gemm_t2_down (the ternary
-    prefill GEMM on the Qwen3-8B projections, 512 rows)."""
+    prefill GEMM on the Qwen3-8B projections, 512 rows), route_group_404 / route_group_1 (the fused
+    router chain on configs[3]'s router at 404 tokens and 1 token)."""
     import mq
     from mq import synth
 
@@ -857,6 +862,15 @@ def profile_case(name, launches):
         ty = torch.empty(512, n, device=dev)
         for _ in range(launches):
             mq.p_gemm_t2(tx, tw, ts, ty, n, k, 512)
+    elif name in ("route_group_404", "route_group_1"):
+        tokens = 404 if name.endswith("404") else 1
+        rng = np.random.default_rng(5)
+        rw = torch.from_numpy((rng.standard_normal((128, 2048)) * 0.02).astype(np.float32)).to(dev)
+        tx = torch.from_numpy(rng.standard_normal((tokens, 2048)).astype(np.float32)).to(dev)
+        ids = torch.empty(tokens, 8, dtype=torch.int32, device=dev)
+        wts = torch.empty(tokens, 8, device=dev)
+        for _ in range(launches):
+            mq.route_group(rw, tx, ids, wts, 8, group=tokens > 2)
     elif name in ("moe_prefill", "moe_decode"):
         tokens = 404 if name == "moe_prefill" else 1
         m = synth.moe_layer(seed=0, tokens=tokens)

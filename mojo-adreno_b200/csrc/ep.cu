@@ -57,6 +57,8 @@ __global__ void dispatch_kernel(const void *__restrict__ x, int x_f16, const int
                                 const int32_t *__restrict__ local_ids, int topk, int dm, int world, int rank, int cap,
                                 uint16_t *const *peer_rows, int32_t *const *peer_ids, int *const *peer_flags,
                                 int *epoch, int *done) {
+  griddep_launch_dependents();
+  griddep_wait();            // programmatic dependent launch: earlier work on the stream is complete
   const int e = *epoch + 1;  // this layer's epoch: the last CTA stores it for the later steps
   const int vec = dm / 8, slots = world * cap;
   const size_t base_row = static_cast<size_t>(rank) * cap;
@@ -85,6 +87,8 @@ __global__ void dispatch_kernel(const void *__restrict__ x, int x_f16, const int
 
 // Waits for flag slot `which * world + s` of every rank s to reach the epoch.
 __global__ void wait_kernel(const int *flags, int which, int world, const int *epoch) {
+  griddep_launch_dependents();
+  griddep_wait();
   FlagWait w;
   w.flags = flags;
   w.which = which;
@@ -99,6 +103,8 @@ __global__ void wait_kernel(const int *flags, int which, int world, const int *e
 __global__ void return_kernel(const float *__restrict__ z, const int32_t *__restrict__ slot_of,
                               const int32_t *__restrict__ ids, int dm, int world, int rank, int cap,
                               float *const *peer_ret, int *const *peer_flags, const int *epoch, int *done) {
+  griddep_launch_dependents();
+  griddep_wait();
   const int e = *epoch;
   const int vec = dm / 4, slots = world * cap;
   for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < static_cast<int64_t>(slots) * vec;
@@ -185,18 +191,17 @@ extern "C" int mq_ep_dispatch(const void *x, int x_dtype, const int32_t *order, 
   MQ_REQUIRE(!x || mq::aligned(x, 16), MQ_EALIGN, "mq_ep_dispatch: x must be 16-byte aligned");
   mq::DeviceInfo dev;
   if (int rc = mq::device_info(&dev)) return rc;
-  mq::ep::dispatch_kernel<<<mq::ep::grid_for(static_cast<int64_t>(world) * cap * (d / 8), dev), 256, 0,
-                            static_cast<cudaStream_t>(stream)>>>(x, x_dtype == MQ_F16, order, local_ids, topk,
-                                                                 static_cast<int>(d), world, rank, cap, peer_rows,
-                                                                 peer_ids, peer_flags, epoch, done);
-  return mq::check_launch("mq_ep_dispatch");
+  const int xh = x_dtype == MQ_F16;
+  return mq::launch_overlapped(mq::ep::dispatch_kernel, dim3(mq::ep::grid_for(static_cast<int64_t>(world) * cap * (d / 8), dev)),
+                               dim3(256), 0, static_cast<cudaStream_t>(stream), "mq_ep_dispatch", x, xh, order, local_ids,
+                               topk, static_cast<int>(d), world, rank, cap, peer_rows, peer_ids, peer_flags, epoch, done);
 }
 
 extern "C" int mq_ep_wait(const int *flags, int which, int world, const int *epoch, void *stream) {
   MQ_REQUIRE(flags && epoch && (which == 0 || which == 1) && world >= 1 && world <= 256, MQ_EINVAL,
              "mq_ep_wait: bad arguments");
-  mq::ep::wait_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(flags, which, world, epoch);
-  return mq::check_launch("mq_ep_wait");
+  return mq::launch_overlapped(mq::ep::wait_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), "mq_ep_wait",
+                               flags, which, world, epoch);
 }
 
 extern "C" int mq_ep_return(const float *z, const int32_t *slot_of, const int32_t *ids, int64_t d, int world, int rank,
@@ -208,8 +213,7 @@ extern "C" int mq_ep_return(const float *z, const int32_t *slot_of, const int32_
   MQ_REQUIRE(mq::aligned(z, 16), MQ_EALIGN, "mq_ep_return: z must be 16-byte aligned");
   mq::DeviceInfo dev;
   if (int rc = mq::device_info(&dev)) return rc;
-  mq::ep::return_kernel<<<mq::ep::grid_for(static_cast<int64_t>(world) * cap * (d / 4), dev), 256, 0,
-                          static_cast<cudaStream_t>(stream)>>>(z, slot_of, ids, static_cast<int>(d), world, rank, cap,
-                                                               peer_ret, peer_flags, epoch, done);
-  return mq::check_launch("mq_ep_return");
+  return mq::launch_overlapped(mq::ep::return_kernel, dim3(mq::ep::grid_for(static_cast<int64_t>(world) * cap * (d / 4), dev)),
+                               dim3(256), 0, static_cast<cudaStream_t>(stream), "mq_ep_return", z, slot_of, ids,
+                               static_cast<int>(d), world, rank, cap, peer_ret, peer_flags, epoch, done);
 }

@@ -510,14 +510,14 @@ int launch(const uint32_t *wq, Params p, cudaStream_t stream, const DeviceInfo &
         return rc;
   }
   if (!p.scales_tma) smap = wmap;  // not read
-  // Split K across warps (ks divides kWarps, at most K's slots): the largest split whose rounds fit
-  // in one wave of the SMs. A split that spills into a second, partly filled wave measured slower
-  // (16384 x 2048: ks = 4, 128 rounds, 7.2 us; ks = 8, 256 rounds, 7.9 us), and so did splitting a
-  // matrix that already fills the SMs more finely (lm_head: ks = 1, 251 rounds, 27.1 us; ks = 4,
-  // 30.4 us).
-  const int nslotk = (p.k + kSlotK - 1) / kSlotK;
+  // Split K across warps (ks divides kWarps): the largest split whose rounds fit in one wave of the
+  // SMs. A split that spills into a second, partly filled wave measured slower (16384 x 2048: ks = 4,
+  // 128 rounds, 7.2 us; ks = 8, 256 rounds, 7.9 us), and so did splitting a matrix that already fills
+  // the SMs more finely (lm_head: ks = 1, 251 rounds, 27.1 us; ks = 4, 30.4 us). ks may exceed K's
+  // slots: the warps past them then have no items and add zeros, and a small matrix spreads over
+  // more SMs (3072 x 2048, 8 slots: 96 CTAs of one tile instead of 48 of two).
   p.ks = 1;
-  for (int ks = 2; ks <= kWarps && ks <= nslotk; ks *= 2) {
+  for (int ks = 2; ks <= kWarps; ks *= 2) {
     if ((p.tiles + kWarps / ks - 1) / (kWarps / ks) > dev.sms) break;
     p.ks = ks;
   }

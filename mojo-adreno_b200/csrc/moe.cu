@@ -94,7 +94,8 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
                                                               int32_t *__restrict__ slot_of, int32_t *__restrict__ tiles,
                                                               int32_t *__restrict__ ntiles, int32_t *__restrict__ local,
                                                               int cap, FlagWait wait = FlagWait(), int small_limit = 0) {
-  griddep_wait();    // launched behind the fused router (programmatic dependent launch): its ids are written
+  griddep_launch_dependents();
+  griddep_wait();    // programmatic dependent launch (behind the fused router, or an exchange step): ids are written
   wait_flags(wait);  // an expert-parallel owner: the senders' rows and ids have arrived
   extern __shared__ int32_t sh[];
   int32_t *warp_cnt = sh;                    // [32 warps][experts]: pairs of the warp's range, then their start
@@ -118,10 +119,22 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
   };
   auto tiles_of = [&](int c) { return tiles ? (c + tile - 1) / tile : 0; };
 
+  // Each lane's first kCache pairs' buckets stay in registers for both passes (their ids are loaded
+  // once, all at the same time); pairs past them (more than 32 x 32 x kCache) are read again.
+  constexpr int kCache = 8;
+  int bc[kCache];
+#pragma unroll
+  for (int j = 0; j < kCache; ++j) {
+    const int i = lo + lane + 32 * j;
+    bc[j] = i < hi ? bucket(i) : -1;
+  }
   // Pass 1: per-warp histograms.
   for (int j = threadIdx.x; j < 32 * experts; j += kGroupThreads) warp_cnt[j] = 0;
   __syncthreads();
-  for (int i = lo + lane; i < hi; i += 32) {
+#pragma unroll
+  for (int j = 0; j < kCache; ++j)
+    if (bc[j] >= 0) atomicAdd(&warp_cnt[warp * experts + bc[j]], 1);
+  for (int i = lo + lane + 32 * kCache; i < hi; i += 32) {
     const int b = bucket(i);
     if (b >= 0) atomicAdd(&warp_cnt[warp * experts + b], 1);
   }
@@ -200,9 +213,16 @@ __global__ void __launch_bounds__(kGroupThreads) group_kernel(const int32_t *__r
 
   // Pass 2: each warp places its own pairs, 32 at a time, in pair order.
   int32_t *my_cnt = warp_cnt + warp * experts;
-  for (int base = lo; base < hi; base += 32) {
+  for (int base = lo, j = 0; base < hi; base += 32, ++j) {
     const int i = base + lane;
-    const int b = i < hi ? bucket(i) : -1;
+    int b = -1;
+    if (j < kCache) {
+#pragma unroll
+      for (int c = 0; c < kCache; ++c)
+        if (c == j) b = bc[c];
+    } else if (i < hi) {
+      b = bucket(i);
+    }
     const unsigned same = __match_any_sync(0xffffffffu, b);
     const int rank = __popc(same & lt_mask);
     int pos = b >= 0 ? start[b] + my_cnt[b] + rank : 0;
@@ -235,7 +255,8 @@ __device__ __forceinline__ uint4 perm8(uint4 v) {  // halves 0..7 -> 0, 4, 1, 5,
 __global__ void gather_kernel(const void *__restrict__ x, int x_f16, const int32_t *__restrict__ order, int pairs,
                               int topk, int d, __half *__restrict__ xg, int perm = 0, const int32_t *valid = nullptr,
                               FlagWait wait = FlagWait()) {
-  griddep_wait();    // launched behind the fused router (programmatic dependent launch): its ids are written
+  griddep_launch_dependents();
+  griddep_wait();    // programmatic dependent launch: earlier work on the stream is complete
   wait_flags(wait);  // an expert-parallel owner: the senders' rows and ids have arrived
   const int vec = d / 8;  // 8 values per thread step
   const int64_t n = static_cast<int64_t>(valid ? min(*valid, pairs) : pairs) * vec;
@@ -267,6 +288,8 @@ __global__ void gather_kernel(const void *__restrict__ x, int x_f16, const int32
 __global__ void small_gather_kernel(const __half *__restrict__ rows, const int32_t *__restrict__ order,
                                     const int32_t *__restrict__ ids, const int32_t *__restrict__ valid, int n_out, int d,
                                     __half *__restrict__ xs, int32_t *__restrict__ cid) {
+  griddep_launch_dependents();
+  griddep_wait();
   const int nv = *valid;
   if (nv > n_out) return;
   const int vec = d / 8;
@@ -281,6 +304,8 @@ __global__ void small_gather_kernel(const __half *__restrict__ rows, const int32
 
 // ---- SwiGLU for the one-token path: a[k][j] = silu(h[k][j]) * h[k][fe + j] (moe_gate_up) -------
 __global__ void silu_mul_kernel(const float *__restrict__ h, float *__restrict__ a, int rows, int fe) {
+  griddep_launch_dependents();
+  griddep_wait();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows * fe; i += gridDim.x * blockDim.x) {
     const int r = i / fe, j = i % fe;
     const float g = h[static_cast<size_t>(r) * 2 * fe + j], u = h[static_cast<size_t>(r) * 2 * fe + fe + j];
@@ -293,6 +318,8 @@ __global__ void silu_mul_kernel(const float *__restrict__ h, float *__restrict__
 __global__ void combine_kernel(const float *__restrict__ z, const int32_t *__restrict__ slot_of,
                                const float *__restrict__ w, int tokens, int topk, int d, int add, float *__restrict__ y,
                                FlagWait wait = FlagWait()) {
+  griddep_launch_dependents();
+  griddep_wait();
   wait_flags(wait);  // an expert-parallel sender: every owner's outputs have come back
   const int vec = d / 4;
   for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < static_cast<int64_t>(tokens) * vec;
@@ -385,14 +412,21 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const float *__r
 }
 
 // ---- the fused router chain: router GEMV + top-k + softmax in one cluster kernel -------------
-// A cluster of 8 CTAs takes kRgTokens tokens; CTA r computes the logits of experts
-// [r * epc, (r + 1) * epc) (epc = ceil(E / 8) <= 32) for them, keeps them in its shared memory,
-// and after a cluster barrier each token is routed by one warp that reads its E logits from the
+// A cluster of 8 CTAs takes TOK tokens (16, or 4 for a few tokens); CTA r computes the logits of
+// experts [r * epc, (r + 1) * epc) (epc = ceil(E / 8) <= 32) for them and keeps them in its shared
+// memory; after a cluster barrier each token is routed by one warp that reads its E logits from the
 // eight CTAs' shared memory (distributed shared memory), so the logits never round-trip through
 // global memory (they are written out only when asked for). The grouping (group_kernel) follows as
 // a programmatic dependent launch. The router follows gemv_f32 / p_gemv_f32 (moek.mojo:143-153,
 // 284-295), the routing route / p_route (moek.mojo:156-197, 385-425).
-constexpr int kRgCluster = 8, kRgThreads = 256, kRgTokens = 16, kRgChunk = 512;
+// The GEMV is register-blocked: a warp owns 8 tokens x 8 experts over a k range; per 128 k its lanes
+// read 4 k of the 8 tokens and of the 8 expert rows from shared memory, so each load feeds 32 fused
+// multiply-adds. x and the CTA's expert rows stream into shared memory 256 k at a time through a
+// 3-stage ring of cp.async copies (the copies of later stages fly while a stage is multiplied). The
+// CTA's warps split its experts into groups of 8 and each stage's k into kKG ranges; a warp's 64 sums
+// are reduced across its lanes by a transposing butterfly, then the kKG partial sums of each logit
+// are added in a fixed order.
+constexpr int kRgCluster = 8, kRgThreads = 256, kRgTokens = 16, kRgChunk = 256, kRgStages = 3;
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -412,74 +446,125 @@ __device__ __forceinline__ float ld_cluster_f32(const float *p, uint32_t rank) {
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
   return v;
 }
+// 16 bytes global -> shared, asynchronously; src_bytes 0 fills the 16 bytes with zeros (src unread).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-template <int EPW, int PER>  // experts per warp (epc <= 8 * EPW), logits per lane in routing (E <= 32 * PER)
+// 32 partial sums per lane -> lane l holds the warp total of sum l (a transposing butterfly: 31 shuffles).
+__device__ __forceinline__ float warp_transpose_sum32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int o = 16, half = 16; o >= 1; o >>= 1, half >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float send = up ? v[i] : v[i + half];
+      const float keep = up ? v[i + half] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0];
+}
+
+// Dynamic shared memory of route_group_kernel<XG>: the ring of (x, w) stages.
+__host__ __device__ constexpr size_t rg_ring_bytes(int xg) {
+  return static_cast<size_t>(kRgStages) * (kRgTokens + 8 * xg) * kRgChunk * sizeof(float);
+}
+
+template <int XG, int PER>  // expert groups of 8 per CTA (epc <= 8 * XG); logits per lane in routing (E <= 32 * PER)
 __global__ void __cluster_dims__(kRgCluster, 1, 1) __launch_bounds__(kRgThreads)
     route_group_kernel(const float *__restrict__ w, const float *__restrict__ x, float *__restrict__ logits,
                        int32_t *__restrict__ ids, float *__restrict__ weights, int tokens, int experts, int topk, int d) {
-  constexpr int kPass = EPW < 2 ? EPW : 2;  // experts a warp accumulates at once (more passes re-read x)
-  __shared__ __align__(16) float xs[kRgTokens][kRgChunk];
-  __shared__ float lg[kRgTokens][32];  // this CTA's experts' logits
+  constexpr int kTG = kRgTokens / 8;                   // token groups of 8
+  constexpr int kKG = (kRgThreads / 32) / (kTG * XG);  // k ranges (warps = kTG x XG x kKG)
+  static_assert(kKG >= 1 && kTG * XG * kKG == kRgThreads / 32 && kRgChunk / kKG >= 128, "warp layout");
+  constexpr int kRows = kRgTokens + 8 * XG;            // rows of a stage: the tokens, then the experts
+  extern __shared__ __align__(16) float ring[];        // [stage][kRows][kRgChunk]
+  __shared__ float part[kKG][kRgTokens][8 * XG];       // per k range: this CTA's logits
+  __shared__ float lg[kRgTokens][32];                  // this CTA's experts' logits
   const uint32_t rank = cluster_ctarank();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int tg = warp % kTG, xg = (warp / kTG) % XG, kg = warp / (kTG * XG);
   const int t0 = static_cast<int>(blockIdx.x / kRgCluster) * kRgTokens;
   const int epc = (experts + kRgCluster - 1) / kRgCluster, e_lo = static_cast<int>(rank) * epc;
+  const int nchunks = (d + kRgChunk - 1) / kRgChunk;
   griddep_launch_dependents();
   griddep_wait();  // x may come from the previous kernel on the stream
-#pragma unroll 1
-  for (int pass = 0; pass < EPW / kPass; ++pass) {
-    float acc[kPass][kRgTokens];
-#pragma unroll
-    for (int j = 0; j < kPass; ++j)
-#pragma unroll
-      for (int t = 0; t < kRgTokens; ++t) acc[j][t] = 0.f;
-    for (int k0 = 0; k0 < d; k0 += kRgChunk) {
-      const int kn = min(kRgChunk, d - k0);
-      __syncthreads();
-      for (int i = threadIdx.x; i < kRgTokens * kRgChunk / 4; i += kRgThreads) {
-        const int t = i / (kRgChunk / 4), k = (i % (kRgChunk / 4)) * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t0 + t < tokens && k < kn) v = *reinterpret_cast<const float4 *>(x + static_cast<size_t>(t0 + t) * d + k0 + k);
-        *reinterpret_cast<float4 *>(&xs[t][k]) = v;
+  // Stage c of the ring: row r < kRgTokens is token t0 + r of x, row kRgTokens + j expert e_lo + j of w;
+  // rows past the tokens, the CTA's experts or d are zero-filled.
+  auto issue = [&](int c) {
+    float *st = ring + static_cast<size_t>(c % kRgStages) * kRows * kRgChunk;
+    const int k0 = c * kRgChunk;
+    for (int i = threadIdx.x; i < kRows * (kRgChunk / 4); i += kRgThreads) {
+      const int r = i / (kRgChunk / 4), k = (i % (kRgChunk / 4)) * 4;
+      const float *src = x;
+      bool live = k0 + k < d;
+      if (r < kRgTokens) {
+        live = live && t0 + r < tokens;
+        if (live) src = x + static_cast<size_t>(t0 + r) * d + k0 + k;
+      } else {
+        const int le = r - kRgTokens, e = e_lo + le;
+        live = live && le < epc && e < experts;
+        if (live) src = w + static_cast<size_t>(e) * d + k0 + k;
       }
-      __syncthreads();
+      cp_async16(st + r * kRgChunk + k, src, live ? 16u : 0u);
+    }
+  };
 #pragma unroll
-      for (int j = 0; j < kPass; ++j) {
-        const int le = warp + 8 * (pass * kPass + j), e = e_lo + le;
-        const bool live = le < epc && e < experts;
-        const float *wr = w + static_cast<size_t>(live ? e : 0) * d + k0;
-        float4 wv[kRgChunk / 128];
+  for (int c = 0; c < kRgStages - 1; ++c) {
+    if (c < nchunks) issue(c);
+    cp_async_commit();
+  }
+  float acc[8][8];  // [expert][token]
 #pragma unroll
-        for (int q = 0; q < kRgChunk / 128; ++q) {
-          const int k = lane * 4 + 128 * q;
-          wv[q] = live && k < kn ? __ldg(reinterpret_cast<const float4 *>(wr + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+  for (int j = 0; j < 8; ++j)
 #pragma unroll
-        for (int q = 0; q < kRgChunk / 128; ++q) {
-          const int k = lane * 4 + 128 * q;
+    for (int t = 0; t < 8; ++t) acc[j][t] = 0.f;
+  constexpr int kSpan = kRgChunk / kKG;  // k of a stage per k range
+  for (int c = 0; c < nchunks; ++c) {
+    if (c + kRgStages - 1 < nchunks) issue(c + kRgStages - 1);
+    cp_async_commit();
+    cp_async_wait<kRgStages - 1>();  // this thread's copies of stage c landed
+    __syncthreads();                 // ... and every thread's
+    const float *st = ring + static_cast<size_t>(c % kRgStages) * kRows * kRgChunk;
 #pragma unroll
-          for (int t = 0; t < kRgTokens; ++t) {
-            const float4 xv = *reinterpret_cast<const float4 *>(&xs[t][k]);
-            acc[j][t] = fmaf(wv[q].x, xv.x, fmaf(wv[q].y, xv.y, fmaf(wv[q].z, xv.z, fmaf(wv[q].w, xv.w, acc[j][t]))));
-          }
-        }
+    for (int q = 0; q < kSpan / 128; ++q) {
+      const int k = kg * kSpan + lane * 4 + 128 * q;
+      float4 wv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wv[j] = *reinterpret_cast<const float4 *>(st + (kRgTokens + xg * 8 + j) * kRgChunk + k);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const float4 xv = *reinterpret_cast<const float4 *>(st + (tg * 8 + t) * kRgChunk + k);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          acc[j][t] = fmaf(wv[j].x, xv.x, fmaf(wv[j].y, xv.y, fmaf(wv[j].z, xv.z, fmaf(wv[j].w, xv.w, acc[j][t]))));
       }
     }
-    // Each warp sums its lanes in a fixed order; the logits stay in shared memory.
+    __syncthreads();  // stage c is free for the copies issued next
+  }
+  cp_async_wait<0>();
+  // lanes -> one sum per (expert, token): two transposing butterflies of 32
 #pragma unroll
-    for (int j = 0; j < kPass; ++j) {
-      const int le = warp + 8 * (pass * kPass + j), e = e_lo + le;
+  for (int h = 0; h < 2; ++h) {
+    float v[32];
 #pragma unroll
-      for (int t = 0; t < kRgTokens; ++t) {
-        float v = acc[j][t];
+    for (int i = 0; i < 32; ++i) v[i] = acc[4 * h + i / 8][i % 8];
+    const float total = warp_transpose_sum32(v, lane);  // expert 4 h + lane / 8, token lane % 8
+    part[kg][tg * 8 + lane % 8][xg * 8 + 4 * h + lane / 8] = total;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kRgTokens * epc; i += kRgThreads) {
+    const int t = i / epc, le = i % epc, e = e_lo + le;
+    if (e >= experts) continue;
+    float v = part[0][t][le];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0 && le < epc && e < experts) {
-          lg[t][le] = v;
-          if (logits && t0 + t < tokens) logits[static_cast<size_t>(t0 + t) * experts + e] = v;
-        }
-      }
-    }
+    for (int g = 1; g < kKG; ++g) v += part[g][t][le];
+    lg[t][le] = v;
+    if (logits && t0 + t < tokens) logits[static_cast<size_t>(t0 + t) * experts + e] = v;
   }
   cluster_sync();
   // Routing: token t0 + tt by warp tt / 8 of CTA tt % 8, its logits gathered from the eight CTAs.
@@ -540,29 +625,62 @@ namespace mq {
 namespace moe {
 // The fused router chain on `stream`: route_group_kernel, then (counts != null) group_kernel as a
 // programmatic dependent launch. Shapes are checked by the callers.
+int route_cluster(const float *w, const float *x, float *logits, int32_t *ids, float *weights, int64_t tokens,
+                  int experts, int topk, int64_t d, cudaStream_t s);
+
+// scratch (may be null): room for tokens x experts fp32 logits. A few tokens (decode) with somewhere
+// to put the logits run the router GEMV over more CTAs (router_kernel: one expert per warp, 32 CTAs
+// for 128 experts) and route_kernel instead of the cluster kernel, which would spend a 16-token tile
+// of work and one 8-SM cluster on them.
 int route_group(const float *w, const float *x, float *logits, int32_t *ids, float *weights, int64_t tokens,
                 int experts, int topk, int64_t d, int tile, int32_t *counts, int32_t *offsets, int32_t *order,
-                int32_t *slot_of, int32_t *tiles, int32_t *ntiles, cudaStream_t s) {
-  const unsigned grid = static_cast<unsigned>((tokens + kRgTokens - 1) / kRgTokens) * kRgCluster;
-  const int epc = (experts + kRgCluster - 1) / kRgCluster;
-  const int ti = static_cast<int>(tokens), ei = experts, di = static_cast<int>(d);
-  int rc;
-  if (epc <= 8)
-    rc = launch_overlapped(route_group_kernel<1, 4>, dim3(grid), dim3(kRgThreads), 0, s, "mq_moe_route_group", w, x,
-                           logits, ids, weights, ti, ei, topk, di);
-  else if (epc <= 16 && experts <= 128)
-    rc = launch_overlapped(route_group_kernel<2, 4>, dim3(grid), dim3(kRgThreads), 0, s, "mq_moe_route_group", w, x,
-                           logits, ids, weights, ti, ei, topk, di);
-  else
-    rc = launch_overlapped(route_group_kernel<4, 8>, dim3(grid), dim3(kRgThreads), 0, s, "mq_moe_route_group", w, x,
-                           logits, ids, weights, ti, ei, topk, di);
-  if (rc || !counts) return rc;
+                int32_t *slot_of, int32_t *tiles, int32_t *ntiles, cudaStream_t s, float *scratch = nullptr) {
+  float *lbuf = logits ? logits : scratch;
+  if (tokens <= 4 && lbuf) {
+    const int warps = kRouterThreads / 32;
+    if (int rc = launch_overlapped(router_kernel<1>, dim3(static_cast<unsigned>((tokens + kRouterTokens - 1) / kRouterTokens),
+                                                         (experts + warps - 1) / warps),
+                                   dim3(kRouterThreads), 0, s, "mq_moe_route_group (router)", w, x, lbuf,
+                                   static_cast<int>(tokens), experts, static_cast<int>(d)))
+      return rc;
+    const int per_block = 256 / 32, grid = static_cast<int>((tokens + per_block - 1) / per_block);
+    if (experts <= 128)
+      route_kernel<4><<<grid, 256, 0, s>>>(lbuf, ids, weights, static_cast<int>(tokens), experts, topk);
+    else
+      route_kernel<8><<<grid, 256, 0, s>>>(lbuf, ids, weights, static_cast<int>(tokens), experts, topk);
+    if (int rc = check_launch("mq_moe_route_group (route)")) return rc;
+  } else {
+    if (int rc = route_cluster(w, x, logits, ids, weights, tokens, experts, topk, d, s)) return rc;
+  }
+  if (!counts) return MQ_OK;
   const size_t smem = (32 * experts + 2 * (experts + 1)) * sizeof(int32_t);
   const int32_t *cids = ids;
   int32_t *no_local = nullptr;
   return launch_overlapped(group_kernel, dim3(1), dim3(kGroupThreads), smem, s, "mq_moe_route_group (grouping)", cids, 1,
                            static_cast<int>(tokens * topk), experts, tile, counts, offsets, order, slot_of, tiles, ntiles,
                            no_local, 0, FlagWait(), 0);
+}
+
+// The cluster kernel: router GEMV, top-k and softmax in one launch.
+int route_cluster(const float *w, const float *x, float *logits, int32_t *ids, float *weights, int64_t tokens,
+                  int experts, int topk, int64_t d, cudaStream_t s) {
+  const int epc = (experts + kRgCluster - 1) / kRgCluster;  // <= 32
+  const unsigned grid = static_cast<unsigned>((tokens + kRgTokens - 1) / kRgTokens) * kRgCluster;
+  const int ti = static_cast<int>(tokens), ei = experts, di = static_cast<int>(d);
+  const char *what = "mq_moe_route_group";
+  int rc;
+  auto go = [&](auto kern, int xg) {
+    const size_t smem = rg_ring_bytes(xg);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+      return fail(MQ_ECUDA, "mq_moe_route_group: shared memory attribute");
+    return launch_overlapped(kern, dim3(grid), dim3(kRgThreads), smem, s, what, w, x, logits, ids, weights, ti, ei, topk,
+                             di);
+  };
+  if (epc <= 16 && experts <= 128)  // (fewer experts leave rows of the CTA's two groups of 8 empty)
+    rc = go(route_group_kernel<2, 4>, 2);
+  else
+    rc = go(route_group_kernel<4, 8>, 4);
+  return rc;
 }
 }  // namespace moe
 }  // namespace mq
@@ -607,10 +725,11 @@ extern "C" int mq_ep_plan(const int32_t *ids, int64_t tokens, int topk, int expe
   MQ_REQUIRE(capacity >= 0 && static_cast<int64_t>(capacity) * world < (1 << 30), MQ_EINVAL,
              "mq_ep_plan: bad capacity %d", capacity);
   const size_t smem = (32 * world + 2 * (world + 1)) * sizeof(int32_t);
-  mq::moe::group_kernel<<<1, mq::moe::kGroupThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      ids, experts / world, static_cast<int>(tokens * topk), world, 1, counts, offsets, order, slot_of, nullptr, nullptr,
-      local_ids, capacity);
-  return mq::check_launch("mq_ep_plan");
+  int32_t *no_tiles = nullptr;
+  return mq::launch_overlapped(mq::moe::group_kernel, dim3(1), dim3(mq::moe::kGroupThreads), smem,
+                               static_cast<cudaStream_t>(stream), "mq_ep_plan", ids, experts / world,
+                               static_cast<int>(tokens * topk), world, 1, counts, offsets, order, slot_of, no_tiles,
+                               no_tiles, local_ids, capacity, mq::FlagWait(), 0);
 }
 
 extern "C" int mq_moe_gather(const void *x, int x_dtype, const int32_t *order, int64_t pairs, int topk, int64_t d,
@@ -641,9 +760,10 @@ extern "C" int mq_moe_combine(const float *z, const int32_t *slot_of, const floa
   MQ_REQUIRE(mq::aligned(z, 16) && mq::aligned(y, 16), MQ_EALIGN, "mq_moe_combine: z and y must be 16-byte aligned");
   mq::DeviceInfo dev;
   if (int rc = mq::device_info(&dev)) return rc;
-  mq::moe::combine_kernel<<<mq::moe::grid_for(tokens * (d / 4), 256, dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      z, slot_of, weights, static_cast<int>(tokens), topk, static_cast<int>(d), add != 0, y);
-  return mq::check_launch("mq_moe_combine");
+  return mq::launch_overlapped(mq::moe::combine_kernel, dim3(mq::moe::grid_for(tokens * (d / 4), 256, dev)), dim3(256), 0,
+                               static_cast<cudaStream_t>(stream), "mq_moe_combine", z, slot_of, weights,
+                               static_cast<int>(tokens), topk, static_cast<int>(d), static_cast<int>(add != 0), y,
+                               mq::FlagWait());
 }
 
 namespace mq {
@@ -711,9 +831,11 @@ int experts(const void *x, int x_dtype, const int32_t *ids, const uint32_t *gu_w
   if (int rc = device_info(&dev)) return rc;
   if (P <= small_pairs) {
     float *a = reinterpret_cast<float *>(w.a), *z = w.z;
-    gather_kernel<<<grid_for(P * (d / 8), 256, dev), 256, 0, s>>>(x, x_dtype == MQ_F16, nullptr, static_cast<int>(P),
-                                                                  topk, static_cast<int>(d), w.xg, 0, nullptr, wait);
-    if (int rc = check_launch("mq_moe_forward gather")) return rc;
+    const int32_t *no_order = nullptr;
+    if (int rc = launch_overlapped(gather_kernel, dim3(grid_for(P * (d / 8), 256, dev)), dim3(256), 0, s,
+                                   "mq_moe_forward gather", x, static_cast<int>(x_dtype == MQ_F16), no_order,
+                                   static_cast<int>(P), topk, static_cast<int>(d), w.xg, 0, no_order, wait))
+      return rc;
     if (int rc = gemv::gemv_q4_grouped(gu_wq, gu_ws, experts_n * 2 * fe, w.xg, a, ids, static_cast<int>(P),
                                        static_cast<int>(2 * fe), static_cast<int>(fe), d, group, 1, s, 1, 1))
       return rc;
@@ -726,15 +848,19 @@ int experts(const void *x, int x_dtype, const int32_t *ids, const uint32_t *gu_w
   }
   if (!grouped) {  // grouped: the fused router chain already wrote the grouping into w
     const size_t smem = (32 * experts_n + 2 * (experts_n + 1)) * sizeof(int32_t);
-    group_kernel<<<1, kGroupThreads, smem, s>>>(ids, 1, static_cast<int>(P), experts_n, kTileM, w.counts, w.offsets,
-                                                 w.order, w.slot_of, w.tiles, w.ntiles, nullptr, 0, wait);
-    if (int rc = check_launch("mq_moe_forward group")) return rc;
+    int32_t *no_local = nullptr;
+    if (int rc = launch_overlapped(group_kernel, dim3(1), dim3(kGroupThreads), smem, s, "mq_moe_forward group", ids, 1,
+                                   static_cast<int>(P), experts_n, kTileM, w.counts, w.offsets, w.order, w.slot_of,
+                                   w.tiles, w.ntiles, no_local, 0, wait, 0))
+      return rc;
   }
   // The activations and the SwiGLU outputs travel in the products' dequantisation k order (perm); only
   // the pairs the grouping kept are gathered (offsets[experts] of them).
-  gather_kernel<<<grid_for(P * (d / 8), 256, dev), 256, 0, s>>>(x, x_dtype == MQ_F16, w.order, static_cast<int>(P), topk,
-                                                                static_cast<int>(d), w.xg, 1, w.offsets + experts_n);
-  if (int rc = check_launch("mq_moe_forward gather")) return rc;
+  if (int rc = launch_overlapped(gather_kernel, dim3(grid_for(P * (d / 8), 256, dev)), dim3(256), 0, s,
+                                 "mq_moe_forward gather", x, static_cast<int>(x_dtype == MQ_F16), w.order,
+                                 static_cast<int>(P), topk, static_cast<int>(d), w.xg, 1, w.offsets + experts_n,
+                                 FlagWait()))
+    return rc;
   if (int rc = moe_gemm_run(1, gu_wq, gu_ws, reinterpret_cast<const uint16_t *>(w.xg), P, d, experts_n, 2 * fe, group,
                             w.tiles, w.ntiles, w.max_tiles, kTileM, w.a, s, 1))
     return rc;
@@ -807,7 +933,8 @@ extern "C" int mq_moe_layer(const float *x, const float *router_w, const uint32_
   // The grouping is needed only by the grouped tensor-core products (more than kSmallPairs pairs).
   const bool grouped = tokens > 1 && P > mq::moe::kSmallPairs;
   if (int rc = mq::moe::route_group(router_w, x, logits, ids, weights, tokens, experts, topk, d, mq::moe::kTileM,
-                                    grouped ? w.counts : nullptr, w.offsets, w.order, w.slot_of, w.tiles, w.ntiles, s))
+                                    grouped ? w.counts : nullptr, w.offsets, w.order, w.slot_of, w.tiles, w.ntiles, s,
+                                    w.z))
     return rc;
   if (tokens == 1) {  // decode: the streaming GEMVs over the selected experts' rows (as mq_moe_forward)
     float *a = reinterpret_cast<float *>(w.a), *z = w.z;
@@ -876,21 +1003,24 @@ extern "C" int mq_ep_expert_step(const uint16_t *rows, const int32_t *ids, const
   if (int rc = mq::device_info(&dev)) return rc;
   {
     const size_t smem = (32 * experts + 2 * (experts + 1)) * sizeof(int32_t);
-    mq::moe::group_kernel<<<1, mq::moe::kGroupThreads, smem, s>>>(ids, 1, static_cast<int>(P), experts,
-                                                                  mq::moe::kTileM, w.counts, w.offsets, w.order,
-                                                                  w.slot_of, w.tiles, w.ntiles, nullptr, 0, wait,
-                                                                  kEpSmall);
-    if (int rc = mq::check_launch("mq_ep_expert_step group")) return rc;
+    int32_t *no_local = nullptr;
+    if (int rc = mq::launch_overlapped(mq::moe::group_kernel, dim3(1), dim3(mq::moe::kGroupThreads), smem, s,
+                                       "mq_ep_expert_step group", ids, 1, static_cast<int>(P), experts, mq::moe::kTileM,
+                                       w.counts, w.offsets, w.order, w.slot_of, w.tiles, w.ntiles, no_local, 0, wait,
+                                       kEpSmall))
+      return rc;
   }
   // per-pair path: its buffers after the layer's workspace
   uint8_t *small = static_cast<uint8_t *>(workspace) + need.bytes;
   __half *xs = reinterpret_cast<__half *>(small);
   int32_t *cid = reinterpret_cast<int32_t *>(small + mq::moe::align_up(kEpSmall * d * 2));
   float *a32 = reinterpret_cast<float *>(small + mq::moe::align_up(kEpSmall * d * 2) + mq::moe::align_up(kEpSmall * 4));
-  mq::moe::small_gather_kernel<<<mq::moe::grid_for(std::min<int64_t>(kEpSmall, P) * (d / 8), 256, dev), 256, 0, s>>>(
-      reinterpret_cast<const __half *>(rows), w.order, ids, valid, static_cast<int>(std::min<int64_t>(kEpSmall, P)),
-      static_cast<int>(d), xs, cid);
-  if (int rc = mq::check_launch("mq_ep_expert_step small gather")) return rc;
+  if (int rc = mq::launch_overlapped(mq::moe::small_gather_kernel,
+                                     dim3(mq::moe::grid_for(std::min<int64_t>(kEpSmall, P) * (d / 8), 256, dev)), dim3(256),
+                                     0, s, "mq_ep_expert_step small gather", reinterpret_cast<const __half *>(rows),
+                                     w.order, ids, valid, static_cast<int>(std::min<int64_t>(kEpSmall, P)),
+                                     static_cast<int>(d), xs, cid))
+    return rc;
   const int nsmall = static_cast<int>(std::min<int64_t>(kEpSmall, P));
   if (int rc = mq::gemv::gemv_q4_grouped(gu_wq, gu_ws, experts * 2 * fe, xs, a32, cid, nsmall, static_cast<int>(2 * fe),
                                          static_cast<int>(fe), d, group, 1, s, 1, 1, valid, nsmall))
@@ -902,9 +1032,10 @@ extern "C" int mq_ep_expert_step(const uint16_t *rows, const int32_t *ids, const
     return mq_ep_return(w.z, w.slot_of, ids, d, world, rank, cap, peer_ret, peer_flags, epoch, done, s);
   }
   // grouped path (no tiles when the per-pair path ran): activations in the products' k order
-  mq::moe::gather_kernel<<<mq::moe::grid_for(P * (d / 8), 256, dev), 256, 0, s>>>(
-      rows, 1, w.order, static_cast<int>(P), 1, static_cast<int>(d), w.xg, 1, valid);
-  if (int rc = mq::check_launch("mq_ep_expert_step gather")) return rc;
+  if (int rc = mq::launch_overlapped(mq::moe::gather_kernel, dim3(mq::moe::grid_for(P * (d / 8), 256, dev)), dim3(256), 0,
+                                     s, "mq_ep_expert_step gather", rows, 1, w.order, static_cast<int>(P), 1,
+                                     static_cast<int>(d), w.xg, 1, valid, mq::FlagWait()))
+    return rc;
   if (int rc = mq::moe_gemm_run(1, gu_wq, gu_ws, reinterpret_cast<const uint16_t *>(w.xg), P, d, experts, 2 * fe, group,
                                 w.tiles, w.ntiles, w.max_tiles, mq::moe::kTileM, w.a, s, 1))
     return rc;
@@ -930,7 +1061,7 @@ extern "C" int mq_ep_combine(const float *ret, const int32_t *slot_of, const flo
   wait.which = 1;
   wait.world = world;
   wait.epoch = epoch;
-  mq::moe::combine_kernel<<<mq::moe::grid_for(tokens * (d / 4), 256, dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      ret, slot_of, weights, static_cast<int>(tokens), topk, static_cast<int>(d), add != 0, y, wait);
-  return mq::check_launch("mq_ep_combine");
+  return mq::launch_overlapped(mq::moe::combine_kernel, dim3(mq::moe::grid_for(tokens * (d / 4), 256, dev)), dim3(256), 0,
+                               static_cast<cudaStream_t>(stream), "mq_ep_combine", ret, slot_of, weights,
+                               static_cast<int>(tokens), topk, static_cast<int>(d), static_cast<int>(add != 0), y, wait);
 }

@@ -212,13 +212,20 @@ def test_route_group_fused_chain(cuda, tokens, experts, d):
     np.testing.assert_array_equal(order.cpu().numpy(), rorder)
     np.testing.assert_array_equal(slot_of.cpu().numpy()[rorder], np.arange(tokens * topk))
     assert int(ntiles.item()) == int(np.sum((np.diff(ro) + 63) // 64))
-    # without the grouping: the same routing
+    # without the grouping and without a logits buffer (a few tokens then take the cluster kernel too)
     ids2 = torch.empty_like(ids)
     wts2 = torch.empty_like(wts)
     mq.route_group(t(w, cuda), t(x, cuda), ids2, wts2, topk=topk, group=False)
     torch.cuda.synchronize()
-    np.testing.assert_array_equal(ids2.cpu().numpy(), rid)
-    np.testing.assert_array_equal(wts2.cpu().numpy(), wts.cpu().numpy())
+    assert mq.device_status() == 0
+    if tokens > 4:  # the same kernel as above: the same routing, bit for bit
+        np.testing.assert_array_equal(ids2.cpu().numpy(), rid)
+        np.testing.assert_array_equal(wts2.cpu().numpy(), wts.cpu().numpy())
+    else:  # the cluster kernel sums in another order: routing of near-equal logits may differ, so check
+        # its weights against the oracle on the first logits where the chosen experts agree
+        same = (ids2.cpu().numpy() == rid).all(axis=1)
+        assert same.mean() >= 0.5
+        np.testing.assert_allclose(wts2.cpu().numpy()[same], rw[same], rtol=1e-4, atol=1e-6)
 
 
 @pytest.mark.parametrize("tokens", [404, 1, 2, 3])
