@@ -8,8 +8,8 @@
 //    so the epochs agree) and rank r writes its pairs' fp16 rows and owner-local expert ids straight into
 //    each owner's receive buffer (plain stores through CUDA IPC mappings of the peers' memory), at
 //    the fixed slots [r * cap, r * cap + cap), ids -1 past its pairs. The CTA that finishes last
-//    raises rank r's dispatch flag on every owner to the epoch (store-release at system scope, after
-//    every CTA's stores were fenced).
+//    raises rank r's dispatch flag on every owner to the epoch (one system-scope fence, then strong
+//    stores, after every CTA's stores were fenced).
 //  * mq_ep_expert_step waits until every rank's rows arrived (acquire loads in the first kernel, a
 //    bounded wait: on time-out it records a status and lets the layer go on), runs the owner's experts
 //    on the received rows (ids -1 skipped) and writes each output row straight back into its sender's
@@ -27,8 +27,9 @@ namespace mq {
 namespace ep {
 
 
-__device__ __forceinline__ void st_release_sys(int *p, int v) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// A strong (relaxed, system-scope) store; after a system-scope fence it is a release.
+__device__ __forceinline__ void st_relaxed_sys(int *p, int v) {
+  asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // The CTA that arrives last at `done` (after every CTA fenced its stores at system scope) raises
@@ -36,8 +37,10 @@ __device__ __forceinline__ void st_release_sys(int *p, int v) {
 // when `epoch` is given, stores the new epoch (every CTA read the old one before its arrival).
 // The CTA barrier orders the CTA's writes before its thread 0, whose GPU-scope fence and arrival
 // pass them on to the last CTA to arrive (the grid-barrier pattern: fences are cumulative); that
-// CTA's one system-scope fence and store-release then publish every CTA's writes to the peers. A
-// system-scope fence in every thread serialised thousands of them (15 us for a handful of rows).
+// CTA's one system-scope fence, followed by plain strong stores of the flags (a fence then a strong
+// store is a release), then publishes every CTA's writes to the peers: one fence however many peers
+// (a store-release per peer would fence once per peer). A system-scope fence in every thread
+// serialised thousands of them (15 us for a handful of rows).
 __device__ void signal_peers(int *const *peer_flags, int which, int world, int rank, int e, int *done,
                              int *epoch = nullptr) {
   __syncthreads();
@@ -47,7 +50,7 @@ __device__ void signal_peers(int *const *peer_flags, int which, int world, int r
       *done = 0;
       if (epoch) *epoch = e;
       __threadfence_system();
-      for (int d = 0; d < world; ++d) st_release_sys(peer_flags[d] + which * world + rank, e);
+      for (int d = 0; d < world; ++d) st_relaxed_sys(peer_flags[d] + which * world + rank, e);
     }
   }
 }
@@ -120,6 +123,8 @@ __global__ void return_kernel(const float *__restrict__ z, const int32_t *__rest
   signal_peers(peer_flags, 1, world, rank, e, done);
 }
 
+// CTAs for `work` 16-byte items, a few per thread: every CTA of an exchange kernel fences and counts
+// itself in before the flags go up, so fewer CTAs shorten that chain (the loops stride over the rest).
 inline int grid_for(int64_t work, const DeviceInfo &dev) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(dev.sms) * 4)));
 }
@@ -192,7 +197,9 @@ extern "C" int mq_ep_dispatch(const void *x, int x_dtype, const int32_t *order, 
   mq::DeviceInfo dev;
   if (int rc = mq::device_info(&dev)) return rc;
   const int xh = x_dtype == MQ_F16;
-  return mq::launch_overlapped(mq::ep::dispatch_kernel, dim3(mq::ep::grid_for(static_cast<int64_t>(world) * cap * (d / 8), dev)),
+  // At most tokens * topk slots hold a row: size the grid for those (the loop strides over all slots).
+  const int64_t busy = std::min<int64_t>(static_cast<int64_t>(world) * cap, std::max<int64_t>(1, tokens * topk));
+  return mq::launch_overlapped(mq::ep::dispatch_kernel, dim3(mq::ep::grid_for(busy * (d / 8) / 4, dev)),
                                dim3(256), 0, static_cast<cudaStream_t>(stream), "mq_ep_dispatch", x, xh, order, local_ids,
                                topk, static_cast<int>(d), world, rank, cap, peer_rows, peer_ids, peer_flags, epoch, done);
 }
@@ -213,7 +220,7 @@ extern "C" int mq_ep_return(const float *z, const int32_t *slot_of, const int32_
   MQ_REQUIRE(mq::aligned(z, 16), MQ_EALIGN, "mq_ep_return: z must be 16-byte aligned");
   mq::DeviceInfo dev;
   if (int rc = mq::device_info(&dev)) return rc;
-  return mq::launch_overlapped(mq::ep::return_kernel, dim3(mq::ep::grid_for(static_cast<int64_t>(world) * cap * (d / 4), dev)),
+  return mq::launch_overlapped(mq::ep::return_kernel, dim3(mq::ep::grid_for(static_cast<int64_t>(world) * cap * (d / 4) / 4, dev)),
                                dim3(256), 0, static_cast<cudaStream_t>(stream), "mq_ep_return", z, slot_of, ids,
                                static_cast<int>(d), world, rank, cap, peer_ret, peer_flags, epoch, done);
 }
