@@ -480,6 +480,19 @@ template <int G, int NT>
 int launch(const uint32_t *wq, Params p, cudaStream_t stream, const DeviceInfo &dev) {
   p.scales_tma = G == 32 && (p.k / G) % 8 == 0 && aligned(p.ws, 16);
   p.slot_bytes = ((kWordBytes + (p.scales_tma ? kRows * kScaleHalvesTma * 2 : 0) + 1023) / 1024) * 1024;
+  // Split K across warps (ks divides kWarps): the largest split whose rounds fit in one wave of the
+  // SMs. A split that spills into a second, partly filled wave measured slower (16384 x 2048: ks = 4,
+  // 128 rounds, 7.2 us; ks = 8, 256 rounds, 7.9 us), and so did splitting a matrix that already fills
+  // the SMs more finely (lm_head: ks = 1, 251 rounds, 27.1 us; ks = 4, 30.4 us). ks may exceed K's
+  // slots: the warps past them then have no items and add zeros, and a small matrix spreads over
+  // more SMs (3072 x 2048, 8 slots: 96 CTAs of one tile instead of 48 of two).
+  p.ks = 1;
+  for (int ks = 2; ks <= kWarps; ks *= 2) {
+    if ((p.tiles + kWarps / ks - 1) / (kWarps / ks) > dev.sms) break;
+    p.ks = ks;
+  }
+  p.rt = kWarps / p.ks;
+  p.nrounds = (p.tiles + p.rt - 1) / p.rt;
   Layout L{};
   for (p.slots = kMaxSlots; p.slots >= 1; --p.slots) {
     L = layout(p.k, p.batch, p.xpg ? p.batch : NT, p.slots, p.slot_bytes);
@@ -510,19 +523,6 @@ int launch(const uint32_t *wq, Params p, cudaStream_t stream, const DeviceInfo &
         return rc;
   }
   if (!p.scales_tma) smap = wmap;  // not read
-  // Split K across warps (ks divides kWarps): the largest split whose rounds fit in one wave of the
-  // SMs. A split that spills into a second, partly filled wave measured slower (16384 x 2048: ks = 4,
-  // 128 rounds, 7.2 us; ks = 8, 256 rounds, 7.9 us), and so did splitting a matrix that already fills
-  // the SMs more finely (lm_head: ks = 1, 251 rounds, 27.1 us; ks = 4, 30.4 us). ks may exceed K's
-  // slots: the warps past them then have no items and add zeros, and a small matrix spreads over
-  // more SMs (3072 x 2048, 8 slots: 96 CTAs of one tile instead of 48 of two).
-  p.ks = 1;
-  for (int ks = 2; ks <= kWarps; ks *= 2) {
-    if ((p.tiles + kWarps / ks - 1) / (kWarps / ks) > dev.sms) break;
-    p.ks = ks;
-  }
-  p.rt = kWarps / p.ks;
-  p.nrounds = (p.tiles + p.rt - 1) / p.rt;
   auto kern = gemv_q4_kernel<G, NT>;
   static size_t configured[64] = {};
   if (int rc = ensure_smem(kern, smem, configured, "mq_gemv_q4")) return rc;
