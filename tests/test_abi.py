@@ -114,3 +114,33 @@ def test_python_ops_refuse_cpu_tensors():
     y = torch.zeros(1, 16)
     with pytest.raises(mq.MQError, match="CUDA"):
         mq.gemv_q4(wq, ws, x, y, 256, group=32)
+
+
+def test_router_chain_and_layer_reject_bad_arguments_before_launch():
+    P = ctypes.c_void_p
+    ok = P(1 << 20)
+    # mq_moe_route_group(w, x, logits, ids, weights, tokens, experts, topk, d, tile, counts, offsets, order,
+    #                    slot_of, tiles, ntiles, stream)
+    rc, msg = _status("mq_moe_route_group", None, ok, None, ok, ok, 4, 128, 8, 2048, 64, None, None, None, None, None,
+                      None, None)
+    assert rc == -1 and "null" in msg
+    rc, msg = _status("mq_moe_route_group", ok, ok, None, ok, ok, 4, 300, 8, 2048, 64, None, None, None, None, None,
+                      None, None)
+    assert rc == -1 and "experts" in msg
+    rc, msg = _status("mq_moe_route_group", ok, ok, None, ok, ok, 4, 128, 8, 2050, 64, None, None, None, None, None,
+                      None, None)
+    assert rc == -1 and "multiple of 4" in msg
+    rc, msg = _status("mq_moe_route_group", ok, ok, None, ok, ok, 4, 128, 8, 2048, 64, ok, None, None, None, None,
+                      None, None)
+    assert rc == -1 and "grouping outputs" in msg
+    rc, msg = _status("mq_moe_route_group", P((1 << 20) + 4), ok, None, ok, ok, 4, 128, 8, 2048, 64, None, None, None,
+                      None, None, None, None)
+    assert rc == -2 and "aligned" in msg
+    # mq_moe_layer(x, router_w, gu_wq, gu_ws, dn_wq, dn_ws, y, ids, weights, logits, tokens, experts, topk, d, fe,
+    #              group, add, workspace, bytes, stream)
+    rc, msg = _status("mq_moe_layer", ok, ok, ok, ok, ok, ok, ok, ok, ok, None, 4, 128, 8, 2048, 700, 32, 0, ok, 1 << 30,
+                      None)
+    assert rc == -1 and "multiples of 256" in msg
+    rc, msg = _status("mq_moe_layer", ok, ok, ok, ok, ok, ok, ok, ok, ok, None, 4, 128, 8, 2048, 768, 32, 0, ok, 16,
+                      None)
+    assert rc == -1 and "workspace" in msg
