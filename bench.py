@@ -435,6 +435,19 @@ def run_mq(args):
                           "TFLOP/s_per_gpu": round(tf / world, 1),
                           "frac_of_measured_bf16_peak_per_gpu": round(tf / world / tflops_peak, 4)}
         del gt_
+        if name == synth.QWEN3_TERNARY[0][0]:  # the tile and split choice across prompt lengths
+            sweep = {}
+            for rows in (64, 128, 256, 1024, 2048):
+                sx_ = torch.from_numpy(trng.standard_normal((rows, k)).astype(np.float16)).to(dev)
+                sy_ = torch.empty(rows, hi - lo, device=dev)
+                gs_ = graph_of(lambda: [mq.p_gemm_t2(sx_, tw_d, ts_d, sy_, hi - lo, k, rows) for _ in range(10)])
+                sms_ = max_over_ranks(time_graphs([gs_], 10, stream) / 10, world)
+                stf = 2.0 * rows * n * k / (sms_ * 1e-3) / 1e12
+                sweep[str(rows)] = {"ms": round(sms_, 5), "TFLOP/s_per_gpu": round(stf / world, 1),
+                                    "frac_of_measured_bf16_peak_per_gpu": round(stf / world / tflops_peak, 4)}
+                del gs_
+            tprefill[name]["rows_sweep"] = sweep
+            tprefill[name]["rows_sweep_note"] = "weights L2-resident (the 12.6 MB shard stays in L2 across launches)"
 
     # ---- secondary: the decode layer at batch 64 through the tensor-core path
     b64 = synth.llama_layer(batch=64, seed=0)

@@ -579,18 +579,35 @@ int launch(const uint32_t *wq, const __half *x16, Params p, cudaStream_t stream,
   // tile, two CTAs per SM (two independent pipelines hide each other's latencies). More: tiles of up
   // to 256 tokens and one CTA per SM, so each weight tile is dequantised as few times as possible.
   const bool two_per_sm = p.m <= 128;
-  p.tiles_m = two_per_sm ? 1 : (p.m + 255) / 256;
-  p.bn = ((p.m + p.tiles_m - 1) / p.tiles_m + 15) / 16 * 16;
   p.tiles_n = (p.n + kBM - 1) / kBM;
   // Split K (in pairs of 128-k blocks) into as many parts as one wave of the SMs holds (two CTAs per
   // SM when they share it): the longest part sets the time (431 tokens x 3072 x 2048: 48 tiles x 3
   // parts of at most 12 blocks).
   const int nkb = p.k / kBK, pairs = nkb / 2;
-  const int tiles = p.tiles_m * p.tiles_n;
   const int slots = two_per_sm ? 2 * dev.sms : dev.sms;
-  const int splitk = std::max(1, std::min(pairs, slots / std::max(tiles, 1)));
-  p.kb_split = ((pairs + splitk - 1) / splitk) * 2;
-  p.splitk = (nkb + p.kb_split - 1) / p.kb_split;
+  auto plan_k = [&](int tiles_m, int &kb_split, int &splitk) {
+    const int tiles = tiles_m * p.tiles_n;
+    const int s = std::max(1, std::min(pairs, slots / std::max(tiles, 1)));
+    kb_split = ((pairs + s - 1) / s) * 2;
+    splitk = (nkb + kb_split - 1) / kb_split;
+  };
+  // Token tiles: the fewest of at most 256 tokens, or one more when that fills the waves of SMs
+  // better. A 128 x N x 16 MMA costs about 96 cycles for N <= 128 and 138 at N = 256 (measured), so
+  // a wave of narrower tiles can finish sooner than a part-filled extra wave of wide ones
+  // (512 x 12288 x 4096 ternary: 3 tiles of 176 tokens, 288 CTAs in two full waves, +4 % over
+  // 2 tiles of 256, 192 CTAs in a wave and a third).
+  auto cost = [&](int tiles_m) {
+    int kb_split, splitk;
+    plan_k(tiles_m, kb_split, splitk);
+    const int bn = ((p.m + tiles_m - 1) / tiles_m + 15) / 16 * 16;
+    const int64_t waves = (static_cast<int64_t>(tiles_m) * p.tiles_n * splitk + slots - 1) / slots;
+    return waves * kb_split * (96 + std::max(0, bn - 128) * 42 / 128);
+  };
+  p.tiles_m = two_per_sm ? 1 : (p.m + 255) / 256;
+  if (!two_per_sm && cost(p.tiles_m + 1) < cost(p.tiles_m)) ++p.tiles_m;
+  p.bn = ((p.m + p.tiles_m - 1) / p.tiles_m + 15) / 16 * 16;
+  const int tiles = p.tiles_m * p.tiles_n;
+  plan_k(p.tiles_m, p.kb_split, p.splitk);
   // Pipeline depth: as many stages as the SM's shared memory (or half of it) holds.
   const size_t budget = two_per_sm ? dev.smem_optin / 2 - 1024 : dev.smem_optin;
   Layout L{};
