@@ -43,6 +43,16 @@ def test_gemm_small(cuda, n, k, m, group):
     assert normwise(y, ref(wq, ws, x, group)) <= TOL
 
 
+def test_gemm_extra_token_tile(cuda):
+    """512 tokens over 12288 rows: three token tiles of 176 (288 CTAs in two full waves) instead of two
+    of 256 (192 CTAs, a wave and a third)."""
+    rng = np.random.default_rng(512)
+    x = rng.standard_normal((512, 512)).astype(np.float16)
+    wq, ws = synth.q4_matrix(rng, 12288, 512, 32)
+    y = run(cuda, wq, ws, x, 32)
+    assert normwise(y, ref(wq, ws, x, 32)) <= TOL
+
+
 @pytest.mark.parametrize("name", ["gate_up", "down", "qkv"])
 def test_gemm_prefill_config(cuda, name):
     """Llama-3.2-1B prefill shapes, 431 tokens, Q4_0 G=32, fp16 X."""

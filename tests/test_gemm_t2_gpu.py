@@ -20,7 +20,8 @@ def dense(w, s, n, k):
 
 
 @pytest.mark.parametrize("rows,n,k,xdt", [(128, 4096, 4096, np.float32), (37, 1000, 512, np.float32),
-                                          (431, 2048, 1024, np.float16), (5, 132, 256, np.float32)])
+                                          (431, 2048, 1024, np.float16), (5, 132, 256, np.float32),
+                                          (512, 12288, 512, np.float16)])  # 3 token tiles of 176 (wave fill)
 def test_gemm_t2_matches_oracle(cuda, rows, n, k, xdt):
     rng = np.random.default_rng(rows + n + k)
     w, s = synth.ternary_matrix(rng, n, k)

@@ -184,16 +184,16 @@ def test_router_logits_and_routing(cuda, tokens, experts, d):
     np.testing.assert_allclose(wts.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
 
 
-@pytest.mark.parametrize("tokens,experts,d", [(404, 128, 2048), (1, 128, 2048), (7, 60, 768), (33, 128, 4100),
-                                              (17, 256, 512), (5, 20, 64)])
-def test_route_group_fused_chain(cuda, tokens, experts, d):
+@pytest.mark.parametrize("tokens,experts,d,topk", [(404, 128, 2048, 8), (1, 128, 2048, 8), (7, 60, 768, 8),
+                                                   (33, 128, 4100, 8), (17, 256, 512, 8), (5, 20, 64, 8),
+                                                   (64, 128, 2048, 2), (3, 16, 256, 1)])
+def test_route_group_fused_chain(cuda, tokens, experts, d, topk):
     """The fused router chain (one cluster kernel: router GEMV + top-k + softmax from distributed shared
     memory, then the grouping): logits against float64, routing bit-exact against the oracle on the
     chain's own logits, grouping bit-exact against the oracle's expert lists of those ids."""
     rng = np.random.default_rng(3 * tokens + experts + d)
     w = (rng.standard_normal((experts, d)) * 0.02).astype(np.float32)
     x = rng.standard_normal((tokens, d)).astype(np.float32)
-    topk = min(8, experts)
     logits = torch.empty(tokens, experts, device=cuda)
     ids = torch.empty(tokens, topk, dtype=torch.int32, device=cuda)
     wts = torch.empty(tokens, topk, device=cuda)
@@ -228,13 +228,13 @@ def test_route_group_fused_chain(cuda, tokens, experts, d):
         np.testing.assert_allclose(wts2.cpu().numpy()[same], rw[same], rtol=1e-4, atol=1e-6)
 
 
-@pytest.mark.parametrize("tokens", [404, 1, 2, 3])
-def test_moe_layer_with_router(cuda, tokens):
+@pytest.mark.parametrize("tokens,group", [(404, 32), (1, 32), (2, 32), (3, 32), (404, 128), (1, 128)])
+def test_moe_layer_with_router(cuda, tokens, group):
     """The whole layer with its router on the device (mq_moe_layer), in a CUDA graph replayed twice:
     the routing equals the oracle's on the chain's logits, the output the fp64 layer on that routing.
     1 token runs the decode GEMVs, 2 tokens (16 pairs) the small-pair GEMVs, 3 and 404 the grouped
     tensor-core products on the chain's grouping."""
-    m = synth.moe_layer(seed=11, tokens=tokens)
+    m = synth.moe_layer(seed=11, tokens=tokens, group=group)
     rw = (np.random.default_rng(5).standard_normal((128, 2048)) * 0.02).astype(np.float32)
     tx, trw = t(m["x"], cuda), t(rw, cuda)
     gw = [t(m[k], cuda) for k in ("gu_wq", "gu_ws", "dn_wq", "dn_ws")]
@@ -243,12 +243,12 @@ def test_moe_layer_with_router(cuda, tokens):
     wts = torch.empty(tokens, 8, device=cuda)
     logits = torch.empty(tokens, 128, device=cuda)
     ws = torch.empty(mq.lib.mq_moe_workspace_size(tokens, 128, 8, 2048, 768), dtype=torch.uint8, device=cuda)
-    mq.moe_layer(tx, trw, *gw, y, 2048, 768, group=32, ids=ids, weights=wts, logits=logits, workspace=ws)
+    mq.moe_layer(tx, trw, *gw, y, 2048, 768, group=group, ids=ids, weights=wts, logits=logits, workspace=ws)
     torch.cuda.synchronize()
     y.fill_(float("nan"))
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        mq.moe_layer(tx, trw, *gw, y, 2048, 768, group=32, ids=ids, weights=wts, logits=logits, workspace=ws)
+        mq.moe_layer(tx, trw, *gw, y, 2048, 768, group=group, ids=ids, weights=wts, logits=logits, workspace=ws)
     for _ in range(2):
         g.replay()
     torch.cuda.synchronize()
@@ -256,5 +256,5 @@ def test_moe_layer_with_router(cuda, tokens):
     rid, rwts = omoe.route(logits.cpu().numpy(), 8)
     np.testing.assert_array_equal(ids.cpu().numpy(), rid)
     np.testing.assert_allclose(wts.cpu().numpy(), rwts, rtol=2e-6, atol=1e-7)
-    ref = omoe.moe_layer(m["x"], rid, rwts, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], 32, 768)
+    ref = omoe.moe_layer(m["x"], rid, rwts, m["gu_wq"], m["gu_ws"], m["dn_wq"], m["dn_ws"], group, 768)
     assert normwise(y.cpu().numpy(), ref) <= TOL
