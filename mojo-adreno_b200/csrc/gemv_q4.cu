@@ -127,13 +127,19 @@ __device__ __forceinline__ uint32_t pack_bytes(int a, int b, int c, int d) {
 }
 
 // The work of one warp, as a sequence of (tile, slot of K) items: round j of this CTA covers
-// tile (blockIdx.x + j * gridDim.x) * rt + rtl, K slots kw * spw .. + per_round - 1.
+// tile (blockIdx.x + j * gridDim.x) * rt + rtl, K slots kw * spw .. + per_round - 1. With spread
+// (whole rows per warp, several rounds) tiles are dealt to the warps across the CTAs instead:
+// round j of warp rtl covers tile (j * rt + rtl) * gridDim.x + blockIdx.x, so every CTA gets the
+// same number of tiles within one (4008 lm_head tiles: 27 or 28 per CTA, where whole rounds of 16
+// gave 103 CTAs 32 and 45 CTAs 16, leaving a third of the SMs idle in the second round).
 struct Items {
   int rtl, kw, spw, per_round, rt, tiles, grid, cta;
+  bool spread;
+  __device__ int tile_of(int j) const { return spread ? (j * rt + rtl) * grid + cta : (cta + j * grid) * rt + rtl; }
   __device__ bool get(uint32_t u, int &tile, int &sk) const {
     if (per_round <= 0) return false;
     const int j = static_cast<int>(u) / per_round, i = static_cast<int>(u) % per_round;
-    tile = (cta + j * grid) * rt + rtl;
+    tile = tile_of(j);
     sk = kw * spw + i;
     return tile < tiles;
   }
@@ -165,6 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   items.tiles = p.tiles;
   items.grid = gridDim.x;
   items.cta = blockIdx.x;
+  items.spread = p.ks == 1 && p.nrounds > static_cast<int>(gridDim.x);
 
   // Each warp streams its own tiles: lane 0 issues the TMA loads for the next S items.
   auto issue = [&](uint32_t u) {
@@ -319,8 +326,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t u = 0, u_abort = 0;
   bool aborted = false;
 
-  for (int r = blockIdx.x; r < p.nrounds; r += gridDim.x) {
-    const int tile = r * p.rt + items.rtl;
+  for (int r = blockIdx.x, j = 0; items.spread ? items.tile_of(j) - items.rtl * static_cast<int>(gridDim.x) < p.tiles
+                                                : r < p.nrounds;
+       r += gridDim.x, ++j) {
+    const int tile = items.tile_of(j);
     const int tb = p.xpg ? min(tile, p.tiles - 1) / p.tpg : 0;  // x vector of this tile's expert slot
     const int wrow0 = weight_row0(p, min(tile, p.tiles - 1));
     float acc[NT][2][2];  // [token][row tile][row g, row g + 8], this lane's group
