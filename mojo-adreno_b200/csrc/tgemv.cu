@@ -123,12 +123,18 @@ __host__ __device__ inline Layout layout(int k, int nb, int slots, int cand_roun
 // (v, i) beats (bv, bi): larger value, or the same value at a lower index.
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
+// spread (whole outputs per warp, no candidate blocks, several rounds): round j of warp rtl covers
+// tile (j * rt + rtl) * gridDim.x + blockIdx.x, so every CTA gets the same number of tiles within
+// one (the 151936-output head: 4748 tiles are 32 or 33 per CTA, where whole rounds of 16 gave one
+// CTA a third round while the others had finished two).
 struct Items {
   int rtl, kw, spw, per_round, rt, tiles, grid, cta;
+  bool spread;
+  __device__ int tile_of(int j) const { return spread ? (j * rt + rtl) * grid + cta : (cta + j * grid) * rt + rtl; }
   __device__ bool get(uint32_t u, int &tile, int &sk) const {
     if (per_round <= 0) return false;
     const int j = static_cast<int>(u) / per_round, i = static_cast<int>(u) % per_round;
-    tile = (cta + j * grid) * rt + rtl;
+    tile = tile_of(j);
     sk = kw * spw + i;
     return tile < tiles;
   }
@@ -160,6 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   items.tiles = p.tiles;
   items.grid = gridDim.x;
   items.cta = blockIdx.x;
+  items.spread = !p.cand && p.ks == 1 && p.nrounds > static_cast<int>(gridDim.x);
 
   auto issue = [&](uint32_t u) {
     int tile, sk;
@@ -297,8 +304,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool aborted = false;
 
   int jr = 0;  // this CTA's round count
-  for (int r = blockIdx.x; r < p.nrounds; r += gridDim.x, ++jr) {
-    const int tile = r * p.rt + items.rtl;
+  for (int r = blockIdx.x; items.spread ? items.tile_of(jr) - items.rtl * static_cast<int>(gridDim.x) < p.tiles
+                                         : r < p.nrounds;
+       r += gridDim.x, ++jr) {
+    const int tile = items.tile_of(jr);
     const int col = tile * kCols + 4 * cgc;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};  // token q, outputs col .. col + 3
     if (tile < p.tiles) {
