@@ -890,7 +890,6 @@ extern "C" int mq_moe_forward(const void *x, int x_dtype, const int32_t *ids, co
   MQ_REQUIRE(mq::aligned(workspace, 256), MQ_EALIGN, "mq_moe_forward: workspace must be 256-byte aligned");
   const mq::moe::Work w = mq::moe::carve(static_cast<uint8_t *>(workspace), tokens, experts, topk, d, fe);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t P = tokens * topk;
   if (tokens == 1 && x_dtype == MQ_F32) {
     // One token (decode): the streaming GEMV over the selected experts' rows, as moe_gate_up /
     // moe_down do (moek.mojo:200-223): a = silu(gate_e x) * (up_e x) in one launch, z_k = down_e a_k,
