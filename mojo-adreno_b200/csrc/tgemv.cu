@@ -202,7 +202,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   // In a launch of one round per CTA (latency-bound) the first S weight tiles of each warp go out
   // before the dependency wait: the only kernels that let this one start before they finish (this
-  // library's GEMV and GEMM kernels) write their outputs, never weights, and any other kernel finishes
+  // library's GEMV, GEMM, MoE and exchange kernels) write outputs and scratch, never weights, and any
+  // other kernel finishes
   // before this one starts, so the weights are final (12288 x 4096: 7.6 -> 7.0 us). Multi-round
   // launches (the head) keep the loads after the staging, which measured faster there.
   const bool pre = p.nrounds <= static_cast<int>(gridDim.x);
