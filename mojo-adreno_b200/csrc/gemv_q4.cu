@@ -202,14 +202,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.scales_tma) prefetch_tmap(&smap);
   }
   __syncwarp();
-  // In a launch of one round per CTA (a small matrix, latency-bound) the first S weight tiles of each
-  // warp go out before the dependency wait: the only kernels that let this one start before they
-  // finish (this library's GEMV, GEMM, MoE and exchange kernels) write outputs and scratch, never
-  // weights, and any other kernel finishes before this one starts, so the weights are final. Not with
-  // expert ids (written by
-  // earlier kernels) or a device gate (the launch may exit before consuming them), and not in
-  // multi-round launches, where it measured slower (lm_head: 27.4 -> 28.8 us; qkv 3072 x 2048:
-  // 4.4 -> 4.2 us).
+  // In a launch of one round per CTA (a small matrix, latency-bound) the first S weight tiles of each warp go out
+  // before the dependency wait: the only kernels that let this one start before they finish (this library's GEMV, GEMM,
+  // MoE and exchange kernels) write outputs and scratch, never weights, and any other kernel finishes before this one
+  // starts, so the weights are final. Not with expert ids (written by earlier kernels) or a device gate (the launch may
+  // exit before consuming them), and not in multi-round launches, where it measured slower (lm_head: 27.4 -> 28.8 us;
+  // qkv 3072 x 2048: 4.4 -> 4.2 us).
   const bool pre = !p.ids && !p.gate && p.nrounds <= static_cast<int>(gridDim.x);
   if (pre)
     for (int s = 0; s < S; ++s) issue(s);

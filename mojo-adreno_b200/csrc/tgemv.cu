@@ -200,12 +200,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.scales_tma) prefetch_tmap(&smap);
   }
   __syncwarp();
-  // In a launch of one round per CTA (latency-bound) the first S weight tiles of each warp go out
-  // before the dependency wait: the only kernels that let this one start before they finish (this
-  // library's GEMV, GEMM, MoE and exchange kernels) write outputs and scratch, never weights, and any
-  // other kernel finishes
-  // before this one starts, so the weights are final (12288 x 4096: 7.6 -> 7.0 us). Multi-round
-  // launches (the head) keep the loads after the staging, which measured faster there.
+  // In a launch of one round per CTA (latency-bound) the first S weight tiles of each warp go out before the dependency
+  // wait: the only kernels that let this one start before they finish (this library's GEMV, GEMM, MoE and exchange
+  // kernels) write outputs and scratch, never weights, and any other kernel finishes before this one starts, so the
+  // weights are final (12288 x 4096: 7.6 -> 7.0 us). Multi-round launches (the head) keep the loads after the staging,
+  // which measured faster there.
   const bool pre = p.nrounds <= static_cast<int>(gridDim.x);
   if (pre)
     for (int s = 0; s < S; ++s) issue(s);
